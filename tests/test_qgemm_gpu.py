@@ -1,0 +1,185 @@
+"""The B200 qGEMM against the oracle (the reference's qmv arithmetic, pinned bit-for-bit to the reference's
+own kernel source). Tolerance: max |y - y_ref| / max |y_ref| <= 1e-2 and mean |y - y_ref| / mean |y_ref| <= 1e-3,
+both outputs bf16."""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from ironmule_b200 import _lib, kernels
+from oracle import bf16, qmv, quant
+
+from .gpu_util import MAX_REL, MEAN_REL, bf16_bits_to_torch, case, rel_errors, to_device, torch_to_bf16_bits
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def run(dev, wq, s, b, x, **kw):
+    w_t, s_t, b_t, x_t = to_device(wq, s, b, x, dev)
+    y = kernels.qgemm(x_t, w_t, s_t, b_t, **kw)
+    torch.cuda.synchronize()
+    return torch_to_bf16_bits(y)
+
+
+@pytest.mark.parametrize("m", [1, 5])
+@pytest.mark.parametrize("variant,split", [("mma", True), ("mma", False), ("fma", False)])
+def test_config1_full_size(cuda, m, variant, split):
+    """K=3840, N=15360, W ~ N(0, 0.02), seed 0; M=1 decode and M=5 verify."""
+    wq, s, b, x = case(15360, 3840, m, seed=0)
+    want = qmv.qmv(wq, s, b, x, vpt=8)
+    got = run(cuda, wq, s, b, x, variant=variant, split_k=split)
+    mx, mean = rel_errors(got, want)
+    assert mx <= MAX_REL and mean <= MEAN_REL, (mx, mean)
+
+
+@pytest.mark.parametrize("path", sorted(GOLDEN.glob("qmv_*.npz")), ids=lambda p: p.stem)
+def test_reference_golden_vectors(cuda, path):
+    d = np.load(path)
+    got = run(cuda, d["wq"], d["scales"], d["biases"], d["x"])
+    mx, mean = rel_errors(got, d["y_bf0"])
+    assert mx <= MAX_REL and mean <= MEAN_REL, (mx, mean)
+
+
+@pytest.mark.parametrize("n,k", [(15360, 3840), (2560, 9728), (1024, 1024), (96, 320)])
+def test_row_invariance(cuda, n, k):
+    """A row's bits do not depend on how many rows share the call (verify == decode)."""
+    wq, s, b, x = case(n, k, 32, seed=5)
+    full = {m: run(cuda, wq, s, b, x[:m]) for m in (1, 5, 8, 13, 32)}
+    for m, y in full.items():
+        assert np.array_equal(y, full[32][:m]), m
+
+
+def test_split_k_is_deterministic_and_within_tolerance(cuda):
+    wq, s, b, x = case(2560, 9728, 5, seed=2)
+    want = qmv.qmv(wq, s, b, x, vpt=8)
+    a = run(cuda, wq, s, b, x, split_k=True)
+    c = run(cuda, wq, s, b, x, split_k=True)
+    assert np.array_equal(a, c)
+    for got in (a, run(cuda, wq, s, b, x, split_k=False)):
+        mx, mean = rel_errors(got, want)
+        assert mx <= MAX_REL and mean <= MEAN_REL
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 40])
+def test_forced_splits(cuda, splits):
+    wq, s, b, x = case(640, 5120, 3, seed=9)
+    want = qmv.qmv(wq, s, b, x, vpt=8)
+    _lib.call("im_qgemm_set_splits", splits)
+    try:
+        got = run(cuda, wq, s, b, x, split_k=True)
+    finally:
+        _lib.call("im_qgemm_set_splits", 0)
+    mx, mean = rel_errors(got, want)
+    assert mx <= MAX_REL and mean <= MEAN_REL
+
+
+@pytest.mark.parametrize("n,k,m", [(1, 64, 1), (33, 64, 2), (17, 128, 7), (40, 1088, 9), (64, 4096, 32), (8, 15360, 2)])
+def test_edge_shapes(cuda, n, k, m):
+    wq, s, b, x = case(n, k, m, seed=n + k + m)
+    want = qmv.qmv(wq, s, b, x, vpt=8)
+    got = run(cuda, wq, s, b, x)
+    mx, mean = rel_errors(got, want)
+    assert mx <= MAX_REL and mean <= 2 * MEAN_REL  # tiny outputs: a few values dominate the mean
+
+
+def test_fma_variant_edge_shapes(cuda):
+    for n, k, m in [(1, 64, 1), (37, 320, 8), (1000, 2048, 3)]:
+        wq, s, b, x = case(n, k, m, seed=n)
+        got = run(cuda, wq, s, b, x, variant="fma")
+        mx, _ = rel_errors(got, qmv.qmv(wq, s, b, x, vpt=8))
+        assert mx <= MAX_REL
+
+
+def test_residual_epilogue_is_the_rounded_sum(cuda):
+    wq, s, b, x = case(1536, 1024, 5, seed=4)
+    w_t, s_t, b_t, x_t = to_device(wq, s, b, x, cuda)
+    res = torch.randn(5, 1536, device=cuda).to(torch.bfloat16)
+    y0 = kernels.qgemm(x_t, w_t, s_t, b_t)
+    y1 = kernels.qgemm(x_t, w_t, s_t, b_t, epilogue="residual", residual=res)
+    inplace = res.clone()
+    kernels.qgemm(x_t, w_t, s_t, b_t, epilogue="residual", residual=inplace, out=inplace)
+    want = (res.float() + y0.float()).to(torch.bfloat16)
+    assert torch.equal(y1.view(torch.int16), want.view(torch.int16))
+    assert torch.equal(inplace.view(torch.int16), want.view(torch.int16))
+
+
+@pytest.mark.parametrize("epi", ["swiglu", "geglu"])
+def test_gated_epilogues(cuda, epi):
+    inter, k, m = 96, 512, 5
+    rng = np.random.default_rng(11)
+    wg = bf16.round_f32(rng.normal(0, 0.05, (inter, k)).astype(np.float32))
+    wu = bf16.round_f32(rng.normal(0, 0.05, (inter, k)).astype(np.float32))
+    x = bf16.from_f32(rng.normal(0, 1, (m, k)).astype(np.float32))
+    inter_w = np.concatenate([np.concatenate([wg[i:i + 16], wu[i:i + 16]]) for i in range(0, inter, 16)])
+    wq, s, b = quant.quantize(inter_w)
+    got = run(cuda, wq, s, b, x, epilogue=epi)
+    plain = bf16.to_f32(run(cuda, wq, s, b, x)).reshape(m, inter // 16, 2, 16)
+    g = plain[:, :, 0, :].reshape(m, inter)
+    u = plain[:, :, 1, :].reshape(m, inter)
+    if epi == "swiglu":
+        sig = bf16.round_f32((1.0 / (1.0 + np.exp(-g.astype(np.float64)))).astype(np.float32))
+        act = bf16.round_f32(g * sig)
+    else:
+        inner = np.float32(0.7978845608028654) * (g + np.float32(0.044715) * g * g * g)
+        act = bf16.round_f32((0.5 * g * (1.0 + np.tanh(inner.astype(np.float64)))).astype(np.float32))
+    want = bf16.from_f32(act * u)
+    diff = np.abs(bf16.to_f32(got) - bf16.to_f32(want))
+    ulp = np.abs(bf16.to_f32(want)) * 2.0 ** -7 + 1e-30
+    assert np.all(diff <= 2 * ulp)  # transcendental ulps may move one bf16 rounding
+    assert np.mean(got == want) > 0.97
+
+
+def test_gpu_quantiser_matches_the_oracle_bit_for_bit(cuda):
+    rng = np.random.default_rng(21)
+    w = bf16.round_f32(rng.normal(0, 0.02, (300, 1024)).astype(np.float32))
+    w[3, :64] = 0.125  # a constant group
+    wq, s, b = quant.quantize(w)
+    gq, gs, gb = kernels.quantize(bf16_bits_to_torch(bf16.from_f32(w), cuda))
+    assert np.array_equal(gq.cpu().numpy().view(np.uint32), wq)
+    assert np.array_equal(torch_to_bf16_bits(gs), s)
+    assert np.array_equal(torch_to_bf16_bits(gb), b)
+
+
+def test_qmv_surface_modules(cuda):
+    from ironmule_b200 import qmv_fast_shared, qmv_k3840, qmv_shared
+
+    wq, s, b, x = case(256, 3840, 2, seed=13)
+    w_t, s_t, b_t, x_t = to_device(wq, s, b, x, cuda)
+    want = qmv.qmv(wq, s, b, x, vpt=8)
+    y = qmv_k3840.run(qmv_k3840.K3840, w_t, s_t, b_t, x_t[0:1], 256, 3840)
+    assert y.shape == (1, 256)
+    a, c = qmv_shared.run_shared(w_t, s_t, b_t, [x_t[0:1], x_t[1:2]], 256)
+    assert torch.equal(a.view(torch.int16), y.view(torch.int16))  # shared == alone, bit for bit
+    mx, mean = rel_errors(torch_to_bf16_bits(torch.cat([a, c])), want)
+    assert mx <= MAX_REL and mean <= MEAN_REL
+    wq2, s2, b2, x2 = case(64, 4096, 2, seed=14)
+    w2, s2t, b2t, x2t = to_device(wq2, s2, b2, x2, cuda)
+    outs = qmv_fast_shared.run_fast(w2, s2t, b2t, [x2t[0:1], x2t[1:2]], 64, 4096)
+    mx, _ = rel_errors(torch_to_bf16_bits(torch.cat(outs)), qmv.qmv(wq2, s2, b2, x2, vpt=16))
+    assert mx <= MAX_REL
+
+
+def test_k3840_enable_and_variant_install(cuda):
+    from ironmule_b200 import qmv_k3840, qmv_variant
+    from ironmule_b200.layers import QuantizedLinear
+
+    wq, s, b, x = case(64, 3840, 1, seed=15)
+    w_t, s_t, b_t, x_t = to_device(wq, s, b, x, cuda)
+    model = torch.nn.Sequential(QuantizedLinear(w_t, s_t, b_t), torch.nn.Identity())
+    with pytest.raises(qmv_k3840.K3840Unsupported):
+        qmv_k3840.enable(model, None)
+    assert isinstance(model[0], QuantizedLinear)  # refused: untouched
+    before = model(x_t.view(1, 1, -1))
+    info = qmv_k3840.enable(model, identity="random-init")
+    assert info["admitted"] == 1 and isinstance(model[0], qmv_k3840.K3840QuantizedLinear)
+    assert torch.equal(model(x_t.view(1, 1, -1)).view(torch.int16), before.view(torch.int16))
+    assert qmv_k3840.disable(model) == 1
+    gate, report = qmv_variant.install(model, "random-init")
+    assert report["admitted"] == 1 and not gate.active
+    gate.open("test")
+    assert torch.equal(model(x_t.view(1, 1, -1)).view(torch.int16), before.view(torch.int16))
+    assert qmv_variant.uninstall(model) == 1
