@@ -1,0 +1,444 @@
+#!/usr/bin/env python
+"""Benchmark of the speculative-decoding hot path on B200 (one JSON line on rank 0).
+
+Workload (default, BASELINE config "end-to-end greedy speculative decoding, batch 1"): Qwen3-4B-shaped target
+(36 layers, hidden 2560, 32/8 heads, head_dim 128, SwiGLU 9728, vocab 151936, tied embeddings) and
+Qwen3-0.6B-shaped draft (28 layers, hidden 1024, 16/8 heads, SwiGLU 3072), both random-init and quantised to
+MLX-affine 4-bit group 64 on the device; k = 4 drafts; a 512-token prompt of uniform random ids (seed 0 +
+rank); greedy acceptance. A step is one speculative round (4 draft passes + 1 verify pass + accept); `value`
+is committed tokens per second over all ranks (replicas, one independent sequence per GPU; no collective on
+the data path), timed with CUDA events over K rounds replayed from one captured CUDA graph. Every round
+streams the full 3.6 GB of weights, far more than the 126 MB L2, so no flush is needed.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload spec_decode|verify_step]
+
+--impl reference times the CPU implementation of the same round (the oracle port in oracle/spec.py: the
+reference's greedy round with projections dequantised and dotted in float32 by OpenMP C code) on the box's host
+cores; rank 0 alone runs it under torchrun.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+K_DRAFTS = 4
+PROMPT = 512
+NEW_TOKENS = 256
+MAX_CTX = 1536
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["spec_decode", "verify_step"], default="spec_decode")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi samples (200 ms) of the SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.out = index, None, ""
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def reduce_max(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---- CPU side (oracle port): the reported baseline and the --impl reference arm ---------------------------
+def cpu_round_rate(rounds: int, warmup: int, prompt_len: int = 16, threads: int | None = None) -> dict:
+    """Committed tokens/s of the CPU port of the round on random-weight models of the benchmark's shapes."""
+    if threads:
+        os.environ["OMP_NUM_THREADS"] = str(threads)
+    from ironmule_b200.engine import PRESETS
+    from oracle.spec import CpuSpecDecoder, random_model
+
+    import numpy as np
+
+    slots = prompt_len + (rounds + warmup + 2) * (K_DRAFTS + 1) + 8
+    target = random_model(PRESETS["qwen3-4b"], seed=0, slots=slots)
+    draft = random_model(PRESETS["qwen3-0.6b"], seed=1, slots=slots)
+    dec = CpuSpecDecoder(target, draft, k=K_DRAFTS, slots=slots)
+    prompt = np.random.default_rng(0).integers(0, 151936, prompt_len).tolist()
+    dec.start(prompt)
+    for _ in range(warmup):
+        dec.round()
+    made = 0
+    t0 = time.perf_counter()
+    for _ in range(rounds):
+        made += len(dec.round())
+    sec = time.perf_counter() - t0
+    return {"value": made / sec, "seconds": sec, "rounds": rounds, "tokens": made}
+
+
+def cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, world: int, rank: int) -> None:
+    if rank != 0:
+        return
+    n = cores()
+    res = cpu_round_rate(args.steps, args.warmup, threads=n)
+    sample = (f"{args.steps} rounds after {args.warmup} warm-up rounds, 16-token prompt, Qwen3-4B/0.6B shapes with "
+              f"random 4-bit weights, k=4 greedy, OpenMP dequantise-and-dot projections on {n} threads")
+    line = {"impl": "reference", "metric": "accepted tokens/s (spec decode, Qwen3-4B + 0.6B draft, k=4, batch 1)",
+            "value": round(res["value"], 4), "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1000 * res["seconds"] / args.steps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, 4-bit weights",
+            "data": "synthetic (random weights and prompt)",
+            "config": {"workload": "config 2: greedy spec decode Qwen3-4B target + Qwen3-0.6B draft, k=4, batch 1",
+                       "cpu_path": "oracle port (the reference's CPU paths, MLX CPU and llama.cpp, are not installed)"},
+            "cpu_baseline": {"value": round(res["value"], 4), "unit": "tokens/s", "cores": n, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(res["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- GPU side --------------------------------------------------------------------------------------------
+def qgemm_roofline(target, peak_gbs: float, reps: int = 20) -> dict:
+    """The dominant kernel: every qGEMM of one verify pass (M = k+1 = 5 rows: 36 x [qkv, o, gate_up, down] and
+    the head), captured once as a graph and replayed; CUDA events on the launching stream give the mean
+    launch duration and the achieved bandwidth over the algorithmic bytes (4-bit weights at 0.5625 B per
+    weight + activations in + results out)."""
+    import torch
+
+    from ironmule_b200 import kernels
+
+    m = K_DRAFTS + 1
+    c = target.cfg
+    x = torch.randn((m, max(c.inter, c.heads * c.head_dim, c.hidden)), device=target.device).to(torch.bfloat16)
+    res = torch.zeros((m, c.hidden), dtype=torch.bfloat16, device=target.device)
+    out = torch.zeros((m, c.vocab), dtype=torch.bfloat16, device=target.device)
+    calls, total_bytes = [], 0
+
+    def add(lin, epi):
+        nonlocal total_bytes
+        n_out = lin.n // 2 if epi == "swiglu" else lin.n
+        calls.append((lin, epi))
+        total_bytes += lin.n * lin.k * 9 // 16 + m * lin.k * 2 + m * n_out * 2 + (m * lin.n * 2 if epi == "residual" else 0)
+
+    for layer in target.layers:
+        add(layer.qkv, "store")
+        add(layer.o, "residual")
+        add(layer.gate_up, "swiglu")
+        add(layer.down, "residual")
+    add(target.embed, "store")
+
+    def run():
+        for lin, epi in calls:
+            xin = x.view(-1)[: m * lin.k].view(m, lin.k)
+            kernels.qgemm(xin, lin.w, lin.s, lin.b, epilogue=epi, residual=res if epi == "residual" else None,
+                          out=res if epi == "residual" else out, ws=target.ws_gemm)
+
+    run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run()
+    g.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1000 / reps
+    launches = len(calls)
+    achieved = total_bytes / sec / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "qgemm_verify_pass_traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch_mean")
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+            "frac": round(achieved / peak_gbs, 4), "traffic": traffic,
+            "kernel": "qgemm_mma_kernel (all 145 qGEMMs of one Qwen3-4B verify pass, M=5)",
+            "launches": launches, "us_per_launch": round(sec / launches * 1e6, 2),
+            "algorithmic_bytes_per_launch": total_bytes // launches, "pass_us": round(sec * 1e6, 1)}
+
+
+def run_spec_decode(args, world: int, rank: int, local: int) -> None:
+    import torch
+
+    from ironmule_b200.engine import PRESETS, QuantModel, SpecDecoder
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pk = peaks()
+    target = QuantModel(PRESETS["qwen3-4b"], device, seed=0, max_ctx=MAX_CTX, max_rows=32, max_logit_rows=8)
+    draft = QuantModel(PRESETS["qwen3-0.6b"], device, seed=1, max_ctx=MAX_CTX, max_rows=8, max_logit_rows=8)
+    dec = SpecDecoder(target, draft, k=K_DRAFTS, batch=1)
+    gen = torch.Generator().manual_seed(rank)
+    prompt = torch.randint(0, PRESETS["qwen3-4b"].vocab, (PROMPT,), generator=gen, dtype=torch.int32)
+
+    # ---- device-timed rounds from the captured graph
+    room = MAX_CTX - PROMPT - K_DRAFTS - 8
+    dec.start([prompt.to(device)], max_new=room)
+    dec.round()
+    torch.cuda.synchronize()
+    dec.capture()
+    dec.run_rounds(args.warmup)
+    torch.cuda.synchronize()
+    before = dec.read_stats()
+    stream = torch.cuda.current_stream(device)
+    clocks = Clocks(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed_rounds")
+    e0.record(stream)
+    dec.run_rounds(args.steps)
+    e1.record(stream)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    after = dec.read_stats()
+    tokens = after.tokens - before.tokens
+    accepted = after.accepted - before.accepted
+    if after.tokens - before.tokens < args.steps:
+        print(f"warning: the sequence hit its length limit during timing ({tokens} tokens in {args.steps} rounds)",
+              file=sys.stderr)
+    max_ms = reduce_max(ms, world)
+    total_tokens = reduce_sum(float(tokens), world)
+    value = total_tokens / (max_ms / 1000)
+
+    roof = qgemm_roofline(target, pk["hbm_gbs"])
+    round_bytes = K_DRAFTS * draft.cfg.weight_bytes() + target.cfg.weight_bytes()
+
+    # ---- end to end through the public streaming API (host prompt in, every round's tokens read back)
+    e2e = None
+    if not args.no_e2e:
+        dec.generate([prompt.tolist()], 8)  # warm
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = time.perf_counter()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        out = dec.generate([prompt.tolist()], NEW_TOKENS)
+        s1.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        rounds = dec.read_stats().rounds
+        e2e_ms = reduce_max(max(s0.elapsed_time(s1), wall * 1000), world)
+        e2e_tokens = reduce_sum(float(len(out[0])), world)
+        e2e = {"value": round(e2e_tokens / (e2e_ms / 1000), 3), "unit": "tokens/s",
+               "h2d_bytes_per_step": round(PROMPT * 4 / max(rounds, 1), 2),
+               "d2h_bytes_per_step": 4 + 4 * (K_DRAFTS + 1),
+               "what": f"generate(): {PROMPT}-token host prompt -> prefill both models -> {NEW_TOKENS} new tokens, "
+                       f"each round's tokens copied to pinned host memory and handed to the caller",
+               "rounds": rounds}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        n = cores()
+        res = cpu_round_rate(rounds=3, warmup=1, threads=n)
+        cpu = {"value": round(res["value"], 4), "unit": "tokens/s", "cores": n, "kind": "port",
+               "sample": "3 speculative rounds (after 1 warm-up) on a 16-token prompt, Qwen3-4B/0.6B shapes, "
+                         "random 4-bit weights, k=4 greedy; oracle port with OpenMP dequantise-and-dot projections"}
+
+    if rank == 0:
+        line = {
+            "metric": "accepted tokens/s (spec decode, Qwen3-4B + 0.6B draft, k=4, batch 1)",
+            "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, 4-bit weights (MLX affine g64)",
+            "data": "synthetic (random-init weights, uniform random prompt)",
+            "config": {"workload": "BASELINE config 2: greedy speculative decoding, Qwen3-4B target + Qwen3-0.6B "
+                                   "draft, 4-bit affine g64, k=4, batch 1 per GPU, 512-token prompt",
+                       "global_batch": world, "prompt": PROMPT, "k": K_DRAFTS,
+                       "parallelism": f"replicas x{world}", "l2": "weights per round 3.6 GB >> 126 MB L2",
+                       "accepted_per_round": round(accepted / args.steps, 4),
+                       "round_weight_bytes": round_bytes,
+                       "round_hbm_frac": round(round_bytes / (max_ms / args.steps / 1000) / 1e9 / pk["hbm_gbs"], 4)},
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "gpu_launches": dec.launches_per_round() * args.steps,
+            "peak_source": pk["source"]}
+        print(json.dumps(line), flush=True)
+
+
+def run_verify_step(args, world: int, rank: int, local: int) -> None:
+    """one verify step's qGEMM (K=3840, N=15360, M=5, W ~ N(0, 0.02)) and greedy acceptance
+    of 4 drafts against a 151936-vocab logit row per verified row (logits = the projection's output tiled to
+    151936 entries plus fixed noise), with 8 rotating weight copies (266 MB) so the weights cannot sit in L2."""
+    import torch
+
+    from ironmule_b200 import kernels
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pk = peaks()
+    gen = torch.Generator(device=device).manual_seed(0)
+    copies = [kernels.quantize((torch.randn((15360, 3840), generator=gen, device=device) * 0.02).to(torch.bfloat16))
+              for _ in range(8)]
+    x = torch.randn((5, 3840), generator=gen, device=device).to(torch.bfloat16)
+    y = torch.empty((5, 15360), dtype=torch.bfloat16, device=device)
+    reps = -(-151936 // 15360)
+    noise = (torch.randn((5, reps * 15360), generator=gen, device=device) * 1e-3).to(torch.bfloat16)
+    logits = torch.empty((5, 151936), dtype=torch.bfloat16, device=device)
+    drafts = torch.randint(0, 151936, (1, 4), generator=gen, device=device, dtype=torch.int32)
+    ws = kernels.workspace(kernels.qgemm_workspace_bytes(5, 15360, 3840), device)
+    tokens = torch.empty((1, 5), dtype=torch.int32, device=device)
+    count = torch.empty((1,), dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def gemms(n):
+        for i in range(n):
+            wq, s, b = copies[i % 8]
+            kernels.qgemm(x, wq, s, b, out=y, ws=ws)
+
+    gemms(3)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        gemms(64)
+    g.replay()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(5):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1000 / (5 * 64)
+    algo = 15360 * 3840 * 9 // 16 + 5 * 3840 * 2 + 5 * 15360 * 2
+    achieved = algo / sec / 1e9
+    line = {"metric": "qGEMM HBM GB/s (verify step, K=3840, N=15360, M=5)", "value": round(achieved, 1),
+            "unit": "GB/s", "n_gpus": world, "steps": 5 * 64, "warmup": 3, "ms_per_step": round(sec * 1e3, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16/4-bit",
+            "data": "synthetic", "config": {"workload": "BASELINE config 1 qGEMM", "rotating_weight_copies": 8},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None}}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main() -> int:
+    args = parse()
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
+        return 0
+    world, rank, local = dist_setup(args)
+    try:
+        if args.workload == "verify_step":
+            run_verify_step(args, world, rank, local)
+        else:
+            run_spec_decode(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -84,13 +84,13 @@ int im_qgemm_set_splits(int splits);
 
 /*
  * Row statistics over a logits matrix: for each row r of logits[rows, V] (bf16, row stride ld elements)
- * writes argmax[r] (lowest index among equal maxima) and, if conf != NULL, the top-1 probability
+ * writes argmax[r * argmax_stride] (lowest index among equal maxima) and, if conf != NULL, the top-1 probability
  * conf[r] = 1 / sum_v exp(l_v - l_max). Replaces the host numpy scan of
  * ironmule/ggml_engine.py:669-683 (_decode_conf) and the per-row argmax at ggml_engine.py:848.
  * `workspace` >= im_argmax_workspace_bytes(rows, V) bytes, 256-byte aligned, zero-filled before first use.
  */
-int im_argmax_rows(const uint16_t* logits, int64_t rows, int64_t V, int64_t ld, int32_t* argmax, float* conf,
-                   void* workspace, size_t workspace_bytes, void* stream);
+int im_argmax_rows(const uint16_t* logits, int64_t rows, int64_t V, int64_t ld, int32_t* argmax,
+                   int64_t argmax_stride, float* conf, void* workspace, size_t workspace_bytes, void* stream);
 size_t im_argmax_workspace_bytes(int64_t rows, int64_t V);
 
 /*
@@ -98,12 +98,12 @@ size_t im_argmax_workspace_bytes(int64_t rows, int64_t V);
  * B*(k+1) logits rows (row b*(k+1)+i scores the token after draft i-1), then per sequence the drafts the
  * target agrees with followed by the target's own next token -- IronMule's `accept`
  * (ironmule/speculation.py:103-108) applied to the argmax of ironmule/ggml_engine.py:1316-1332.
- * drafts int32 [B, k]; out_tokens int32 [B, k+1] (entries past out_count[b] are -1);
+ * drafts int32 [B, k] with row stride drafts_ld; out_tokens int32 [B, k+1] (entries past out_count[b] are -1);
  * out_count int32 [B] (1..k+1); argmax_out int32 [B*(k+1)] may be NULL.
  * `workspace` as for im_argmax_rows with rows = B*(k+1).
  */
 int im_verify_greedy(const uint16_t* logits, int64_t B, int64_t k, int64_t V, int64_t ld, const int32_t* drafts,
-                     int32_t* out_tokens, int32_t* out_count, int32_t* argmax_out, void* workspace,
+                     int64_t drafts_ld, int32_t* out_tokens, int32_t* out_count, int32_t* argmax_out, void* workspace,
                      size_t workspace_bytes, void* stream);
 
 /*
@@ -114,6 +114,79 @@ int im_verify_greedy(const uint16_t* logits, int64_t B, int64_t k, int64_t V, in
  */
 int im_quantize_w4g64(const uint16_t* w, int64_t N, int64_t K, uint32_t* wq, uint16_t* scales, uint16_t* biases,
                       void* stream);
+
+/*
+ * RMSNorm over rows (input row stride ldx elements, output rows contiguous):
+ * out[m, :] = bf16((x[m, :] * inv_rms) * w'), inv_rms = 1/sqrt(mean(x^2) + eps), with
+ * w' = weight (gemma_style = 0, Qwen3) or 1 + weight (gemma_style = 1, Gemma-3). One fixed reduction order per
+ * row. The norms of the verify forward: ironmule/paired_research.py:177-215 (Gemma-3 pre/post norms) and
+ * mlx_lm's Qwen3 input/post-attention/final norms called from ironmule/runtime.py:505-545.
+ */
+int im_rmsnorm(const uint16_t* x, int64_t ldx, const uint16_t* weight, uint16_t* out, int64_t M, int64_t H,
+               float eps, int gemma_style, void* stream);
+
+/*
+ * The per-head step between the qkv projection and attention, fused: for each row m of the packed projection
+ * qkv[M, (Hq + 2 Hkv) D] (q heads, then k heads, then v heads): q/k RMSNorm over D (q_norm, k_norm; 1 + w when
+ * gemma_style), non-interleaved RoPE at row_pos[m] with angle = pos * inv_freq[i] (inv_freq float [D/2]),
+ * q -> q_out[M, Hq, D]; k and v -> the paged caches [pages][Hkv][16][D] at slot row_slot[m] of sequence
+ * row_seq[m] (page = page_table[seq * max_pages + slot / 16]). D is 128 or 256.
+ * Reference: the q/k norm + RoPE of ironmule/paired_research.py:177-215 and ironmule/dense_plan.py:365-370,
+ * and the KV slot writes of the stacked plan's forward, ironmule/dense_plan.py:337-363.
+ */
+int im_qk_norm_rope_kv(const uint16_t* qkv, const uint16_t* q_norm, const uint16_t* k_norm, const float* inv_freq,
+                       const int32_t* row_pos, const int32_t* row_slot, const int32_t* row_seq,
+                       const int32_t* page_table, int64_t max_pages, int64_t M, int64_t Hq, int64_t Hkv, int64_t D,
+                       float eps, int gemma_style, uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache,
+                       void* stream);
+
+/*
+ * Embedding gather from a 4-bit table: out[m, :] = bf16(scale * q + bias) of row tokens[m * tokens_stride] (int32;
+ * clamped to [0, V)), times bf16(mult) when mult != 1 (Gemma-3 scales by sqrt(hidden)). The tied table
+ * doubles as the LM head through im_qgemm_w4g64 (nn.QuantizedEmbedding / as_linear,
+ * ironmule/cuda_native.py:227-229).
+ */
+int im_embed_w4g64(const int32_t* tokens, int64_t tokens_stride, const uint32_t* wq, const uint16_t* scales,
+                   const uint16_t* biases, int64_t M, int64_t V, int64_t H, float mult, uint16_t* out, void* stream);
+
+/*
+ * Paged verification attention: out[M, Hq, D] for q[M, Hq, D] whose rows are grouped by sequence (rows of
+ * sequence b are seq_rows[b] .. seq_rows[b+1]-1, int32 [B+1]); row r sees the KV slots s <= row_slot[r] of its
+ * sequence (causal verify mask), also s > row_slot[r] - window when window > 0 (sliding window), and, when
+ * tree_mask != NULL, a slot s >= tree_base[b] only if bit (s - tree_base[b]) of tree_mask[r] is set (draft
+ * tree). GQA with Hq/Hkv query heads per KV head; scores scaled by `scale`; softmax in float32.
+ * KV keys are split at fixed absolute multiples of keys_per_split (a multiple of 64) -- keep it fixed for a
+ * model so a row's bits never depend on the launch. max_kv_len bounds every sequence's kv length (the grid
+ * size; larger slots are not read). `workspace` >= im_attention_workspace_bytes(...), 256-byte aligned,
+ * zero-filled before first use; calls sharing it must not overlap on the GPU.
+ * Replaces FA2 partial + combine of ironmule/dense_plan.py:111-195, :258-274 (causal by per-row length,
+ * :345) and the sliding-window Gemma form of ironmule/dense_gemma.py:47-300.
+ */
+int im_attention_paged(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
+                       const int32_t* page_table, int64_t max_pages, const int32_t* seq_rows, const int32_t* row_slot,
+                       const uint64_t* tree_mask, const int32_t* tree_base, int64_t B, int64_t max_rows_per_seq,
+                       int64_t Hq, int64_t Hkv, int64_t D, int64_t max_kv_len, int64_t keys_per_split, int64_t window,
+                       float scale, uint16_t* out, void* workspace, size_t workspace_bytes, void* stream);
+size_t im_attention_workspace_bytes(int64_t B, int64_t max_rows_per_seq, int64_t Hq, int64_t Hkv, int64_t D,
+                                    int64_t max_kv_len, int64_t keys_per_split);
+
+/*
+ * Device bookkeeping of one speculative round with k drafts for B sequences (no host round trip).
+ * hist int32 [B, cap] holds each sequence's committed tokens, n int32 [B] their count, target int32 [B] the
+ * length at which a sequence stops committing; slot_cap = pages * 16 bounds every KV slot.
+ * im_spec_prepare fills the round's row buffers: d0_tok/d0_pos [B*2] (draft pass 0: the last two committed
+ * tokens), d_pos [(k-1), B] (draft pass i at slot n-1+i), v_tok/v_pos [B*(k+1)] (verify rows: the last
+ * committed token then the k drafts, which the draft passes' argmax writes into v_tok[b*(k+1)+i]).
+ * im_spec_commit appends out_tokens[b, :out_count[b]] (from im_verify_greedy or im_accept_stochastic) to
+ * hist and advances n; stats int64 [B, 3] (rounds, tokens committed, drafts accepted) accumulates if non-NULL.
+ * Reference: the per-step row building, accept and KV rollback of ironmule/ggml_engine.py:1155-1343 and the
+ * draft slot bookkeeping of ironmule/draft_model.py:203-274.
+ */
+int im_spec_prepare(const int32_t* hist, int64_t cap, const int32_t* n, const int32_t* target, int64_t B, int64_t k,
+                    int64_t slot_cap, int32_t* d0_tok, int32_t* d0_pos, int32_t* d_pos, int32_t* v_tok,
+                    int32_t* v_pos, void* stream);
+int im_spec_commit(int32_t* hist, int64_t cap, int32_t* n, const int32_t* target, int64_t B, int64_t k,
+                   const int32_t* out_tokens, const int32_t* out_count, int64_t* stats, void* stream);
 
 #ifdef __cplusplus
 }

@@ -30,10 +30,19 @@ SIGNATURES: dict[str, tuple] = {
     "im_qgemm_w4g64_ex": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _INT, _INT, _P, _SZ, _P]),
     "im_qgemm_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "im_qgemm_set_splits": (_INT, [_INT]),
-    "im_argmax_rows": (_INT, [_P, _I64, _I64, _I64, _P, _P, _P, _SZ, _P]),
+    "im_argmax_rows": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _P, _P, _SZ, _P]),
     "im_argmax_workspace_bytes": (_SZ, [_I64, _I64]),
-    "im_verify_greedy": (_INT, [_P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P]),
+    "im_verify_greedy": (_INT, [_P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _SZ, _P]),
     "im_quantize_w4g64": (_INT, [_P, _I64, _I64, _P, _P, _P, _P]),
+    "im_rmsnorm": (_INT, [_P, _I64, _P, _P, _I64, _I64, ctypes.c_float, _INT, _P]),
+    "im_qk_norm_rope_kv": (_INT, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, ctypes.c_float,
+                                  _INT, _P, _P, _P, _P]),
+    "im_embed_w4g64": (_INT, [_P, _I64, _P, _P, _P, _I64, _I64, _I64, ctypes.c_float, _P, _P]),
+    "im_attention_paged": (_INT, [_P, _P, _P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
+                                  _I64, _I64, ctypes.c_float, _P, _P, _SZ, _P]),
+    "im_attention_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _I64, _I64, _I64]),
+    "im_spec_prepare": (_INT, [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P]),
+    "im_spec_commit": (_INT, [_P, _I64, _P, _P, _I64, _I64, _P, _P, _P, _P]),
 }
 
 

@@ -63,7 +63,8 @@ struct AmWork {
 
 __global__ void __launch_bounds__(AM_THREADS)
 argmax_kernel(const uint16_t* __restrict__ logits, int rows, int V, long long ld, int chunks, int chunk_len,
-              int32_t* argmax, float* conf, AmWork work, int B, int k, const int32_t* __restrict__ drafts,
+              int32_t* argmax, int out_stride, float* conf, AmWork work, int B, int k,
+              const int32_t* __restrict__ drafts, int drafts_ld,
               int32_t* out_tokens, int32_t* out_count) {
   const int chunk = blockIdx.x, row = blockIdx.y;
   const int v0 = chunk * chunk_len;
@@ -119,7 +120,7 @@ argmax_kernel(const uint16_t* __restrict__ logits, int rows, int V, long long ld
       acc = stat_merge(acc, p);
     }
     const int best = acc.idx == 0x7fffffff ? 0 : acc.idx;
-    if (argmax) argmax[r] = best;
+    if (argmax) argmax[(size_t)r * out_stride] = best;
     if (conf) conf[r] = acc.s > 0.f ? 1.0f / acc.s : 0.f;
     if (out_count) work.part[(size_t)r * chunks].idx = best;  // hand the pick to the acceptance step
   }
@@ -129,8 +130,8 @@ argmax_kernel(const uint16_t* __restrict__ logits, int rows, int V, long long ld
     for (int b = threadIdx.x; b < B; b += AM_THREADS) {
       const int base = b * (k + 1);
       int n = 0;
-      while (n < k && drafts[(size_t)b * k + n] == picks[(size_t)(base + n) * chunks].idx) n++;
-      for (int i = 0; i < n; i++) out_tokens[(size_t)b * (k + 1) + i] = drafts[(size_t)b * k + i];
+      while (n < k && drafts[(size_t)b * drafts_ld + n] == picks[(size_t)(base + n) * chunks].idx) n++;
+      for (int i = 0; i < n; i++) out_tokens[(size_t)b * (k + 1) + i] = drafts[(size_t)b * drafts_ld + i];
       out_tokens[(size_t)b * (k + 1) + n] = picks[(size_t)(base + n) * chunks].idx;
       for (int i = n + 1; i <= k; i++) out_tokens[(size_t)b * (k + 1) + i] = -1;
       out_count[b] = n + 1;
@@ -155,8 +156,9 @@ static size_t am_bytes(int64_t rows, int64_t V) {
   return 256 + (size_t)rows * chunks * sizeof(RowStat);
 }
 
-static int am_launch(const uint16_t* logits, int64_t rows, int64_t V, int64_t ld, int32_t* argmax, float* conf,
-                     int B, int k, const int32_t* drafts, int32_t* out_tokens, int32_t* out_count, void* workspace,
+static int am_launch(const uint16_t* logits, int64_t rows, int64_t V, int64_t ld, int32_t* argmax,
+                     int64_t out_stride, float* conf, int B, int k, const int32_t* drafts, int64_t drafts_ld,
+                     int32_t* out_tokens, int32_t* out_count, void* workspace,
                      size_t workspace_bytes, void* stream) {
   IM_REQUIRE(rows >= 1 && rows <= 65535 && V >= 1 && V < (1ll << 31) && ld >= V, IM_INVALID,
              "argmax: bad sizes rows=%lld V=%lld ld=%lld", (long long)rows, (long long)V, (long long)ld);
@@ -171,7 +173,8 @@ static int am_launch(const uint16_t* logits, int64_t rows, int64_t V, int64_t ld
               reinterpret_cast<RowStat*>(reinterpret_cast<char*>(workspace) + 256)};
   dim3 grid(chunks, (unsigned)rows);
   argmax_kernel<<<grid, AM_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      logits, (int)rows, (int)V, (long long)ld, chunks, len, argmax, conf, work, B, k, drafts, out_tokens, out_count);
+      logits, (int)rows, (int)V, (long long)ld, chunks, len, argmax, (int)out_stride, conf, work, B, k, drafts,
+      (int)drafts_ld, out_tokens, out_count);
   return check_launch("argmax_kernel");
 }
 
@@ -185,20 +188,21 @@ extern "C" size_t im_argmax_workspace_bytes(int64_t rows, int64_t V) {
 }
 
 extern "C" int im_argmax_rows(const uint16_t* logits, int64_t rows, int64_t V, int64_t ld, int32_t* argmax,
-                              float* conf, void* workspace, size_t workspace_bytes, void* stream) {
+                              int64_t argmax_stride, float* conf, void* workspace, size_t workspace_bytes,
+                              void* stream) {
   clear_error();
-  IM_REQUIRE(argmax, IM_INVALID, "im_argmax_rows: null argmax output");
-  return am_launch(logits, rows, V, ld, argmax, conf, 0, 0, nullptr, nullptr, nullptr, workspace, workspace_bytes,
-                   stream);
+  IM_REQUIRE(argmax && argmax_stride >= 1, IM_INVALID, "im_argmax_rows: null argmax output or bad stride");
+  return am_launch(logits, rows, V, ld, argmax, argmax_stride, conf, 0, 0, nullptr, 0, nullptr, nullptr, workspace,
+                   workspace_bytes, stream);
 }
 
 extern "C" int im_verify_greedy(const uint16_t* logits, int64_t B, int64_t k, int64_t V, int64_t ld,
-                                const int32_t* drafts, int32_t* out_tokens, int32_t* out_count, int32_t* argmax_out,
-                                void* workspace, size_t workspace_bytes, void* stream) {
+                                const int32_t* drafts, int64_t drafts_ld, int32_t* out_tokens, int32_t* out_count,
+                                int32_t* argmax_out, void* workspace, size_t workspace_bytes, void* stream) {
   clear_error();
-  IM_REQUIRE(B >= 1 && k >= 0 && k <= 64, IM_INVALID, "im_verify_greedy: bad B=%lld k=%lld", (long long)B,
-             (long long)k);
+  IM_REQUIRE(B >= 1 && k >= 0 && k <= 64 && drafts_ld >= k, IM_INVALID, "im_verify_greedy: bad B=%lld k=%lld",
+             (long long)B, (long long)k);
   IM_REQUIRE(out_tokens && out_count && (k == 0 || drafts), IM_INVALID, "im_verify_greedy: null output");
-  return am_launch(logits, B * (k + 1), V, ld, argmax_out, nullptr, (int)B, (int)k, drafts, out_tokens, out_count,
-                   workspace, workspace_bytes, stream);
+  return am_launch(logits, B * (k + 1), V, ld, argmax_out, 1, nullptr, (int)B, (int)k, drafts, drafts_ld,
+                   out_tokens, out_count, workspace, workspace_bytes, stream);
 }

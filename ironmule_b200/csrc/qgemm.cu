@@ -33,6 +33,10 @@ constexpr uint32_t BF16X2_ONE = 0x3F803F80u;
 constexpr uint32_t BF16X2_128 = 0x43004300u;  // bf16 128.0 in both halves; 128+q is exact for q < 128
 
 static int g_split_override = 0;         // sweep hook: force the CTA-level K split (0 = automatic)
+// Workspace layout, the same for every shape so that shapes may share one buffer: per-tile arrival
+// counters in a fixed region at the start (kept at zero between launches), the CTA partials after it.
+constexpr size_t QG_COUNTER_BYTES = 16384;
+constexpr int QG_MAX_SPLIT_TILES = (int)(QG_COUNTER_BYTES / 4);
 
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -280,6 +284,7 @@ qgemm_mma_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ sc
 #pragma unroll
         for (int i = 0; i < 4; i++) __stcg(mine + ((tt * NT + nt) * 4 + i) * 32 + lane, v[tt][nt][i]);
     __threadfence();
+    __syncwarp();
     unsigned prev = 0;
     if (lane == 0) prev = atomicAdd(counters + tile, 1u);
     prev = __shfl_sync(0xffffffffu, prev, 0);
@@ -415,12 +420,12 @@ static QgemmPlan plan_mma(int64_t M, int64_t N, int64_t K, bool have_workspace) 
     const int cap = G / (QG_WARPS * 2);
     s = s < 1 ? 1 : (s > cap ? (cap < 1 ? 1 : cap) : s);
     if (g_split_override > 0) s = g_split_override < G ? g_split_override : G;
+    if (p.tiles > QG_MAX_SPLIT_TILES) s = 1;
   }
   p.splits = s;
-  // counters (one per tile, padded to 256 B) + partials (always sized for NT = 4)
-  const size_t counters = ((size_t)p.tiles * 4 + 255) / 256 * 256;
+  // fixed counter region + partials (always sized for NT = 4)
   const size_t partials = s > 1 ? (size_t)p.tiles * s * QG_T * 4 * 4 * 32 * sizeof(float) : 0;
-  p.workspace = s > 1 ? counters + partials : 0;
+  p.workspace = s > 1 ? QG_COUNTER_BYTES + partials : 0;
   return p;
 }
 
@@ -429,9 +434,7 @@ static void launch_mma(const QgemmPlan& p, const uint32_t* w, const uint16_t* s,
                        const uint16_t* x, uint16_t* y, const uint16_t* res, int M, int N, int K, void* ws,
                        cudaStream_t st) {
   unsigned* counters = reinterpret_cast<unsigned*>(ws);
-  float* partial = ws ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) +
-                                                 ((size_t)p.tiles * 4 + 255) / 256 * 256)
-                      : nullptr;
+  float* partial = ws ? reinterpret_cast<float*>(reinterpret_cast<char*>(ws) + QG_COUNTER_BYTES) : nullptr;
   dim3 grid(p.tiles, p.splits);
   qgemm_mma_kernel<NT, EPI, 4><<<grid, QG_THREADS, 0, st>>>(w, s, b, x, y, res, M, N, K, p.splits, partial, counters);
 }

@@ -1,0 +1,459 @@
+"""The B200 speculative-decoding engine: 4-bit Qwen3 / Gemma-3 shaped models on libimspec kernels, a paged KV
+cache, and the draft -> verify -> accept round captured as one CUDA graph.
+
+This is the device counterpart of the reference's engines' step loops (IronMule ironmule/ggml_engine.py:1155-1343,
+ironmule/runtime.py:702-776, ironmule/dense_plan.py:488-529): the same round -- draft k tokens with the small
+model, verify them with the target in one multi-row forward, keep the agreed prefix plus the target's own
+token, roll the KV back -- with the argmax, the acceptance and the bookkeeping on the device.
+
+Layout in HBM per model: 4-bit weights (MLX affine, group 64) per layer -- qkv packed [q; k; v] rows, o,
+gate/up interleaved in 16-row blocks (gate rows then the matching up rows, so one qGEMM CTA holds both halves
+of the SwiGLU), down -- plus bf16 norm weights; the tied 4-bit embedding doubles as the LM head. KV caches are
+[layers][pages][Hkv][16][D] bf16 with a page table per sequence slot.
+
+Forward of M rows (any mix of sequences): embed -> per layer [RMSNorm, qkv qGEMM, q/k norm + RoPE + KV
+write, paged attention, o qGEMM + residual, RMSNorm, gate/up qGEMM + SwiGLU, down qGEMM + residual] ->
+final RMSNorm of the rows that need logits -> head qGEMM. Every kernel is row-invariant, so a verify row's
+logits equal those of a one-row decode bit for bit, and speculation never changes a greedy answer.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from . import kernels
+
+PAGE = 16
+MAX_QGEMM_ROWS = 32
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    name: str
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    inter: int
+    vocab: int
+    rope_theta: float = 1_000_000.0
+    eps: float = 1e-6
+    family: str = "qwen3"          # "qwen3" (SwiGLU, w-norms) or "gemma3" (GeGLU, (1+w)-norms, post-norms)
+    sliding_window: int = 0         # gemma3: local layers see the last `sliding_window` slots
+    global_every: int = 0           # gemma3: layer i is global when (i + 1) % global_every == 0
+    rope_local_theta: float = 10_000.0
+    query_scale: float = 0.0        # attention scale; 0 -> head_dim ** -0.5
+
+    @property
+    def qkv_rows(self) -> int:
+        return (self.heads + 2 * self.kv_heads) * self.head_dim
+
+    @property
+    def scale(self) -> float:
+        return self.query_scale or self.head_dim ** -0.5
+
+    def params(self) -> int:
+        per_layer = (self.hidden * self.qkv_rows + self.heads * self.head_dim * self.hidden
+                     + 3 * self.hidden * self.inter)
+        return self.layers * per_layer + self.vocab * self.hidden
+
+    def weight_bytes(self) -> int:
+        """Bytes of 4-bit weights (0.5 B per weight + 4 B of scale and bias per 64) read by one forward pass."""
+        return self.params() * 9 // 16
+
+    def kv_bytes_per_token(self) -> int:
+        return self.layers * 2 * self.kv_heads * self.head_dim * 2
+
+    def is_global(self, layer: int) -> bool:
+        return self.family != "gemma3" or self.global_every == 0 or (layer + 1) % self.global_every == 0
+
+
+PRESETS = {
+    # BASELINE configs 2/3: Qwen3-4B target and Qwen3-0.6B draft (tied embeddings, vocab 151936)
+    "qwen3-4b": ModelConfig("qwen3-4b", 2560, 36, 32, 8, 128, 9728, 151936),
+    "qwen3-0.6b": ModelConfig("qwen3-0.6b", 1024, 28, 16, 8, 128, 3072, 151936),
+    # BASELINE config 4 / 5a: Gemma-3 12B and 27B (sliding window 1024 on 5 of 6 layers)
+    "gemma3-12b": ModelConfig("gemma3-12b", 3840, 48, 16, 8, 256, 15360, 262144, family="gemma3",
+                              sliding_window=1024, global_every=6, query_scale=256 ** -0.5),
+    "gemma3-27b": ModelConfig("gemma3-27b", 5376, 62, 32, 16, 128, 21504, 262144, family="gemma3",
+                              sliding_window=1024, global_every=6, query_scale=168 ** -0.5),
+    # small shapes for tests
+    "tiny-target": ModelConfig("tiny-target", 256, 2, 4, 2, 128, 512, 1000),
+    "tiny-draft": ModelConfig("tiny-draft", 128, 2, 2, 1, 128, 256, 1000),
+}
+
+
+@dataclass
+class Linear4:
+    """One 4-bit projection on the device."""
+    w: torch.Tensor
+    s: torch.Tensor
+    b: torch.Tensor
+
+    @property
+    def n(self) -> int:
+        return int(self.w.shape[0])
+
+    @property
+    def k(self) -> int:
+        return int(self.w.shape[1]) * 8
+
+
+@dataclass
+class Layer:
+    qkv: Linear4
+    o: Linear4
+    gate_up: Linear4
+    down: Linear4
+    in_norm: torch.Tensor
+    post_norm: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """[I, K] gate and up -> [2I, K] in 16-row blocks: gate[16j:16j+16], up[16j:16j+16], ..."""
+    inter, k = gate.shape
+    if inter % 16:
+        raise ValueError("intermediate size must be a multiple of 16")
+    return torch.stack([gate.view(inter // 16, 16, k), up.view(inter // 16, 16, k)], dim=1).reshape(2 * inter, k)
+
+
+@dataclass
+class RowMeta:
+    """Device metadata for a forward of M rows: token ids (with a stride), slot / position / sequence per row,
+    sequence row offsets [B+1]; static host facts for the launch geometry."""
+    tokens: torch.Tensor
+    token_stride: int
+    pos: torch.Tensor
+    seq: torch.Tensor
+    seq_rows: torch.Tensor
+    rows: int
+    max_rows_per_seq: int
+
+
+class QuantModel:
+    """A random-init 4-bit model resident on one GPU, with its paged KV cache and preallocated activations."""
+
+    def __init__(self, cfg: ModelConfig, device: torch.device | str = "cuda", *, seed: int = 0,
+                 sigma: float = 0.02, max_seqs: int = 1, max_ctx: int = 1024, max_rows: int = 32,
+                 max_logit_rows: int = 32, keys_per_split: int = 64):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.max_seqs, self.max_rows, self.max_logit_rows = max_seqs, max_rows, max_logit_rows
+        self.pages_per_seq = -(-max_ctx // PAGE)
+        self.max_ctx = self.pages_per_seq * PAGE
+        self.keys_per_split = keys_per_split
+        gen = torch.Generator(device=self.device).manual_seed(seed)
+        self._build_weights(gen, sigma)
+        self._build_cache()
+        self._build_buffers()
+
+    # ---- weights ----------------------------------------------------------------------------------------
+    def _rand(self, gen, n, k, sigma) -> torch.Tensor:
+        return (torch.randn((n, k), generator=gen, device=self.device) * sigma).to(torch.bfloat16)
+
+    def _lin(self, w: torch.Tensor) -> Linear4:
+        return Linear4(*kernels.quantize(w.contiguous()))
+
+    def _norm(self, gen, n) -> torch.Tensor:
+        base = 0.0 if self.cfg.family == "gemma3" else 1.0
+        return (base + 0.02 * torch.randn((n,), generator=gen, device=self.device)).to(torch.bfloat16)
+
+    def _build_weights(self, gen, sigma) -> None:
+        c = self.cfg
+        self.embed = self._lin(self._rand(gen, c.vocab, c.hidden, sigma))
+        self.layers: list[Layer] = []
+        for _ in range(c.layers):
+            qkv = self._lin(self._rand(gen, c.qkv_rows, c.hidden, sigma))
+            o = self._lin(self._rand(gen, c.hidden, c.heads * c.head_dim, sigma))
+            gate, up = self._rand(gen, c.inter, c.hidden, sigma), self._rand(gen, c.inter, c.hidden, sigma)
+            gate_up = self._lin(interleave_gate_up(gate, up))
+            del gate, up
+            down = self._lin(self._rand(gen, c.hidden, c.inter, sigma))
+            self.layers.append(Layer(qkv, o, gate_up, down, self._norm(gen, c.hidden), self._norm(gen, c.hidden),
+                                     self._norm(gen, c.head_dim), self._norm(gen, c.head_dim)))
+        self.final_norm = self._norm(gen, c.hidden)
+        d = c.head_dim
+        idx = torch.arange(0, d // 2, dtype=torch.float64)
+        self.inv_freq = (c.rope_theta ** (-2.0 * idx / d)).to(torch.float32).to(self.device)
+        self.inv_freq_local = (c.rope_local_theta ** (-2.0 * idx / d)).to(torch.float32).to(self.device)
+
+    # ---- cache and buffers ------------------------------------------------------------------------------
+    def _build_cache(self) -> None:
+        c = self.cfg
+        pages = self.max_seqs * self.pages_per_seq
+        shape = (c.layers, pages, c.kv_heads, PAGE, c.head_dim)
+        self.k_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
+        self.v_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
+        # a fixed page range per sequence slot; the table is what the kernels read
+        self.page_table = torch.arange(pages, dtype=torch.int32, device=self.device).view(self.max_seqs, -1)
+
+    def _build_buffers(self) -> None:
+        c, r, dev = self.cfg, self.max_rows, self.device
+        bf = torch.bfloat16
+        self.h = torch.zeros((r, c.hidden), dtype=bf, device=dev)
+        self.xn = torch.zeros((r, c.hidden), dtype=bf, device=dev)
+        self.qkv = torch.zeros((r, c.qkv_rows), dtype=bf, device=dev)
+        self.q = torch.zeros((r, c.heads, c.head_dim), dtype=bf, device=dev)
+        self.attn = torch.zeros((r, c.heads * c.head_dim), dtype=bf, device=dev)  # [M, Hq, D] packed
+        self.act = torch.zeros((r, c.inter), dtype=bf, device=dev)
+        self.hn = torch.zeros((self.max_logit_rows, c.hidden), dtype=bf, device=dev)
+        self.logits = torch.zeros((self.max_logit_rows, c.vocab), dtype=bf, device=dev)
+        # scratch: one buffer per kernel family, sized for the largest call this model makes
+        q_need = max(kernels.qgemm_workspace_bytes(min(r, MAX_QGEMM_ROWS), n, k) for n, k in self._gemm_shapes())
+        head_need = kernels.qgemm_workspace_bytes(self.max_logit_rows, c.vocab, c.hidden)
+        self.ws_gemm = kernels.workspace(max(q_need, head_need), dev)
+        a_need = max(kernels.attention_workspace_bytes(self.max_seqs, rows, c.heads, c.kv_heads, c.head_dim,
+                                                       self.max_ctx, self.keys_per_split)
+                     for rows in (1, 8, r))
+        self.ws_attn = kernels.workspace(a_need, dev)
+        self.ws_argmax = kernels.workspace(kernels.argmax_workspace_bytes(self.max_logit_rows, c.vocab), dev)
+
+    def _gemm_shapes(self):
+        c = self.cfg
+        return [(c.qkv_rows, c.hidden), (c.hidden, c.heads * c.head_dim), (2 * c.inter, c.hidden),
+                (c.hidden, c.inter)]
+
+    # ---- forward ------------------------------------------------------------------------------------------
+    def forward(self, meta: RowMeta, max_kv_len: int, logit_rows: tuple[int, int, int] | None) -> torch.Tensor | None:
+        """Run M = meta.rows rows through the model, writing their K/V at their slots. logit_rows =
+        (first row, count, row step) selects the rows whose logits land in self.logits[:count]."""
+        c, m = self.cfg, meta.rows
+        if m > min(self.max_rows, MAX_QGEMM_ROWS):
+            raise ValueError(f"{m} rows exceed this model's per-forward limit")
+        gemma = c.family == "gemma3"
+        mult = math.sqrt(c.hidden) if gemma else 1.0
+        h, xn = self.h, self.xn
+        kernels.embed(meta.tokens, self.embed.w, self.embed.s, self.embed.b, mult=mult, out=h, rows=m,
+                      stride=meta.token_stride)
+        for li, layer in enumerate(self.layers):
+            kernels.rmsnorm(h, layer.in_norm, c.eps, gemma=gemma, out=xn, rows=m)
+            kernels.qgemm(xn, layer.qkv.w, layer.qkv.s, layer.qkv.b, out=self.qkv, rows=m, ws=self.ws_gemm)
+            glob = c.is_global(li)
+            kernels.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm,
+                                    self.inv_freq if glob else self.inv_freq_local, meta.pos, meta.pos, meta.seq,
+                                    self.page_table, c.heads, c.kv_heads, c.head_dim, c.eps, self.k_cache[li],
+                                    self.v_cache[li], gemma=gemma, q_out=self.q, rows=m)
+            kernels.attention(self.q, self.k_cache[li], self.v_cache[li], self.page_table, meta.seq_rows, meta.pos,
+                              max_rows_per_seq=meta.max_rows_per_seq, max_kv_len=max_kv_len, scale=c.scale,
+                              keys_per_split=self.keys_per_split,
+                              window=0 if glob else c.sliding_window, out=self.attn, rows=m, ws=self.ws_attn)
+            kernels.qgemm(self.attn, layer.o.w, layer.o.s, layer.o.b, epilogue="residual", residual=h, out=h,
+                          rows=m, ws=self.ws_gemm)
+            kernels.rmsnorm(h, layer.post_norm, c.eps, gemma=gemma, out=xn, rows=m)
+            kernels.qgemm(xn, layer.gate_up.w, layer.gate_up.s, layer.gate_up.b,
+                          epilogue="geglu" if gemma else "swiglu", out=self.act, rows=m, ws=self.ws_gemm)
+            kernels.qgemm(self.act, layer.down.w, layer.down.s, layer.down.b, epilogue="residual", residual=h,
+                          out=h, rows=m, ws=self.ws_gemm)
+        if logit_rows is None:
+            return None
+        first, count, step = logit_rows
+        kernels.rmsnorm(h[first:], self.final_norm, c.eps, gemma=gemma, out=self.hn, rows=count,
+                        ldx=step * c.hidden)
+        kernels.qgemm(self.hn, self.embed.w, self.embed.s, self.embed.b, out=self.logits, rows=count,
+                      ws=self.ws_gemm)
+        return self.logits[:count]
+
+    # ---- eager helpers (prefill, plain decode, tests) -----------------------------------------------------
+    def _meta(self, tokens: torch.Tensor, positions: list[int], seq: int) -> RowMeta:
+        dev = self.device
+        m = len(positions)
+        return RowMeta(tokens=tokens, token_stride=1,
+                       pos=torch.tensor(positions, dtype=torch.int32, device=dev),
+                       seq=torch.full((m,), seq, dtype=torch.int32, device=dev),
+                       seq_rows=torch.tensor([0, m], dtype=torch.int32, device=dev),
+                       rows=m, max_rows_per_seq=m)
+
+    def prefill(self, tokens: torch.Tensor, seq: int = 0, start: int = 0) -> None:
+        """Write the KV of `tokens` (int32 on the device) at slots start.. of sequence slot `seq`."""
+        total = tokens.numel()
+        step = min(self.max_rows, MAX_QGEMM_ROWS)
+        for off in range(0, total, step):
+            part = tokens[off:off + step].contiguous()
+            meta = self._meta(part, list(range(start + off, start + off + part.numel())), seq)
+            self.forward(meta, max_kv_len=self.max_ctx, logit_rows=None)
+
+    def logits_for(self, tokens: torch.Tensor, start: int, seq: int = 0) -> torch.Tensor:
+        """Feed `tokens` (one forward, rows at slots start..) and return every row's logits [M, V]."""
+        m = tokens.numel()
+        meta = self._meta(tokens.contiguous(), list(range(start, start + m)), seq)
+        return self.forward(meta, max_kv_len=self.max_ctx, logit_rows=(0, m, 1))
+
+
+@dataclass
+class SpecStats:
+    rounds: int = 0
+    tokens: int = 0
+    accepted: int = 0
+
+
+class SpecDecoder:
+    """Greedy speculative decoding of `batch` sequences with `k` drafts per round, the round on the device.
+
+    Each sequence slot b holds its committed tokens on the device. A round is: prepare the row buffers; draft
+    pass 0 (the last two committed tokens) and passes 1..k-1 (one draft each) through the draft model, each
+    followed by a device argmax that writes the next draft straight into the verify rows; one verify forward of
+    the target over k+1 rows per sequence; greedy acceptance on the device; commit. `capture()` records one
+    round as a CUDA graph; `run_rounds(n)` replays it n times with no host synchronisation.
+    """
+
+    def __init__(self, target: QuantModel, draft: QuantModel, *, k: int = 4, batch: int = 1):
+        if target.cfg.vocab != draft.cfg.vocab:
+            raise ValueError("draft and target must share a vocabulary")
+        if batch > min(target.max_seqs, draft.max_seqs):
+            raise ValueError("batch exceeds the models' sequence slots")
+        if batch * (k + 1) > min(target.max_rows, MAX_QGEMM_ROWS) or batch * (k + 1) > target.max_logit_rows:
+            raise ValueError("batch * (k + 1) verify rows exceed the target's per-forward limit")
+        if 2 * batch > draft.max_rows or batch > draft.max_logit_rows:
+            raise ValueError("draft pass rows exceed the draft model's limit")
+        self.target, self.draft, self.k, self.batch = target, draft, k, batch
+        dev = target.device
+        self.device = dev
+        b = batch
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.cap = min(target.max_ctx, draft.max_ctx)
+        self.hist = torch.zeros((b, self.cap), **i32)
+        self.n = torch.full((b,), 2, **i32)
+        self.target_len = torch.zeros((b,), **i32)
+        self.stats = torch.zeros((b, 3), dtype=torch.int64, device=dev)
+        self.d0_tok = torch.zeros((2 * b,), **i32)
+        self.d0_pos = torch.zeros((2 * b,), **i32)
+        self.d_pos = torch.zeros((max(k - 1, 1), b), **i32)
+        self.v_tok = torch.zeros((b * (k + 1),), **i32)
+        self.v_pos = torch.zeros((b * (k + 1),), **i32)
+        self.out_tokens = torch.zeros((b, k + 1), **i32)
+        self.out_count = torch.zeros((b,), **i32)
+        ar = torch.arange(b, **i32)
+        self.seq_d0 = ar.repeat_interleave(2)
+        self.rows_d0 = torch.arange(0, 2 * b + 1, 2, **i32)
+        self.seq_d = ar.clone()
+        self.rows_d = torch.arange(0, b + 1, **i32)
+        self.seq_v = ar.repeat_interleave(k + 1)
+        self.rows_v = torch.arange(0, b * (k + 1) + 1, k + 1, **i32)
+        self.ws_verify = kernels.workspace(kernels.argmax_workspace_bytes(b * (k + 1), target.cfg.vocab), dev)
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.gpu_launches_per_round = 0
+
+    # ---- one round, issued on the current stream --------------------------------------------------------
+    def round(self) -> None:
+        t, d, k, b = self.target, self.draft, self.k, self.batch
+        slot_cap = self.cap
+        kernels.spec_prepare(self.hist, self.n, self.target_len, b, k, slot_cap, self.d0_tok, self.d0_pos,
+                             self.d_pos if k > 1 else None, self.v_tok, self.v_pos)
+        # draft pass 0: two rows per sequence; logits of the second row
+        meta = RowMeta(self.d0_tok, 1, self.d0_pos, self.seq_d0, self.rows_d0, 2 * b, 2)
+        logits = d.forward(meta, max_kv_len=slot_cap, logit_rows=(1, b, 2))
+        kernels.argmax_rows(logits, out=self.v_tok[1:], out_stride=k + 1, ws=d.ws_argmax, rows=b)
+        for i in range(1, k):
+            meta = RowMeta(self.v_tok[i:], k + 1, self.d_pos[i - 1], self.seq_d, self.rows_d, b, 1)
+            logits = d.forward(meta, max_kv_len=slot_cap, logit_rows=(0, b, 1))
+            kernels.argmax_rows(logits, out=self.v_tok[i + 1:], out_stride=k + 1, ws=d.ws_argmax, rows=b)
+        meta = RowMeta(self.v_tok, 1, self.v_pos, self.seq_v, self.rows_v, b * (k + 1), k + 1)
+        logits = t.forward(meta, max_kv_len=slot_cap, logit_rows=(0, b * (k + 1), 1))
+        kernels.verify_greedy(logits, self.v_tok[1:], b=b, k=k, drafts_ld=k + 1, tokens=self.out_tokens,
+                              count=self.out_count, ws=self.ws_verify)
+        kernels.spec_commit(self.hist, self.n, self.target_len, b, k, self.out_tokens, self.out_count, self.stats)
+
+    def launches_per_round(self) -> int:
+        """libimspec kernel launches in one round (counted from the round's structure)."""
+        per_layer = 8
+        def fwd(model, logits):
+            return 1 + per_layer * model.cfg.layers + (2 if logits else 0)
+        return 1 + self.k * (fwd(self.draft, True) + 1) + fwd(self.target, True) + 1 + 1
+
+    # ---- state ------------------------------------------------------------------------------------------
+    def start(self, prompts: list[torch.Tensor], max_new: int) -> None:
+        """Load prompts (int32 device tensors, length >= 2) into the sequence slots and prefill both models
+        with all but the last prompt token."""
+        if len(prompts) != self.batch:
+            raise ValueError("one prompt per sequence slot")
+        for b, p in enumerate(prompts):
+            length = p.numel()
+            if length < 2 or length + max_new + self.k + 1 > self.cap:
+                raise ValueError("prompt too short or too long for the cache")
+            self.hist[b, :length] = p.to(torch.int32)
+            self.n[b] = length
+            self.target_len[b] = length + max_new
+            self.target.prefill(p[:-1].to(torch.int32), seq=b)
+            self.draft.prefill(p[:-1].to(torch.int32), seq=b)
+        self.stats.zero_()
+
+    def capture(self) -> None:
+        """Record one round as a CUDA graph (after one eager round has loaded every kernel)."""
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.round()
+
+    def run_rounds(self, rounds: int) -> None:
+        for _ in range(rounds):
+            if self.graph is not None:
+                self.graph.replay()
+            else:
+                self.round()
+
+    def generate(self, prompts, max_new: int, on_token=None) -> list[list[int]]:
+        """The public streaming call: host prompts (lists of token ids, one per sequence slot) in, the generated
+        tokens out. Every round's accepted tokens are read back to the host and passed to
+        `on_token(seq, tokens)` (the reference's `generate(prompt_ids, max_tokens, on_token)`,
+        ironmule_product/ggml_bridge.py:231-270). The round runs as the captured graph when `capture()` was
+        called, else eagerly."""
+        pinned = [torch.as_tensor(p, dtype=torch.int32).pin_memory() for p in prompts]
+        self.start([p.to(self.device, non_blocking=True) for p in pinned], max_new)
+        lens = [p.numel() for p in pinned]
+        done_upto = list(lens)
+        host_n = torch.zeros(self.batch, dtype=torch.int32).pin_memory()
+        host_tok = torch.zeros((self.batch, self.k + 1), dtype=torch.int32).pin_memory()
+        targets = [ln + max_new for ln in lens]
+        out: list[list[int]] = [[] for _ in range(self.batch)]
+        stream = torch.cuda.current_stream(self.device)
+        while True:
+            self.run_rounds(1)
+            host_n.copy_(self.n, non_blocking=True)
+            host_tok.copy_(self.out_tokens, non_blocking=True)
+            stream.synchronize()
+            finished = True
+            for b in range(self.batch):
+                n_b = min(int(host_n[b]), targets[b])
+                new = n_b - done_upto[b]
+                if new > 0:
+                    toks = host_tok[b, :new].tolist()
+                    out[b].extend(toks)
+                    if on_token is not None:
+                        on_token(b, toks)
+                    done_upto[b] = n_b
+                finished &= n_b >= targets[b]
+            if finished:
+                return out
+
+    def done(self) -> bool:
+        return bool(torch.all(self.n >= self.target_len).item())
+
+    def read_stats(self) -> SpecStats:
+        s = self.stats.sum(dim=0).tolist()
+        return SpecStats(rounds=int(s[0]), tokens=int(s[1]), accepted=int(s[2]))
+
+    def generated(self, b: int, prompt_len: int) -> list[int]:
+        n = int(self.n[b].item())
+        end = min(n, int(self.target_len[b].item()))
+        return self.hist[b, prompt_len:end].tolist()
+
+
+def greedy_decode(model: QuantModel, prompt: torch.Tensor, max_new: int, seq: int = 0) -> list[int]:
+    """Plain greedy decoding, one token per forward (the reference's non-speculative step); the baseline
+    that speculation must reproduce token for token."""
+    prompt = prompt.to(torch.int32)
+    model.prefill(prompt[:-1], seq=seq)
+    out: list[int] = []
+    last = prompt[-1:].clone()
+    pos = prompt.numel() - 1
+    for _ in range(max_new):
+        logits = model.logits_for(last, pos, seq=seq)
+        idx, _ = kernels.argmax_rows(logits, ws=model.ws_argmax)
+        last = idx.clone()
+        out.append(int(idx.item()))
+        pos += 1
+    return out

@@ -3,6 +3,10 @@ stream, no host synchronisation. PyTorch supplies memory and streams; the arithm
 
 Weights use MLX's affine 4-bit layout: `w` int32/uint32 [N, K/8] (8 codes per word, low nibble first),
 `scales` and `biases` bf16 [N, K/64].
+
+Kernels that reduce across CTAs borrow a zero-filled scratch buffer. Pass one explicitly (`ws=`, a uint8 CUDA
+tensor from `workspace()`) where the call is captured in a CUDA graph or may overlap another call;
+otherwise a shared per-device buffer is used.
 """
 from __future__ import annotations
 
@@ -34,43 +38,62 @@ def _check(t: torch.Tensor, name: str, dtypes: tuple, device: torch.device | Non
         raise ValueError(f"{name} must be contiguous")
 
 
-class Workspace:
-    """Zero-filled scratch buffers the kernels borrow (split-K partials, reduction counters). One buffer per
-    (device, stream, purpose); the kernels leave their counters at zero, so a buffer is reused as is. Grow
-    it before capturing a CUDA graph: allocation is not allowed during capture."""
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """A zero-filled scratch buffer of at least `nbytes` usable bytes (256-byte aligned inside)."""
+    return torch.zeros(max(int(nbytes), 1 << 16) + 256, dtype=torch.uint8, device=device)
 
-    _buffers: dict[tuple, torch.Tensor] = {}
-    _lock = threading.Lock()
+
+def _ws(buf: torch.Tensor, need: int) -> tuple[int, int]:
+    ptr = buf.data_ptr()
+    pad = (-ptr) % 256
+    size = buf.numel() - pad
+    if size < need:
+        raise ValueError(f"workspace of {need} bytes needed, {size} given")
+    return ptr + pad, size
+
+
+class _Shared:
+    """Per-(device, purpose) shared scratch for eager calls. The kernels leave counters at zero, so a buffer
+    is reused as is; it grows by reallocation (never during CUDA graph capture: pass `ws=` there)."""
+
+    buffers: dict[tuple, torch.Tensor] = {}
+    lock = threading.Lock()
 
     @classmethod
-    def get(cls, device: torch.device, nbytes: int, purpose: str) -> torch.Tensor:
-        key = (device.index, torch.cuda.current_stream(device).cuda_stream, purpose)
-        with cls._lock:
-            buf = cls._buffers.get(key)
-            if buf is None or buf.numel() < nbytes:
-                size = max(nbytes, 1 << 16)
-                buf = torch.zeros(size + 256, dtype=torch.uint8, device=device)
-                cls._buffers[key] = buf
+    def get(cls, device: torch.device, need: int, purpose: str) -> torch.Tensor:
+        key = (device.index, purpose)
+        with cls.lock:
+            buf = cls.buffers.get(key)
+            if buf is None or buf.numel() - 256 < need:
+                buf = workspace(need, device)
+                cls.buffers[key] = buf
         return buf
 
-    @staticmethod
-    def aligned_ptr(buf: torch.Tensor) -> tuple[int, int]:
-        ptr = buf.data_ptr()
-        pad = (-ptr) % 256
-        return ptr + pad, buf.numel() - pad
+
+def _scratch(ws, device, need, purpose):
+    if need == 0:
+        return None, 0
+    buf = ws if ws is not None else _Shared.get(device, need, purpose)
+    return _ws(buf, need)
+
+
+def qgemm_workspace_bytes(m: int, n: int, k: int) -> int:
+    return int(_lib.load().im_qgemm_workspace_bytes(m, n, k))
 
 
 def qgemm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *,
           epilogue: str = "store", residual: torch.Tensor | None = None, out: torch.Tensor | None = None,
-          variant: str = "auto", split_k: bool = True) -> torch.Tensor:
-    """y[M, N] = x[M, K] . dequantize(w)[N, K]^T (bf16), or a fused epilogue of it."""
+          variant: str = "auto", split_k: bool = True, ws: torch.Tensor | None = None,
+          rows: int | None = None) -> torch.Tensor:
+    """y[M, N] = x[M, K] . dequantize(w)[N, K]^T (bf16), or a fused epilogue of it. `rows` limits M to the
+    first rows of x."""
     device = x.device
     _check(x, "x", (torch.bfloat16,))
     _check(w, "w", (torch.int32, torch.uint32), device)
     _check(scales, "scales", (torch.bfloat16,), device)
     _check(biases, "biases", (torch.bfloat16,), device)
-    x2 = x.reshape(-1, x.shape[-1])
-    m, k = x2.shape
+    k = x.shape[-1]
+    m = x.numel() // k if rows is None else rows
     n = w.shape[0]
     if w.shape[1] * 8 != k or scales.shape != (n, k // 64) or biases.shape != (n, k // 64):
         raise ValueError(f"shape mismatch: x {tuple(x.shape)}, w {tuple(w.shape)}, scales {tuple(scales.shape)}")
@@ -78,58 +101,64 @@ def qgemm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.
     n_out = n // 2 if epi in (_lib.EPI_SWIGLU, _lib.EPI_GEGLU) else n
     if out is None:
         out = torch.empty((m, n_out), dtype=torch.bfloat16, device=device)
-    else:
-        _check(out, "out", (torch.bfloat16,), device)
-        if out.numel() != m * n_out:
-            raise ValueError("out has the wrong size")
+    elif out.dtype != torch.bfloat16 or out.device != device or out.numel() < m * n_out:
+        raise ValueError("out must be a bf16 tensor on x's device with room for the result")
     res_ptr = None
     if epi == _lib.EPI_RESIDUAL:
-        if residual is None:
-            raise ValueError("the residual epilogue needs `residual`")
-        _check(residual, "residual", (torch.bfloat16,), device)
-        if residual.numel() != m * n:
-            raise ValueError("residual has the wrong size")
+        if residual is None or residual.dtype != torch.bfloat16 or residual.numel() < m * n:
+            raise ValueError("the residual epilogue needs a bf16 `residual` of the output's size")
         res_ptr = residual.data_ptr()
-    ws_ptr, ws_bytes = None, 0
-    if split_k:
-        need = _lib.load().im_qgemm_workspace_bytes(m, n, k)
-        if need:
-            ws_ptr, ws_bytes = Workspace.aligned_ptr(Workspace.get(device, need + 256, "qgemm"))
-    _lib.call("im_qgemm_w4g64_ex", w.data_ptr(), scales.data_ptr(), biases.data_ptr(), x2.data_ptr(),
+    need = qgemm_workspace_bytes(m, n, k) if split_k else 0
+    ws_ptr, ws_bytes = _scratch(ws, device, need, "qgemm")
+    _lib.call("im_qgemm_w4g64_ex", w.data_ptr(), scales.data_ptr(), biases.data_ptr(), x.data_ptr(),
               out.data_ptr(), res_ptr, m, n, k, epi, _VARIANTS[variant], ws_ptr, ws_bytes, _stream(device))
-    return out.view(*x.shape[:-1], n_out)
+    if rows is None and out.numel() == m * n_out:
+        return out.view(*x.shape[:-1], n_out)
+    return out
 
 
-def argmax_rows(logits: torch.Tensor, with_conf: bool = False):
-    """(argmax int32 [rows], conf float32 [rows] or None) over the last axis of bf16 logits."""
+def argmax_workspace_bytes(rows: int, v: int) -> int:
+    return int(_lib.load().im_argmax_workspace_bytes(rows, v))
+
+
+def argmax_rows(logits: torch.Tensor, with_conf: bool = False, *, out: torch.Tensor | None = None,
+                out_stride: int = 1, conf_out: torch.Tensor | None = None, ws: torch.Tensor | None = None,
+                rows: int | None = None):
+    """(argmax int32, conf float32 or None) over the last axis of bf16 logits; `out` may be a strided int32
+    buffer (row r written at out[r * out_stride])."""
     _check(logits, "logits", (torch.bfloat16,))
     device = logits.device
-    rows, v = logits.reshape(-1, logits.shape[-1]).shape
-    idx = torch.empty(rows, dtype=torch.int32, device=device)
-    conf = torch.empty(rows, dtype=torch.float32, device=device) if with_conf else None
-    need = _lib.load().im_argmax_workspace_bytes(rows, v)
-    ws_ptr, ws_bytes = Workspace.aligned_ptr(Workspace.get(device, need + 256, "argmax"))
-    _lib.call("im_argmax_rows", logits.data_ptr(), rows, v, v, idx.data_ptr(),
+    v = logits.shape[-1]
+    rows = logits.numel() // v if rows is None else rows
+    idx = torch.empty(rows, dtype=torch.int32, device=device) if out is None else out
+    conf = conf_out if conf_out is not None else (
+        torch.empty(rows, dtype=torch.float32, device=device) if with_conf else None)
+    ws_ptr, ws_bytes = _scratch(ws, device, argmax_workspace_bytes(rows, v), "argmax")
+    _lib.call("im_argmax_rows", logits.data_ptr(), rows, v, v, idx.data_ptr(), out_stride,
               conf.data_ptr() if conf is not None else None, ws_ptr, ws_bytes, _stream(device))
     return idx, conf
 
 
-def verify_greedy(logits: torch.Tensor, drafts: torch.Tensor, *, tokens: torch.Tensor | None = None,
-                  count: torch.Tensor | None = None, picks: torch.Tensor | None = None):
-    """Greedy acceptance for B sequences with k drafts: logits bf16 [B*(k+1), V], drafts int32 [B, k].
-    Returns (tokens int32 [B, k+1] padded with -1, count int32 [B])."""
+def verify_greedy(logits: torch.Tensor, drafts: torch.Tensor, *, b: int | None = None, k: int | None = None,
+                  drafts_ld: int | None = None, tokens: torch.Tensor | None = None,
+                  count: torch.Tensor | None = None, picks: torch.Tensor | None = None,
+                  ws: torch.Tensor | None = None):
+    """Greedy acceptance for B sequences with k drafts each: logits bf16 [B*(k+1), V], drafts int32 [B, k]
+    (or a strided view: pass b, k, drafts_ld). Returns (tokens int32 [B, k+1] padded with -1, count int32 [B])."""
     _check(logits, "logits", (torch.bfloat16,))
     device = logits.device
-    _check(drafts, "drafts", (torch.int32,), device)
-    b, k = drafts.shape
+    if drafts.dtype != torch.int32 or drafts.device != device:
+        raise TypeError("drafts must be int32 on the logits' device")
+    if b is None:
+        b, k = drafts.shape
+        drafts_ld = k
     v = logits.shape[-1]
-    if logits.numel() != b * (k + 1) * v:
+    if logits.numel() < b * (k + 1) * v:
         raise ValueError("logits must hold B*(k+1) rows")
     tokens = torch.empty((b, k + 1), dtype=torch.int32, device=device) if tokens is None else tokens
     count = torch.empty(b, dtype=torch.int32, device=device) if count is None else count
-    need = _lib.load().im_argmax_workspace_bytes(b * (k + 1), v)
-    ws_ptr, ws_bytes = Workspace.aligned_ptr(Workspace.get(device, need + 256, "argmax"))
-    _lib.call("im_verify_greedy", logits.data_ptr(), b, k, v, v, drafts.data_ptr(), tokens.data_ptr(),
+    ws_ptr, ws_bytes = _scratch(ws, device, argmax_workspace_bytes(b * (k + 1), v), "argmax")
+    _lib.call("im_verify_greedy", logits.data_ptr(), b, k, v, v, drafts.data_ptr(), drafts_ld, tokens.data_ptr(),
               count.data_ptr(), picks.data_ptr() if picks is not None else None, ws_ptr, ws_bytes,
               _stream(device))
     return tokens, count
@@ -148,3 +177,84 @@ def quantize(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]
     _lib.call("im_quantize_w4g64", w.data_ptr(), n, k, wq.data_ptr(), scales.data_ptr(), biases.data_ptr(),
               _stream(w.device))
     return wq, scales, biases
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, *, gemma: bool = False,
+            out: torch.Tensor | None = None, rows: int | None = None, ldx: int | None = None) -> torch.Tensor:
+    """RMSNorm of `rows` rows of x (row stride `ldx` elements; default: all rows, contiguous)."""
+    _check(weight, "weight", (torch.bfloat16,), x.device)
+    if x.dtype != torch.bfloat16 or x.device.type != "cuda":
+        raise TypeError("x must be a bf16 CUDA tensor")
+    h = weight.numel()
+    ldx = h if ldx is None else ldx
+    rows = x.numel() // h if rows is None else rows
+    out = torch.empty((rows, h), dtype=torch.bfloat16, device=x.device) if out is None else out
+    _lib.call("im_rmsnorm", x.data_ptr(), ldx, weight.data_ptr(), out.data_ptr(), rows, h, float(eps),
+              int(gemma), _stream(x.device))
+    return out
+
+
+def qk_norm_rope_kv(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor, inv_freq: torch.Tensor,
+                    row_pos: torch.Tensor, row_slot: torch.Tensor, row_seq: torch.Tensor, page_table: torch.Tensor,
+                    hq: int, hkv: int, d: int, eps: float, k_cache: torch.Tensor, v_cache: torch.Tensor, *,
+                    gemma: bool = False, q_out: torch.Tensor | None = None, rows: int | None = None) -> torch.Tensor:
+    m = qkv.shape[0] if rows is None else rows
+    q_out = torch.empty((m, hq, d), dtype=torch.bfloat16, device=qkv.device) if q_out is None else q_out
+    _lib.call("im_qk_norm_rope_kv", qkv.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(), inv_freq.data_ptr(),
+              row_pos.data_ptr(), row_slot.data_ptr(), row_seq.data_ptr(), page_table.data_ptr(),
+              page_table.shape[-1], m, hq, hkv, d, float(eps), int(gemma), q_out.data_ptr(), k_cache.data_ptr(),
+              v_cache.data_ptr(), _stream(qkv.device))
+    return q_out
+
+
+def embed(tokens: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *,
+          mult: float = 1.0, out: torch.Tensor | None = None, rows: int | None = None,
+          stride: int = 1) -> torch.Tensor:
+    """Rows tokens[0], tokens[stride], ... of the 4-bit table, dequantised (bf16 [rows, H])."""
+    if tokens.dtype != torch.int32 or tokens.device.type != "cuda":
+        raise TypeError("tokens must be an int32 CUDA tensor")
+    v, h = wq.shape[0], wq.shape[1] * 8
+    m = tokens.numel() if rows is None else rows
+    out = torch.empty((m, h), dtype=torch.bfloat16, device=tokens.device) if out is None else out
+    _lib.call("im_embed_w4g64", tokens.data_ptr(), stride, wq.data_ptr(), scales.data_ptr(), biases.data_ptr(), m,
+              v, h, float(mult), out.data_ptr(), _stream(tokens.device))
+    return out
+
+
+def attention_workspace_bytes(b: int, rows: int, hq: int, hkv: int, d: int, max_kv_len: int, kpc: int) -> int:
+    return int(_lib.load().im_attention_workspace_bytes(b, rows, hq, hkv, d, max_kv_len, kpc))
+
+
+def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, page_table: torch.Tensor,
+              seq_rows: torch.Tensor, row_slot: torch.Tensor, *, max_rows_per_seq: int, max_kv_len: int,
+              scale: float, keys_per_split: int = 64, window: int = 0, tree_mask: torch.Tensor | None = None,
+              tree_base: torch.Tensor | None = None, out: torch.Tensor | None = None, rows: int | None = None,
+              ws: torch.Tensor | None = None) -> torch.Tensor:
+    """Paged verification attention; q [M, Hq, D] -> out [M, Hq, D] (bf16)."""
+    hq, d = q.shape[-2], q.shape[-1]
+    m = q.shape[0] if rows is None else rows
+    hkv = k_cache.shape[-3]
+    b = seq_rows.numel() - 1
+    out = torch.empty((m, hq, d), dtype=torch.bfloat16, device=q.device) if out is None else out
+    need = attention_workspace_bytes(b, max_rows_per_seq, hq, hkv, d, max_kv_len, keys_per_split)
+    if need == 0:
+        raise ValueError("attention shape not supported")
+    ws_ptr, ws_bytes = _scratch(ws, q.device, need, "attention")
+    _lib.call("im_attention_paged", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), page_table.data_ptr(),
+              page_table.shape[-1], seq_rows.data_ptr(), row_slot.data_ptr(),
+              tree_mask.data_ptr() if tree_mask is not None else None,
+              tree_base.data_ptr() if tree_base is not None else None, b, max_rows_per_seq, hq, hkv, d, max_kv_len,
+              keys_per_split, window, float(scale), out.data_ptr(), ws_ptr, ws_bytes, _stream(q.device))
+    return out
+
+
+def spec_prepare(hist, n, target, b: int, k: int, slot_cap: int, d0_tok, d0_pos, d_pos, v_tok, v_pos) -> None:
+    _lib.call("im_spec_prepare", hist.data_ptr(), hist.shape[-1], n.data_ptr(), target.data_ptr(), b, k, slot_cap,
+              d0_tok.data_ptr(), d0_pos.data_ptr(), d_pos.data_ptr() if d_pos is not None else None,
+              v_tok.data_ptr(), v_pos.data_ptr(), _stream(hist.device))
+
+
+def spec_commit(hist, n, target, b: int, k: int, out_tokens, out_count, stats=None) -> None:
+    _lib.call("im_spec_commit", hist.data_ptr(), hist.shape[-1], n.data_ptr(), target.data_ptr(), b, k,
+              out_tokens.data_ptr(), out_count.data_ptr(), stats.data_ptr() if stats is not None else None,
+              _stream(hist.device))

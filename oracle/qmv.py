@@ -29,6 +29,7 @@ def lib() -> ctypes.CDLL:
         _LIB = ctypes.CDLL(str(path))
         _LIB.oracle_qmv_w4g64.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I, ctypes.c_int, ctypes.c_int]
         _LIB.oracle_qmm_f64.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I]
+        _LIB.oracle_qmm_fast.argtypes = [_P, _P, _P, _P, _P, _I, _I, _I]
     return _LIB
 
 
@@ -95,4 +96,18 @@ def emu(name: str, wq, s, b, x, bf16_partials: bool = False) -> np.ndarray:
         yr = np.zeros((width, n), dtype=np.uint16)
         fn(_ptr(wq), _ptr(s), _ptr(b), _ptr(xr), _ptr(yr), k, n)
         y[r:r + width] = yr
+    return y
+
+
+def qmm_fast(wq, s, b, x) -> np.ndarray:
+    """bf16 bits y [M, N]: dequantise-and-dot in float32 (the timed CPU baseline's projection)."""
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    if x.ndim == 1:
+        x = x[None]
+    m, k = x.shape
+    y = np.zeros((m, wq.shape[0]), dtype=np.uint16)
+    rc = lib().oracle_qmm_fast(_ptr(np.ascontiguousarray(wq)), _ptr(np.ascontiguousarray(s)),
+                               _ptr(np.ascontiguousarray(b)), _ptr(x), _ptr(y), m, wq.shape[0], k)
+    if rc:
+        raise ValueError("qmm_fast: unsupported shape")
     return y

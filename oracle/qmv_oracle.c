@@ -160,3 +160,39 @@ int oracle_qmm_f64(const uint32_t* w, const uint16_t* scales, const uint16_t* bi
     }
     return 0;
 }
+
+/* The CPU baseline's qGEMM (test infrastructure and timed baseline only): per output row, dequantise one
+ * group of 64 weights to float32 (scale*q + bias) and dot it with every activation row, accumulating in
+ * float32 (SIMD partial sums); one bf16 cast per output. The usual CPU formulation of the reference's
+ * quantized matmul (mx.quantized_matmul on the CPU, ironmule/qmv_k3840.py:336-339). */
+#include <stdlib.h>
+int oracle_qmm_fast(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const uint16_t* x,
+                    uint16_t* y, int64_t M, int64_t N, int64_t K) {
+    if (K % 64 || M < 1 || M > 64) return -1;
+    const int64_t G = K / 64;
+    float* xf = (float*)malloc(sizeof(float) * (size_t)(M * K));
+    if (!xf) return -1;
+    for (int64_t i = 0; i < M * K; i++) xf[i] = bf16_to_f32(x[i]);
+#pragma omp parallel for schedule(static)
+    for (int64_t n = 0; n < N; n++) {
+        float acc[64];
+        float wf[64];
+        for (int64_t m = 0; m < M; m++) acc[m] = 0.0f;
+        for (int64_t g = 0; g < G; g++) {
+            const float s = bf16_to_f32(scales[n * G + g]);
+            const float b = bf16_to_f32(biases[n * G + g]);
+            const uint32_t* wp = w + n * (K / 8) + g * 8;
+            for (int i = 0; i < 64; i++) wf[i] = s * (float)((wp[i >> 3] >> (4 * (i & 7))) & 0xfu) + b;
+            for (int64_t m = 0; m < M; m++) {
+                const float* xp = xf + m * K + g * 64;
+                float part = 0.0f;
+#pragma omp simd reduction(+ : part)
+                for (int i = 0; i < 64; i++) part += wf[i] * xp[i];
+                acc[m] += part;
+            }
+        }
+        for (int64_t m = 0; m < M; m++) y[m * N + n] = f32_to_bf16(acc[m]);
+    }
+    free(xf);
+    return 0;
+}

@@ -67,11 +67,11 @@ def test_workspace_sizes():
 
 
 def test_argmax_rejects_bad_arguments():
-    rc, msg = _status("im_argmax_rows", 16, 0, 10, 10, 16, None, 256, 1 << 20, None)
+    rc, msg = _status("im_argmax_rows", 16, 0, 10, 10, 16, 1, None, 256, 1 << 20, None)
     assert rc == _lib.IM_INVALID
-    rc, msg = _status("im_argmax_rows", 16, 2, 10, 10, 16, None, 256, 8, None)
+    rc, msg = _status("im_argmax_rows", 16, 2, 10, 10, 16, 1, None, 256, 8, None)
     assert rc == _lib.IM_INVALID and "workspace" in msg
-    rc, msg = _status("im_verify_greedy", 16, 1, 4, 10, 10, None, 16, 16, None, 256, 1 << 20, None)
+    rc, msg = _status("im_verify_greedy", 16, 1, 4, 10, 10, None, 4, 16, 16, None, 256, 1 << 20, None)
     assert rc == _lib.IM_INVALID
 
 

@@ -1,0 +1,222 @@
+"""Layer kernels and the speculative engine on the B200 against the CPU oracle (oracle/model.py), and the
+engine's own invariants: a verify row equals a one-row decode bit for bit, so speculative decoding returns
+exactly the tokens of plain greedy decoding (the reference's "speculation changes no answer",
+tests/engine/test_speculation.py:79-125), and a draft model identical to the target has every draft accepted."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from ironmule_b200 import engine, kernels
+from oracle import bf16
+from oracle import model as om
+
+from .gpu_util import bf16_bits_to_torch, torch_to_bf16_bits
+
+pytestmark = pytest.mark.gpu
+
+
+def rand_bits(rng, shape, sigma=1.0):
+    return bf16.from_f32(rng.normal(0, sigma, shape).astype(np.float32))
+
+
+def test_rmsnorm_matches_oracle(cuda):
+    rng = np.random.default_rng(0)
+    for gemma in (False, True):
+        x = rand_bits(rng, (7, 2560))
+        w = rand_bits(rng, (2560,), 0.3)
+        got = torch_to_bf16_bits(kernels.rmsnorm(bf16_bits_to_torch(x, cuda), bf16_bits_to_torch(w, cuda), 1e-6,
+                                                 gemma=gemma))
+        want = om.rmsnorm(x, w, 1e-6, gemma)
+        assert np.mean(got == want) > 0.99
+        assert np.max(np.abs(bf16.to_f32(got) - bf16.to_f32(want))) <= 2 ** -6 * np.max(np.abs(bf16.to_f32(want)))
+
+
+def test_strided_rmsnorm_rows(cuda):
+    rng = np.random.default_rng(1)
+    x = rand_bits(rng, (6, 256))
+    w = rand_bits(rng, (256,))
+    xt, wt = bf16_bits_to_torch(x, cuda), bf16_bits_to_torch(w, cuda)
+    every_other = kernels.rmsnorm(xt[1:], wt, 1e-6, rows=3, ldx=512)
+    assert torch.equal(every_other, kernels.rmsnorm(xt, wt, 1e-6)[1::2])
+
+
+def test_qk_norm_rope_kv_matches_oracle(cuda):
+    rng = np.random.default_rng(2)
+    m, hq, hkv, d = 5, 8, 2, 128
+    qkv = rand_bits(rng, (m, (hq + 2 * hkv) * d))
+    qn, kn = rand_bits(rng, (d,), 0.5), rand_bits(rng, (d,), 0.5)
+    pos = np.array([3, 17, 18, 400, 900], dtype=np.int32)
+    inv_freq = (1e6 ** (-2.0 * np.arange(d // 2) / d)).astype(np.float32)
+    pages, max_pages = 64, 64
+    kc = torch.zeros((pages, hkv, 16, d), dtype=torch.bfloat16, device=cuda)
+    vc = torch.zeros_like(kc)
+    table = torch.arange(pages, dtype=torch.int32, device=cuda).flip(0).view(1, max_pages).contiguous()
+    p = torch.from_numpy(pos).to(cuda)
+    q = kernels.qk_norm_rope_kv(bf16_bits_to_torch(qkv, cuda), bf16_bits_to_torch(qn, cuda),
+                                bf16_bits_to_torch(kn, cuda), torch.from_numpy(inv_freq).to(cuda), p, p,
+                                torch.zeros(m, dtype=torch.int32, device=cuda), table, hq, hkv, d, 1e-6, kc, vc)
+    x = qkv.reshape(m, hq + 2 * hkv, d)
+    want_q = om.rope(bf16.to_f32(om.rmsnorm(x[:, :hq], qn, 1e-6)), pos, inv_freq)
+    want_k = om.rope(bf16.to_f32(om.rmsnorm(x[:, hq:hq + hkv], kn, 1e-6)), pos, inv_freq)
+    got_q = torch_to_bf16_bits(q)
+    assert np.mean(got_q == want_q) > 0.97
+    assert np.max(np.abs(bf16.to_f32(got_q) - bf16.to_f32(want_q))) < 0.05
+    tbl = table.cpu().numpy()[0]
+    for r, s in enumerate(pos):
+        page = tbl[s // 16]
+        got_k = torch_to_bf16_bits(kc[page, :, s % 16])
+        assert np.mean(got_k == want_k[r]) > 0.97
+        assert np.array_equal(torch_to_bf16_bits(vc[page, :, s % 16]), x[r, hq + hkv:])
+
+
+def _paged(kv_bits, table_row, pages, cuda):
+    """[S, Hkv, D] slot-major bits -> a [pages, Hkv, 16, D] cache laid out by the page table row."""
+    s, hkv, d = kv_bits.shape
+    cache = np.zeros((pages, hkv, 16, d), dtype=np.uint16)
+    for slot in range(s):
+        cache[table_row[slot // 16], :, slot % 16] = kv_bits[slot]
+    return bf16_bits_to_torch(cache, cuda)
+
+
+@pytest.mark.parametrize("d,hq,hkv,rows,window,kpc", [(128, 32, 8, 5, 0, 64), (128, 16, 8, 2, 0, 128),
+                                                       (256, 16, 8, 5, 100, 64), (128, 4, 1, 32, 0, 256)])
+def test_attention_matches_oracle(cuda, d, hq, hkv, rows, window, kpc):
+    rng = np.random.default_rng(d + hq + rows)
+    b = 3
+    lens = [700, 130, 17 + rows]
+    max_pages = 48
+    table = np.stack([rng.permutation(b * max_pages)[:max_pages] for _ in range(b)]).astype(np.int32)
+    kcache = np.zeros((b * max_pages, hkv, 16, d), dtype=np.uint16)
+    vcache = np.zeros_like(kcache)
+    qs, slots, seq_rows, per_seq = [], [], [0], []
+    for s in range(b):
+        k = rand_bits(rng, (lens[s], hkv, d))
+        v = rand_bits(rng, (lens[s], hkv, d))
+        for slot in range(lens[s]):
+            kcache[table[s, slot // 16], :, slot % 16] = k[slot]
+            vcache[table[s, slot // 16], :, slot % 16] = v[slot]
+        rs = np.arange(lens[s] - rows, lens[s])
+        q = rand_bits(rng, (rows, hq, d))
+        qs.append(q)
+        slots.append(rs)
+        seq_rows.append(seq_rows[-1] + rows)
+        per_seq.append((k, v, rs, q))
+    q_all = np.concatenate(qs)
+    out = kernels.attention(bf16_bits_to_torch(q_all, cuda), bf16_bits_to_torch(kcache, cuda),
+                            bf16_bits_to_torch(vcache, cuda), torch.from_numpy(table).to(cuda),
+                            torch.tensor(seq_rows, dtype=torch.int32, device=cuda),
+                            torch.from_numpy(np.concatenate(slots).astype(np.int32)).to(cuda),
+                            max_rows_per_seq=rows, max_kv_len=max_pages * 16, scale=d ** -0.5,
+                            keys_per_split=kpc, window=window)
+    got = torch_to_bf16_bits(out)
+    for s, (k, v, rs, q) in enumerate(per_seq):
+        want = om.attention(q, k, v, rs, d ** -0.5, window)
+        part = got[seq_rows[s]:seq_rows[s + 1]]
+        err = np.abs(bf16.to_f32(part) - bf16.to_f32(want))
+        assert err.max() <= 1e-2 * np.abs(bf16.to_f32(want)).max() + 1e-3
+        assert np.mean(part == want) > 0.9
+
+
+def test_attention_tree_mask(cuda):
+    rng = np.random.default_rng(9)
+    d, hq, hkv = 128, 4, 2
+    prefix, nodes = 40, 6
+    parents = [-1, 0, 0, 1, 2, 2]  # node 0 is the root of the draft tree
+    masks = []
+    for i in range(nodes):
+        m, j = 0, i
+        while j >= 0:
+            m |= 1 << j
+            j = parents[j]
+        masks.append(m)
+    total = prefix + nodes
+    k, v = rand_bits(rng, (total, hkv, d)), rand_bits(rng, (total, hkv, d))
+    table = np.arange(8, dtype=np.int32)[None]
+    slots = np.arange(prefix, total)
+    q = rand_bits(rng, (nodes, hq, d))
+    out = kernels.attention(bf16_bits_to_torch(q, cuda), _paged(k, table[0], 8, cuda), _paged(v, table[0], 8, cuda),
+                            torch.from_numpy(table).to(cuda), torch.tensor([0, nodes], dtype=torch.int32, device=cuda),
+                            torch.from_numpy(slots.astype(np.int32)).to(cuda), max_rows_per_seq=nodes,
+                            max_kv_len=128, scale=d ** -0.5,
+                            tree_mask=torch.tensor(masks, dtype=torch.int64, device=cuda),
+                            tree_base=torch.tensor([prefix], dtype=torch.int32, device=cuda))
+    want = om.attention(q, k, v, slots, d ** -0.5, tree_mask=masks, tree_base=prefix)
+    err = np.abs(bf16.to_f32(torch_to_bf16_bits(out)) - bf16.to_f32(want))
+    assert err.max() <= 1e-2 * np.abs(bf16.to_f32(want)).max() + 1e-3
+
+
+def tiny(name="tiny-target", seed=0, **kw):
+    return engine.QuantModel(engine.PRESETS[name], "cuda", seed=seed, max_ctx=256, **kw)
+
+
+def test_tiny_forward_matches_oracle(cuda):
+    model = tiny(sigma=0.08)
+    oracle = om.OracleModel.from_device(model)
+    oracle.reset(model.max_ctx)
+    rng = np.random.default_rng(3)
+    prompt = rng.integers(0, model.cfg.vocab, 24).astype(np.int32)
+    got = torch_to_bf16_bits(model.logits_for(torch.from_numpy(prompt).to(cuda), 0))
+    want = oracle.forward(prompt.tolist(), list(range(24)))
+    a, b = bf16.to_f32(got), bf16.to_f32(want)
+    assert np.max(np.abs(a - b)) <= 2e-2 * np.max(np.abs(b))
+    # greedy picks agree except where the oracle's top-2 margin is inside the tolerance
+    top2 = np.sort(b, axis=1)[:, -2:]
+    margin = top2[:, 1] - top2[:, 0]
+    agree = a.argmax(1) == b.argmax(1)
+    assert np.all(agree | (margin < 2e-2 * np.abs(b).max()))
+    assert agree.mean() > 0.8
+
+
+def test_verify_rows_equal_one_row_decodes(cuda):
+    model = tiny(sigma=0.08)
+    rng = np.random.default_rng(4)
+    toks = torch.from_numpy(rng.integers(0, 1000, 30).astype(np.int32)).to(cuda)
+    model.prefill(toks[:20])
+    many = model.logits_for(toks[20:25], 20).clone()
+    one = [model.logits_for(toks[20 + i:21 + i], 20 + i).clone() for i in range(5)]
+    for i in range(5):
+        assert torch.equal(many[i].view(torch.int16), one[i][0].view(torch.int16)), i
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_speculation_changes_no_answer(cuda, graph):
+    target = tiny("tiny-target", seed=1, sigma=0.08)
+    draft = tiny("tiny-draft", seed=2, sigma=0.08, max_rows=8, max_logit_rows=8)
+    prompt = torch.randint(0, 1000, (24,), generator=torch.Generator().manual_seed(5)).to(torch.int32).to(cuda)
+    plain = engine.greedy_decode(target, prompt, 40)
+    dec = engine.SpecDecoder(target, draft, k=4)
+    dec.start([prompt], max_new=40)
+    if graph:
+        dec.round()
+        dec.capture()
+    while not dec.done():
+        dec.run_rounds(4)
+    assert dec.generated(0, prompt.numel()) == plain
+
+
+def test_identical_draft_has_every_draft_accepted(cuda):
+    target = tiny("tiny-target", seed=1, sigma=0.08)
+    draft = tiny("tiny-target", seed=1, sigma=0.08)
+    prompt = torch.arange(2, 30, dtype=torch.int32, device=cuda)
+    dec = engine.SpecDecoder(target, draft, k=4)
+    dec.start([prompt], max_new=25)
+    dec.run_rounds(5)
+    st = dec.read_stats()
+    assert st.rounds == 5 and st.tokens == 25 and st.accepted == 20
+    assert dec.generated(0, prompt.numel()) == engine.greedy_decode(target, prompt, 25)
+
+
+def test_batched_speculation(cuda):
+    target = tiny("tiny-target", seed=1, sigma=0.08, max_seqs=3)
+    draft = tiny("tiny-draft", seed=2, sigma=0.08, max_seqs=3)
+    gen = torch.Generator().manual_seed(6)
+    prompts = [torch.randint(0, 1000, (n,), generator=gen).to(torch.int32).to(cuda) for n in (10, 31, 5)]
+    dec = engine.SpecDecoder(target, draft, k=3, batch=3)
+    dec.start(prompts, max_new=20)
+    while not dec.done():
+        dec.run_rounds(3)
+    for b, p in enumerate(prompts):
+        solo = tiny("tiny-target", seed=1, sigma=0.08)
+        assert dec.generated(b, p.numel()) == engine.greedy_decode(solo, p, 20), b
