@@ -163,7 +163,8 @@ int im_embed_w4g64(const int32_t* tokens, int64_t tokens_stride, const uint32_t*
  * :345) and the sliding-window Gemma form of ironmule/dense_gemma.py:47-300.
  */
 int im_attention_paged(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
-                       const int32_t* page_table, int64_t max_pages, const int32_t* seq_rows, const int32_t* row_slot,
+                       const int32_t* page_table, int64_t max_pages, const int32_t* seq_rows, const int32_t* seq_slot,
+                       const int32_t* row_slot,
                        const uint64_t* tree_mask, const int32_t* tree_base, int64_t B, int64_t max_rows_per_seq,
                        int64_t Hq, int64_t Hkv, int64_t D, int64_t max_kv_len, int64_t keys_per_split, int64_t window,
                        float scale, uint16_t* out, void* workspace, size_t workspace_bytes, void* stream);
@@ -187,6 +188,35 @@ int im_spec_prepare(const int32_t* hist, int64_t cap, const int32_t* n, const in
                     int32_t* v_pos, void* stream);
 int im_spec_commit(int32_t* hist, int64_t cap, int32_t* n, const int32_t* target, int64_t B, int64_t k,
                    const int32_t* out_tokens, const int32_t* out_count, int64_t* stats, void* stream);
+
+/*
+ * Stochastic speculative decoding on a Philox4x32-10 stream (no counterpart in the reference's code, which
+ * accepts greedily only, ironmule/speculation.py:103-108; this is the published speculative-sampling rule that
+ * the north-star configuration asks for). Distributions are softmax(logits / temperature) restricted to the
+ * top-p set {v : logit_v >= l*} (l* the largest logit whose set holds >= top_p of the mass; boundary ties kept)
+ * and renormalised. Philox key = (seed low, seed high), counter = (off low, off high, stream, draw) with
+ * off = offset + (*offset_dev when offset_dev != NULL: a device counter a captured CUDA graph can advance);
+ * uniform = (word0 >> 8) * 2^-24.
+ *
+ * im_accept_stochastic: target_logits [B, k+1, V] (row b*(k+1)+i scores the token after draft i-1), draft_logits
+ * [k, B, V] (pass-major: row i*B+b is the distribution draft i of sequence b was sampled from), drafts int32 [B, k]
+ * (row stride drafts_ld). Draft i is accepted iff u(stream b, draw 2i) * q(d) < p(d); at the first rejection the
+ * token is drawn from norm(max(0, p - q)) with u(b, 2i+1); after k accepts the bonus token is drawn from the
+ * target's row k with u(b, 2k). Writes out_tokens [B, k+1] (-1 padded) and out_count [B]; ratios [B, k] (p/q per
+ * tested draft) when non-NULL. workspace >= im_sampling_workspace_bytes(B*(2k+1)).
+ * im_sample_rows: one token per row of logits [rows, V] from its filtered distribution with u(streams[r] (or r),
+ * draw), written at out[r * out_stride]; workspace >= im_sampling_workspace_bytes(rows).
+ * im_philox4x32_10: the raw stream, out[4i..4i+3] = Philox4x32-10(counter (offset lo, hi, stream_id, i), seed).
+ */
+size_t im_sampling_workspace_bytes(int64_t rows);
+int im_accept_stochastic(const uint16_t* target_logits, const uint16_t* draft_logits, int64_t B, int64_t k, int64_t V,
+                         int64_t ld, const int32_t* drafts, int64_t drafts_ld, float temperature, float top_p,
+                         uint64_t seed, uint64_t offset, const uint64_t* offset_dev, int32_t* out_tokens,
+                         int32_t* out_count, float* ratios, void* workspace, size_t workspace_bytes, void* stream);
+int im_sample_rows(const uint16_t* logits, int64_t rows, int64_t V, int64_t ld, float temperature, float top_p,
+                   uint64_t seed, uint64_t offset, const uint64_t* offset_dev, const uint32_t* streams, uint32_t draw,
+                   int32_t* out, int64_t out_stride, void* workspace, size_t workspace_bytes, void* stream);
+int im_philox4x32_10(uint64_t seed, uint64_t offset, uint32_t stream_id, uint32_t n, uint32_t* out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -38,11 +38,17 @@ SIGNATURES: dict[str, tuple] = {
     "im_qk_norm_rope_kv": (_INT, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, ctypes.c_float,
                                   _INT, _P, _P, _P, _P]),
     "im_embed_w4g64": (_INT, [_P, _I64, _P, _P, _P, _I64, _I64, _I64, ctypes.c_float, _P, _P]),
-    "im_attention_paged": (_INT, [_P, _P, _P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64,
-                                  _I64, _I64, ctypes.c_float, _P, _P, _SZ, _P]),
+    "im_attention_paged": (_INT, [_P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
+                                  _I64, _I64, _I64, ctypes.c_float, _P, _P, _SZ, _P]),
     "im_attention_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _I64, _I64, _I64]),
     "im_spec_prepare": (_INT, [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P]),
     "im_spec_commit": (_INT, [_P, _I64, _P, _P, _I64, _I64, _P, _P, _P, _P]),
+    "im_sampling_workspace_bytes": (_SZ, [_I64]),
+    "im_accept_stochastic": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _P, _I64, ctypes.c_float, ctypes.c_float,
+                                    ctypes.c_uint64, ctypes.c_uint64, _P, _P, _P, _P, _P, _SZ, _P]),
+    "im_sample_rows": (_INT, [_P, _I64, _I64, _I64, ctypes.c_float, ctypes.c_float, ctypes.c_uint64,
+                              ctypes.c_uint64, _P, _P, ctypes.c_uint32, _P, _I64, _P, _SZ, _P]),
+    "im_philox4x32_10": (_INT, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, _P, _P]),
 }
 
 

@@ -35,6 +35,7 @@ struct AttnArgs {
   const uint16_t* vc;
   const int* page_table;
   const int* seq_rows;
+  const int* seq_slot;  // page-table row of each sequence group (NULL: group b uses row b)
   const int* row_slot;
   const unsigned long long* tree_mask;
   const int* tree_base;
@@ -67,6 +68,7 @@ attn_kernel(AttnArgs a) {
   const int tid = threadIdx.x;
   const int G = a.Hq / a.Hkv;
   const int r0 = a.seq_rows[b], nr = a.seq_rows[b + 1] - r0;
+  const int prow = a.seq_slot ? a.seq_slot[b] : b;
   const int q0 = qb * NQ;
   const int nq = max(0, min(NQ, nr * G - q0));
 
@@ -106,7 +108,7 @@ attn_kernel(AttnArgs a) {
       const int slot = kb0 + j;
       uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
       if (slot < k_end) {
-        const int page = a.page_table[(size_t)b * a.max_pages + (slot >> 4)];
+        const int page = a.page_table[(size_t)prow * a.max_pages + (slot >> 4)];
         const size_t off = (((size_t)page * a.Hkv + kvh) * 16 + (slot & 15)) * D + c * 8;
         kv = ldg_u4(a.kc + off);
         vv = ldg_u4(a.vc + off);
@@ -224,29 +226,39 @@ attn_kernel(AttnArgs a) {
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
-  // merge the splits in split order
-  for (int i = 0; i < nq; i++) {
-    float mx = -INFINITY;
-    for (int s = 0; s < a.nsplit; s++) {
-      if (s * a.kpc >= kv_len) break;
-      mx = fmaxf(mx, __ldcg(a.part + ((group * a.nsplit + s) * NQ + i) * (D + 2) + D));
+  // merge the splits in split order: warp w takes query vectors w, w+4, ...; lane owns D/32 dims
+  {
+    const int warp = tid >> 5, lane = tid & 31;
+    constexpr int DPL = D / 32;
+    int used = a.nsplit;
+    while (used > 1 && (used - 1) * a.kpc >= kv_len) used--;
+    for (int i = warp; i < nq; i += AT_THREADS / 32) {
+      float mx = -INFINITY;
+      for (int s0 = lane; s0 < used; s0 += 32)
+        mx = fmaxf(mx, __ldcg(a.part + ((group * a.nsplit + s0) * NQ + i) * (D + 2) + D));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float L = 0.f, O[DPL];
+#pragma unroll
+      for (int e = 0; e < DPL; e++) O[e] = 0.f;
+#pragma unroll 4
+      for (int s = 0; s < used; s++) {
+        const float* p = a.part + ((group * a.nsplit + s) * NQ + i) * (D + 2);
+        const float ms = __ldcg(p + D);
+        const float ls = __ldcg(p + D + 1);
+        float v[DPL];
+#pragma unroll
+        for (int e = 0; e < DPL; e++) v[e] = __ldcg(p + lane + 32 * e);
+        const float w = (ms == -INFINITY || mx == -INFINITY) ? 0.f : expf(ms - mx);
+        L = fmaf(ls, w, L);
+#pragma unroll
+        for (int e = 0; e < DPL; e++) O[e] = fmaf(v[e], w, O[e]);
+      }
+      const int row = r0 + (q0 + i) / G, head = kvh * G + (q0 + i) % G;
+#pragma unroll
+      for (int e = 0; e < DPL; e++)
+        a.out[((size_t)row * a.Hq + head) * D + lane + 32 * e] = to_bf(L > 0.f ? __fdiv_rn(O[e], L) : 0.f);
     }
-    float L = 0.f, O[DPT];
-#pragma unroll
-    for (int e = 0; e < DPT; e++) O[e] = 0.f;
-    for (int s = 0; s < a.nsplit; s++) {
-      if (s * a.kpc >= kv_len) break;
-      const float* p = a.part + ((group * a.nsplit + s) * NQ + i) * (D + 2);
-      const float ms = __ldcg(p + D);
-      const float w = (ms == -INFINITY || mx == -INFINITY) ? 0.f : expf(ms - mx);
-      L = fmaf(__ldcg(p + D + 1), w, L);
-#pragma unroll
-      for (int e = 0; e < DPT; e++) O[e] = fmaf(__ldcg(p + tid + e * AT_THREADS), w, O[e]);
-    }
-    const int row = r0 + (q0 + i) / G, head = kvh * G + (q0 + i) % G;
-#pragma unroll
-    for (int e = 0; e < DPT; e++)
-      a.out[((size_t)row * a.Hq + head) * D + tid + e * AT_THREADS] = to_bf(L > 0.f ? __fdiv_rn(O[e], L) : 0.f);
   }
   if (tid == 0) a.counters[group] = 0u;
 }
@@ -292,7 +304,7 @@ extern "C" size_t im_attention_workspace_bytes(int64_t B, int64_t max_rows_per_s
 
 extern "C" int im_attention_paged(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                                   const int32_t* page_table, int64_t max_pages, const int32_t* seq_rows,
-                                  const int32_t* row_slot, const uint64_t* tree_mask, const int32_t* tree_base,
+                                  const int32_t* seq_slot, const int32_t* row_slot, const uint64_t* tree_mask, const int32_t* tree_base,
                                   int64_t B, int64_t max_rows_per_seq, int64_t Hq, int64_t Hkv, int64_t D,
                                   int64_t max_kv_len, int64_t keys_per_split, int64_t window, float scale,
                                   uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
@@ -321,6 +333,7 @@ extern "C" int im_attention_paged(const uint16_t* q, const uint16_t* k_cache, co
   args.vc = v_cache;
   args.page_table = page_table;
   args.seq_rows = seq_rows;
+  args.seq_slot = seq_slot;
   args.row_slot = row_slot;
   args.tree_mask = reinterpret_cast<const unsigned long long*>(tree_mask);
   args.tree_base = tree_base;

@@ -133,6 +133,7 @@ class RowMeta:
     seq_rows: torch.Tensor
     rows: int
     max_rows_per_seq: int
+    seq_slot: torch.Tensor | None = None  # page-table row per sequence group (None: group b is slot b)
 
 
 class QuantModel:
@@ -241,7 +242,8 @@ class QuantModel:
             kernels.attention(self.q, self.k_cache[li], self.v_cache[li], self.page_table, meta.seq_rows, meta.pos,
                               max_rows_per_seq=meta.max_rows_per_seq, max_kv_len=max_kv_len, scale=c.scale,
                               keys_per_split=self.keys_per_split,
-                              window=0 if glob else c.sliding_window, out=self.attn, rows=m, ws=self.ws_attn)
+                              window=0 if glob else c.sliding_window, out=self.attn, rows=m, ws=self.ws_attn,
+                              seq_slot=meta.seq_slot)
             kernels.qgemm(self.attn, layer.o.w, layer.o.s, layer.o.b, epilogue="residual", residual=h, out=h,
                           rows=m, ws=self.ws_gemm)
             kernels.rmsnorm(h, layer.post_norm, c.eps, gemma=gemma, out=xn, rows=m)
@@ -266,7 +268,8 @@ class QuantModel:
                        pos=torch.tensor(positions, dtype=torch.int32, device=dev),
                        seq=torch.full((m,), seq, dtype=torch.int32, device=dev),
                        seq_rows=torch.tensor([0, m], dtype=torch.int32, device=dev),
-                       rows=m, max_rows_per_seq=m)
+                       rows=m, max_rows_per_seq=m,
+                       seq_slot=torch.tensor([seq], dtype=torch.int32, device=dev))
 
     def prefill(self, tokens: torch.Tensor, seq: int = 0, start: int = 0) -> None:
         """Write the KV of `tokens` (int32 on the device) at slots start.. of sequence slot `seq`."""

@@ -70,6 +70,10 @@ class _Shared:
         return buf
 
 
+def _ptr_or_none(t):
+    return t.data_ptr() if t is not None else None
+
+
 def _scratch(ws, device, need, purpose):
     if need == 0:
         return None, 0
@@ -229,7 +233,7 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pag
               seq_rows: torch.Tensor, row_slot: torch.Tensor, *, max_rows_per_seq: int, max_kv_len: int,
               scale: float, keys_per_split: int = 64, window: int = 0, tree_mask: torch.Tensor | None = None,
               tree_base: torch.Tensor | None = None, out: torch.Tensor | None = None, rows: int | None = None,
-              ws: torch.Tensor | None = None) -> torch.Tensor:
+              ws: torch.Tensor | None = None, seq_slot: torch.Tensor | None = None) -> torch.Tensor:
     """Paged verification attention; q [M, Hq, D] -> out [M, Hq, D] (bf16)."""
     hq, d = q.shape[-2], q.shape[-1]
     m = q.shape[0] if rows is None else rows
@@ -241,7 +245,7 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pag
         raise ValueError("attention shape not supported")
     ws_ptr, ws_bytes = _scratch(ws, q.device, need, "attention")
     _lib.call("im_attention_paged", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), page_table.data_ptr(),
-              page_table.shape[-1], seq_rows.data_ptr(), row_slot.data_ptr(),
+              page_table.shape[-1], seq_rows.data_ptr(), _ptr_or_none(seq_slot), row_slot.data_ptr(),
               tree_mask.data_ptr() if tree_mask is not None else None,
               tree_base.data_ptr() if tree_base is not None else None, b, max_rows_per_seq, hq, hkv, d, max_kv_len,
               keys_per_split, window, float(scale), out.data_ptr(), ws_ptr, ws_bytes, _stream(q.device))
@@ -258,3 +262,49 @@ def spec_commit(hist, n, target, b: int, k: int, out_tokens, out_count, stats=No
     _lib.call("im_spec_commit", hist.data_ptr(), hist.shape[-1], n.data_ptr(), target.data_ptr(), b, k,
               out_tokens.data_ptr(), out_count.data_ptr(), stats.data_ptr() if stats is not None else None,
               _stream(hist.device))
+
+
+def sampling_workspace_bytes(rows: int) -> int:
+    return int(_lib.load().im_sampling_workspace_bytes(rows))
+
+
+def sample_rows(logits: torch.Tensor, temperature: float, top_p: float, seed: int, offset: int = 0, *,
+                offset_dev: torch.Tensor | None = None, streams: torch.Tensor | None = None, draw: int = 0,
+                out: torch.Tensor | None = None, out_stride: int = 1, rows: int | None = None,
+                ws: torch.Tensor | None = None) -> torch.Tensor:
+    """One token per row from softmax(logits / T) restricted to top-p, on the Philox stream."""
+    _check(logits, "logits", (torch.bfloat16,))
+    v = logits.shape[-1]
+    rows = logits.numel() // v if rows is None else rows
+    out = torch.empty(rows, dtype=torch.int32, device=logits.device) if out is None else out
+    ws_ptr, ws_bytes = _scratch(ws, logits.device, sampling_workspace_bytes(rows), "sampling")
+    _lib.call("im_sample_rows", logits.data_ptr(), rows, v, v, float(temperature), float(top_p), int(seed),
+              int(offset), _ptr_or_none(offset_dev), _ptr_or_none(streams), int(draw), out.data_ptr(), out_stride,
+              ws_ptr, ws_bytes, _stream(logits.device))
+    return out
+
+
+def accept_stochastic(target_logits: torch.Tensor, draft_logits: torch.Tensor, drafts: torch.Tensor, *, b: int,
+                      k: int, drafts_ld: int, temperature: float, top_p: float, seed: int, offset: int = 0,
+                      offset_dev: torch.Tensor | None = None, tokens: torch.Tensor | None = None,
+                      count: torch.Tensor | None = None, ratios: torch.Tensor | None = None,
+                      ws: torch.Tensor | None = None):
+    """p/q rejection sampling: target_logits [B, k+1, V], draft_logits [k, B, V] -> (tokens [B, k+1], count [B])."""
+    _check(target_logits, "target_logits", (torch.bfloat16,))
+    _check(draft_logits, "draft_logits", (torch.bfloat16,), target_logits.device)
+    device = target_logits.device
+    v = target_logits.shape[-1]
+    tokens = torch.empty((b, k + 1), dtype=torch.int32, device=device) if tokens is None else tokens
+    count = torch.empty(b, dtype=torch.int32, device=device) if count is None else count
+    ws_ptr, ws_bytes = _scratch(ws, device, sampling_workspace_bytes(b * (2 * k + 1)), "sampling")
+    _lib.call("im_accept_stochastic", target_logits.data_ptr(), draft_logits.data_ptr(), b, k, v, v,
+              drafts.data_ptr(), drafts_ld, float(temperature), float(top_p), int(seed), int(offset),
+              _ptr_or_none(offset_dev), tokens.data_ptr(), count.data_ptr(), _ptr_or_none(ratios), ws_ptr,
+              ws_bytes, _stream(device))
+    return tokens, count
+
+
+def philox(seed: int, offset: int, stream_id: int, n: int, device) -> torch.Tensor:
+    out = torch.empty((n, 4), dtype=torch.int32, device=device)
+    _lib.call("im_philox4x32_10", int(seed), int(offset), int(stream_id), int(n), out.data_ptr(), _stream(device))
+    return out

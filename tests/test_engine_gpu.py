@@ -87,7 +87,7 @@ def test_attention_matches_oracle(cuda, d, hq, hkv, rows, window, kpc):
     b = 3
     lens = [700, 130, 17 + rows]
     max_pages = 48
-    table = np.stack([rng.permutation(b * max_pages)[:max_pages] for _ in range(b)]).astype(np.int32)
+    table = rng.permutation(b * max_pages).reshape(b, max_pages).astype(np.int32)  # disjoint pages per sequence
     kcache = np.zeros((b * max_pages, hkv, 16, d), dtype=np.uint16)
     vcache = np.zeros_like(kcache)
     qs, slots, seq_rows, per_seq = [], [], [0], []
