@@ -30,6 +30,9 @@ SIGNATURES: dict[str, tuple] = {
     "im_qgemm_w4g64_ex": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _INT, _INT, _P, _SZ, _P]),
     "im_qgemm_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "im_qgemm_set_splits": (_INT, [_INT]),
+    "im_qgemm_tma": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _INT, _P, _SZ, _P]),
+    "im_qgemm_tma_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "im_qgemm_tma_status": (_INT, [_P, _P]),
     "im_argmax_rows": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _P, _P, _SZ, _P]),
     "im_argmax_workspace_bytes": (_SZ, [_I64, _I64]),
     "im_verify_greedy": (_INT, [_P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _SZ, _P]),
