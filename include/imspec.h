@@ -76,6 +76,20 @@ int im_qgemm_w4g64_ex(const uint32_t* w, const uint16_t* scales, const uint16_t*
                       uint16_t* y, const uint16_t* residual, int64_t M, int64_t N, int64_t K, int epilogue,
                       int variant, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * im_qgemm_w4g64 for callers that cannot allocate device memory (an engine that owns all device memory through
+ * its own pool, a plugin that may not call cudaMalloc or synchronise on its decode path). No reference
+ * counterpart: it is an addition of this library. It splits K across CTAs with the same plan as
+ * im_qgemm_w4g64_ex given a workspace (so the results are bit-identical), keeping the scratch in one static
+ * device array of im_qgemm_noalloc_capacity() bytes that every GPU loading the library holds until exit.
+ * Shapes whose scratch would exceed it return IM_UNSUPPORTED. The first call on a device looks the array up and
+ * zeroes its counters synchronously, so make it before any stream capture. Calls share the array: calls that
+ * overlap on the GPU race and must not be issued.
+ */
+int im_qgemm_w4g64_noalloc(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const uint16_t* x,
+                           uint16_t* y, int64_t M, int64_t N, int64_t K, void* stream);
+size_t im_qgemm_noalloc_capacity(void);
+
 /* Workspace bytes im_qgemm_w4g64_ex needs for this shape (0: it does not split K). */
 size_t im_qgemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 

@@ -20,6 +20,8 @@
 //    by the last CTA to finish a tile. The partition depends on (N, K) only, never on M, so every
 //    activation row gets the same arithmetic whatever M is (row invariance: a verify row equals a
 //    one-row decode bit for bit).
+#include <mutex>
+
 #include "common.cuh"
 #include "../../include/imspec.h"
 
@@ -530,4 +532,83 @@ extern "C" int im_qgemm_w4g64(const uint32_t* w, const uint16_t* scales, const u
                               const uint16_t* x, uint16_t* y, int64_t M, int64_t N, int64_t K, void* stream) {
   return im_qgemm_w4g64_ex(w, scales, biases, x, y, nullptr, M, N, K, IM_EPI_STORE, IM_QGEMM_AUTO, nullptr, 0,
                            stream);
+}
+
+// ---- entry point for callers that cannot allocate device memory ---------------------------------------------
+// Some callers of this library cannot call cudaMalloc: code running inside another runtime's allocator
+// discipline (a host process whose device memory is owned by a pool it may not grow, a plugin loaded into an
+// engine that forbids allocations on its decode path) or code that must not synchronise the device, which a
+// first-use cudaMalloc can do. For them the split-K qGEMM keeps its scratch (per-tile arrival counters and CTA
+// partials) in one file-scope device array instead of a caller-provided workspace.
+//
+// The array is allocated when the library is loaded, on every GPU that loads it, and held until the process
+// exits. Its address is looked up once per device with cudaGetSymbolAddress (the host-side name of a __device__
+// array is not a device address). The first call on a device does that set-up and zeroes the counters with a
+// synchronous cudaMemset, so it must come before any stream capture on that device. Calls never allocate.
+// Every call shares the one array: the kernel returns its counters to zero, but calls that overlap on the GPU
+// (two streams, or two host threads) race on it and must not be issued.
+constexpr size_t QG_NOALLOC_BYTES = (size_t)8 << 20;  // 16 KiB of counters + ~8 MiB of partials
+static __device__ __align__(256) unsigned char g_qgemm_noalloc_scratch[QG_NOALLOC_BYTES];
+
+namespace {
+constexpr int QG_NOALLOC_MAX_DEVICES = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[QG_NOALLOC_MAX_DEVICES] = {};
+}  // namespace
+
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    set_error("im_qgemm_w4g64_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+    return IM_CUDA_ERROR;
+  }
+  IM_REQUIRE(dev >= 0 && dev < QG_NOALLOC_MAX_DEVICES, IM_UNSUPPORTED, "im_qgemm_w4g64_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_qgemm_noalloc_scratch);
+    if (e != cudaSuccess) {
+      set_error("im_qgemm_w4g64_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      return IM_CUDA_ERROR;
+    }
+    e = cudaMemset(ptr, 0, QG_COUNTER_BYTES);
+    if (e != cudaSuccess) {
+      set_error("im_qgemm_w4g64_noalloc: zeroing the counters: %s", cudaGetErrorString(e));
+      return IM_CUDA_ERROR;
+    }
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return IM_OK;
+}
+
+extern "C" size_t im_qgemm_noalloc_capacity(void) { return QG_NOALLOC_BYTES; }
+
+extern "C" int im_qgemm_w4g64_noalloc(const uint32_t* w, const uint16_t* scales, const uint16_t* biases,
+                                      const uint16_t* x, uint16_t* y, int64_t M, int64_t N, int64_t K, void* stream) {
+  clear_error();
+  IM_REQUIRE(M >= 0 && N >= 1 && K >= 64, IM_INVALID, "im_qgemm_w4g64_noalloc: bad sizes M=%lld N=%lld K=%lld",
+             (long long)M, (long long)N, (long long)K);
+  IM_REQUIRE(K % 64 == 0, IM_UNSUPPORTED, "im_qgemm_w4g64_noalloc: K=%lld is not a multiple of 64", (long long)K);
+  IM_REQUIRE(N <= (1 << 30) && K <= (1 << 24), IM_UNSUPPORTED, "im_qgemm_w4g64_noalloc: N or K too large");
+  IM_REQUIRE(M <= 32, IM_UNSUPPORTED, "im_qgemm_w4g64_noalloc: M=%lld exceeds 32", (long long)M);
+  if (M == 0) return IM_OK;
+  IM_REQUIRE(w && scales && biases && x && y, IM_INVALID, "im_qgemm_w4g64_noalloc: null pointer");
+  IM_REQUIRE(aligned(w, 16) && aligned(x, 16), IM_INVALID, "im_qgemm_w4g64_noalloc: w and x must be 16-byte aligned");
+  IM_REQUIRE(aligned(scales, 2) && aligned(biases, 2) && aligned(y, 2), IM_INVALID,
+             "im_qgemm_w4g64_noalloc: misaligned bf16");
+  const QgemmPlan p = plan_mma(M, N, K, true);
+  IM_REQUIRE(p.workspace <= QG_NOALLOC_BYTES, IM_UNSUPPORTED,
+             "im_qgemm_w4g64_noalloc: this shape needs %zu bytes of scratch; the static scratch holds %zu "
+             "(use im_qgemm_w4g64_ex with a workspace)",
+             p.workspace, QG_NOALLOC_BYTES);
+  void* scratch = nullptr;
+  if (p.splits > 1) {
+    const int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+  }
+  dispatch_mma<IM_EPI_STORE>(p, w, scales, biases, x, y, nullptr, (int)M, (int)N, (int)K, scratch,
+                             reinterpret_cast<cudaStream_t>(stream));
+  return check_launch("qgemm_mma (no-alloc)");
 }
