@@ -113,6 +113,32 @@ size_t im_qgemm_tma_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int im_qgemm_tma_status(const void* workspace, uint32_t* status);
 
 /*
+ * qGEMM v4 over weights repacked once into MMA-fragment order (the engine's resident format).
+ * im_qgemm_pack_w4g64 converts MLX-layout w/scales/biases [N, K] into `packed` (16-byte aligned,
+ * im_qgemm_packed_bytes(N, K) bytes): rows padded to 32-row tiles, one contiguous 1152-byte unit per
+ * (tile, 64-group) holding that tile's codes in lane order and its 32 scales/biases.
+ * im_qgemm_packed computes the same product and epilogues as im_qgemm_w4g64_ex (M <= 32) from it, and can fuse
+ * the RMSNorm that precedes a projection: with norm_weight != NULL, x is the raw residual stream and each row
+ * is normalised on the way in (x * 1/sqrt(sum(x^2)/K + eps) * w', w' = w or 1 + w when gemma_norm), its sum of
+ * squares taken from norm_sq[p * 32 + m] summed over p < norm_parts (per-tile partial sums). With
+ * out_sq != NULL, a store/residual epilogue writes those per-tile partial sums of its own output rows
+ * ([ceil(N/32)][32] floats) for the next normalised GEMM. workspace >= im_qgemm_packed_workspace_bytes(M, N, K)
+ * (256-byte aligned, zero-filled before first use) when that is non-zero; calls sharing it must not overlap.
+ * Replaces the same reference interfaces as im_qgemm_w4g64, plus the RMSNorm before each projection of the
+ * decode layer (ironmule/paired_research.py:177-215).
+ */
+size_t im_qgemm_packed_bytes(int64_t N, int64_t K);
+int im_qgemm_pack_w4g64(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, int64_t N, int64_t K,
+                        void* packed, void* stream);
+size_t im_qgemm_packed_workspace_bytes(int64_t M, int64_t N, int64_t K);
+/* Tuning hook of the K-split policy: a forced split (0 = automatic), the CTA count the automatic policy aims
+ * for, and its largest split. Process-wide; changes workspace sizes, so set it before sizing workspaces. */
+int im_qgemm_packed_tune(int split_override, int target_ctas, int max_split);
+int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* y, const uint16_t* residual, int64_t M, int64_t N,
+                    int64_t K, int epilogue, const float* norm_sq, int64_t norm_parts, const uint16_t* norm_weight,
+                    float eps, int gemma_norm, float* out_sq, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Row statistics over a logits matrix: for each row r of logits[rows, V] (bf16, row stride ld elements)
  * writes argmax[r * argmax_stride] (lowest index among equal maxima) and, if conf != NULL, the top-1 probability
  * conf[r] = 1 / sum_v exp(l_v - l_max). Replaces the host numpy scan of
@@ -172,12 +198,14 @@ int im_qk_norm_rope_kv(const uint16_t* qkv, const uint16_t* q_norm, const uint16
 
 /*
  * Embedding gather from a 4-bit table: out[m, :] = bf16(scale * q + bias) of row tokens[m * tokens_stride] (int32;
- * clamped to [0, V)), times bf16(mult) when mult != 1 (Gemma-3 scales by sqrt(hidden)). The tied table
+ * clamped to [0, V)), times bf16(mult) when mult != 1 (Gemma-3 scales by sqrt(hidden)); out_sq (M <= 32 floats, may
+ * be NULL) receives each row's sum of squares, the norm_sq input of a fused-RMSNorm im_qgemm_packed. The tied table
  * doubles as the LM head through im_qgemm_w4g64 (nn.QuantizedEmbedding / as_linear,
  * ironmule/cuda_native.py:227-229).
  */
 int im_embed_w4g64(const int32_t* tokens, int64_t tokens_stride, const uint32_t* wq, const uint16_t* scales,
-                   const uint16_t* biases, int64_t M, int64_t V, int64_t H, float mult, uint16_t* out, void* stream);
+                   const uint16_t* biases, int64_t M, int64_t V, int64_t H, float mult, uint16_t* out, float* out_sq,
+                   void* stream);
 
 /*
  * Paged verification attention: out[M, Hq, D] for q[M, Hq, D] whose rows are grouped by sequence (rows of

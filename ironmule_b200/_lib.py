@@ -35,6 +35,12 @@ SIGNATURES: dict[str, tuple] = {
     "im_qgemm_tma": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _INT, _P, _SZ, _P]),
     "im_qgemm_tma_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
     "im_qgemm_tma_status": (_INT, [_P, _P]),
+    "im_qgemm_packed_bytes": (_SZ, [_I64, _I64]),
+    "im_qgemm_pack_w4g64": (_INT, [_P, _P, _P, _I64, _I64, _P, _P]),
+    "im_qgemm_packed_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "im_qgemm_packed_tune": (_INT, [_INT, _INT, _INT]),
+    "im_qgemm_packed": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _INT, _P, _I64, _P, ctypes.c_float, _INT, _P, _P,
+                               _SZ, _P]),
     "im_argmax_rows": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _P, _P, _SZ, _P]),
     "im_argmax_workspace_bytes": (_SZ, [_I64, _I64]),
     "im_verify_greedy": (_INT, [_P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _SZ, _P]),
@@ -42,7 +48,7 @@ SIGNATURES: dict[str, tuple] = {
     "im_rmsnorm": (_INT, [_P, _I64, _P, _P, _I64, _I64, ctypes.c_float, _INT, _P]),
     "im_qk_norm_rope_kv": (_INT, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, ctypes.c_float,
                                   _INT, _P, _P, _P, _P]),
-    "im_embed_w4g64": (_INT, [_P, _I64, _P, _P, _P, _I64, _I64, _I64, ctypes.c_float, _P, _P]),
+    "im_embed_w4g64": (_INT, [_P, _I64, _P, _P, _P, _I64, _I64, _I64, ctypes.c_float, _P, _P, _P]),
     "im_attention_paged": (_INT, [_P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
                                   _I64, _I64, _I64, ctypes.c_float, _P, _P, _SZ, _P]),
     "im_attention_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _I64, _I64, _I64]),

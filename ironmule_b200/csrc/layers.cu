@@ -102,7 +102,8 @@ qk_rope_kv_kernel(const uint16_t* __restrict__ qkv, const uint16_t* __restrict__
 // sqrt(hidden), rounded to bf16 as the reference does) when mult != 1.
 __global__ void embed_kernel(const int* __restrict__ tokens, int tstride, const uint32_t* __restrict__ wq,
                              const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, int H, int V,
-                             float mult, uint16_t* __restrict__ out) {
+                             float mult, uint16_t* __restrict__ out, float* __restrict__ out_sq) {
+  __shared__ float sh[4];
   const int m = blockIdx.x;
   int tok = tokens[(size_t)m * tstride];
   tok = tok < 0 ? 0 : (tok >= V ? V - 1 : tok);
@@ -110,6 +111,7 @@ __global__ void embed_kernel(const int* __restrict__ tokens, int tstride, const 
   const uint16_t* srow = sc + (size_t)tok * (H / 64);
   const uint16_t* brow = bi + (size_t)tok * (H / 64);
   const float mb = round_bf(mult);
+  float sq = 0.f;
   for (int wd = threadIdx.x; wd < H / 8; wd += blockDim.x) {
     const uint32_t u = row[wd];
     const float s = bf(srow[wd >> 3]), b = bf(brow[wd >> 3]);
@@ -117,8 +119,16 @@ __global__ void embed_kernel(const int* __restrict__ tokens, int tstride, const 
     for (int e = 0; e < 8; e++) {
       float val = round_bf(fmaf(s, (float)((u >> (4 * e)) & 0xFu), b));
       if (mult != 1.0f) val = val * mb;
-      out[(size_t)m * H + wd * 8 + e] = to_bf(val);
+      const uint16_t o = to_bf(val);
+      out[(size_t)m * H + wd * 8 + e] = o;
+      sq = fmaf(bf(o), bf(o), sq);
     }
+  }
+  if (out_sq) {  // the row's sum of squares for a fused RMSNorm downstream (fixed order: warps, then in order)
+    sq = warp_sum(sq);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = sq;
+    __syncthreads();
+    if (threadIdx.x == 0) out_sq[m] = sh[0] + sh[1] + sh[2] + sh[3];
   }
 }
 
@@ -166,13 +176,14 @@ extern "C" int im_qk_norm_rope_kv(const uint16_t* qkv, const uint16_t* q_norm, c
 
 extern "C" int im_embed_w4g64(const int32_t* tokens, int64_t tokens_stride, const uint32_t* wq,
                               const uint16_t* scales, const uint16_t* biases, int64_t M, int64_t V, int64_t H,
-                              float mult, uint16_t* out, void* stream) {
+                              float mult, uint16_t* out, float* out_sq, void* stream) {
   clear_error();
   IM_REQUIRE(M >= 0 && V >= 1 && H >= 64 && H % 64 == 0 && tokens_stride >= 1, IM_INVALID,
              "im_embed_w4g64: bad sizes");
   if (M == 0) return IM_OK;
   IM_REQUIRE(tokens && wq && scales && biases && out, IM_INVALID, "im_embed_w4g64: null pointer");
+  IM_REQUIRE(!out_sq || M <= 32, IM_INVALID, "im_embed_w4g64: row sums of squares cover at most 32 rows");
   embed_kernel<<<(unsigned)M, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      tokens, (int)tokens_stride, wq, scales, biases, (int)H, (int)V, mult, out);
+      tokens, (int)tokens_stride, wq, scales, biases, (int)H, (int)V, mult, out, out_sq);
   return check_launch("embed_kernel");
 }

@@ -1,0 +1,512 @@
+// qGEMM v4: the engine's 4-bit GEMM over weights repacked once at load into MMA-fragment order.
+//
+// Packed format (im_qgemm_pack_w4g64): rows padded to 32-row tiles; unit (tile, group) = 1152 contiguous bytes,
+// units in tile-major, group-minor order:
+//   codes, 1024 B: lane L (g = L/4, t = L%4) owns bytes [32L, 32L+32) = the 8-byte slice (words 2t, 2t+1 of the
+//     group) of rows g, g+8, 16+g, 24+g of the tile -- exactly the A fragments of the lane's two 16-row MMAs;
+//   scales/biases, 128 B: for g = 0..7, 16 bytes = bf16 scale of rows g, g+8, 16+g, 24+g then their biases.
+// So a warp streams one contiguous 1152-byte unit per group: two 16-byte code loads and one broadcast 16-byte
+// scale/bias load per lane. (MLX's own layout stays the drop-in format of im_qgemm_w4g64; the engine repacks
+// its resident weights once.)
+//
+// The arithmetic is the warp-MMA kernel's (exact bf16 codes 128+q, fp32 group affine s*acc + (b-128 s)*sum(x)).
+// A CTA is 4 warps = 4 consecutive tiles (128 rows) over a K range (CTAs split K when needed); its prologue stages
+// the activation fragments and per-group sums of its K range in shared memory once, optionally applying RMSNorm
+// on the way in: inv_rms of each activation row comes from per-tile sums of squares that the previous residual
+// GEMM (or the embedding) wrote, summed in tile order. A residual epilogue can write those sums for the next GEMM.
+// Partition (tiles x K splits) depends on (N, K) only; rows are independent: a row's bits do not depend on M.
+#include "common.cuh"
+#include "../../include/imspec.h"
+
+namespace im {
+
+constexpr int Q4_WARPS = 4;
+constexpr int Q4_THREADS = Q4_WARPS * 32;
+constexpr int Q4_UNIT = 1152;
+constexpr int Q4_RMAX = 16;               // groups per CTA range (shared-memory budget: 16 KB per 8 rows)
+constexpr size_t Q4_COUNTER_BYTES = 65536;
+constexpr int Q4_DEPTH = 3;               // units in flight per warp
+static int g_q4_split_override = 0;       // sweep hook (0 = automatic)
+static int g_q4_target_ctas = 148 * 4;    // split policy: aim for this many CTAs
+static int g_q4_max_split = 8;
+constexpr uint32_t Q4_128 = 0x43004300u;
+
+__device__ __forceinline__ void q4_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void q4_codes(uint32_t u, uint32_t* p) {
+  p[0] = (u & 0x000F000Fu) | Q4_128;
+  p[1] = ((u >> 4) & 0x000F000Fu) | Q4_128;
+  p[2] = ((u >> 8) & 0x000F000Fu) | Q4_128;
+  p[3] = ((u >> 12) & 0x000F000Fu) | Q4_128;
+}
+
+__device__ __forceinline__ uint4 q4_ld_stream(const void* p) { return ldg_stream_u4(p); }
+
+// ---- repack ---------------------------------------------------------------------------------------------
+__global__ void q4_pack_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ sc,
+                               const uint16_t* __restrict__ bi, int N, int K, unsigned char* __restrict__ out) {
+  const int G = K >> 6;
+  const long long unit = blockIdx.x;  // tile * G + group
+  const int tile = (int)(unit / G), grp = (int)(unit % G);
+  unsigned char* dst = out + unit * Q4_UNIT;
+  const int lane = threadIdx.x;  // 32 threads
+  const int g = lane >> 2, t = lane & 3;
+  const int rows[4] = {g, g + 8, 16 + g, 24 + g};
+  uint32_t words[8];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int r = tile * 32 + rows[j];
+    if (r < N) {
+      const uint32_t* src = w + (size_t)r * (K >> 3) + grp * 8 + 2 * t;
+      words[2 * j] = src[0];
+      words[2 * j + 1] = src[1];
+    } else {
+      words[2 * j] = words[2 * j + 1] = 0u;
+    }
+  }
+  uint4* d = reinterpret_cast<uint4*>(dst + lane * 32);
+  d[0] = make_uint4(words[0], words[1], words[2], words[3]);
+  d[1] = make_uint4(words[4], words[5], words[6], words[7]);
+  if (t == 0) {
+    uint16_t sb[8];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int r = tile * 32 + rows[j];
+      sb[j] = r < N ? sc[(size_t)r * G + grp] : (uint16_t)0;
+      sb[4 + j] = r < N ? bi[(size_t)r * G + grp] : (uint16_t)0;
+    }
+    uint4 v;
+    v.x = (uint32_t)sb[0] | ((uint32_t)sb[1] << 16);
+    v.y = (uint32_t)sb[2] | ((uint32_t)sb[3] << 16);
+    v.z = (uint32_t)sb[4] | ((uint32_t)sb[5] << 16);
+    v.w = (uint32_t)sb[6] | ((uint32_t)sb[7] << 16);
+    *reinterpret_cast<uint4*>(dst + 1024 + g * 16) = v;
+  }
+}
+
+// ---- the GEMM -------------------------------------------------------------------------------------------
+struct Q4Args {
+  const unsigned char* wp;  // packed units
+  const uint16_t* x;        // [M, K] activations (raw residual when norm_w != NULL)
+  uint16_t* y;
+  const uint16_t* res;
+  const float* norm_sq;     // [norm_parts][32] sums of squares of x rows (RMSNorm prologue) or NULL
+  const uint16_t* norm_w;   // [K]
+  float* out_sq;            // [tiles][32] sums of squares of the written rows (residual epilogue) or NULL
+  float* partial;
+  unsigned* counters;
+  float eps;
+  int M, N, K, tiles, splits, norm_parts, gemma_norm;
+};
+
+// Dynamic shared memory: xf [rmax][NT][32 lanes][2 x 16 B] activation fragments, sx [rmax][NT*8] group sums,
+// inv [32] RMSNorm factors.
+__host__ __device__ constexpr size_t q4_smem_bytes(int nt) {
+  return (size_t)Q4_RMAX * nt * 32 * 32 + (size_t)Q4_RMAX * nt * 8 * 4 + 32 * 4;
+}
+
+template <int NT, int EPI>
+__global__ void __launch_bounds__(Q4_THREADS)
+qgemm_packed_kernel(Q4Args a) {
+  extern __shared__ __align__(16) unsigned char q4_raw[];
+  uint4 (*xf)[NT][32][2] = reinterpret_cast<uint4 (*)[NT][32][2]>(q4_raw);
+  float (*sxs)[NT * 8] = reinterpret_cast<float (*)[NT * 8]>(q4_raw + (size_t)Q4_RMAX * NT * 32 * 32);
+  float* inv_s = reinterpret_cast<float*>(q4_raw + (size_t)Q4_RMAX * NT * 32 * 32 + (size_t)Q4_RMAX * NT * 8 * 4);
+  const int G = a.K >> 6;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int split = blockIdx.y;
+  const int cg0 = (int)(((long long)G * split) / a.splits);
+  const int cg1 = (int)(((long long)G * (split + 1)) / a.splits);
+  const int ng = cg1 - cg0;
+  const int tile = blockIdx.x * Q4_WARPS + warp;
+
+  // ---- prologue: RMSNorm factors, then the activation fragments and group sums of [cg0, cg1)
+  if (a.norm_w) {
+    for (int m = threadIdx.x; m < NT * 8; m += Q4_THREADS) {
+      float s = 0.f;
+      if (m < a.M)
+        for (int p = 0; p < a.norm_parts; p++) s += a.norm_sq[p * 32 + m];
+      inv_s[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(s, (float)a.K) + a.eps));
+    }
+    __syncthreads();
+  }
+  // one thread per (group, activation row m, quarter t): 16 values -> fragment order + partial sum
+  for (int job = threadIdx.x; job < ng * NT * 32; job += Q4_THREADS) {
+    const int tq = job & 3;
+    const int m = (job >> 2) % (NT * 8);
+    const int gl = (job >> 2) / (NT * 8);
+    const int grp = cg0 + gl;
+    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+    float part = 0.f;
+    if (m < a.M) {
+      const uint16_t* xp = a.x + (size_t)m * a.K + (size_t)grp * 64 + 16 * tq;
+      lo = __ldg(reinterpret_cast<const uint4*>(xp));
+      hi = __ldg(reinterpret_cast<const uint4*>(xp + 8));
+      if (a.norm_w) {
+        const float inv = inv_s[m];
+        const uint16_t* wv = a.norm_w + (size_t)grp * 64 + 16 * tq;
+        uint32_t* l32 = reinterpret_cast<uint32_t*>(&lo);
+        uint32_t* h32 = reinterpret_cast<uint32_t*>(&hi);
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          uint32_t* word = e < 4 ? &l32[e] : &h32[e - 4];
+          const float w0 = a.gemma_norm ? 1.0f + bf(wv[2 * e]) : bf(wv[2 * e]);
+          const float w1 = a.gemma_norm ? 1.0f + bf(wv[2 * e + 1]) : bf(wv[2 * e + 1]);
+          const uint16_t n0 = to_bf((bf_lo(*word) * inv) * w0);
+          const uint16_t n1 = to_bf((bf_hi(*word) * inv) * w1);
+          *word = (uint32_t)n0 | ((uint32_t)n1 << 16);
+        }
+      }
+      const uint32_t* l32 = reinterpret_cast<const uint32_t*>(&lo);
+      const uint32_t* h32 = reinterpret_cast<const uint32_t*>(&hi);
+#pragma unroll
+      for (int e = 0; e < 4; e++) part += bf_lo(l32[e]) + bf_hi(l32[e]);
+#pragma unroll
+      for (int e = 0; e < 4; e++) part += bf_lo(h32[e]) + bf_hi(h32[e]);
+    }
+    uint4 f0, f1;
+    f0.x = __byte_perm(lo.x, lo.z, 0x5410);
+    f0.y = __byte_perm(lo.x, lo.z, 0x7632);
+    f0.z = __byte_perm(lo.y, lo.w, 0x5410);
+    f0.w = __byte_perm(lo.y, lo.w, 0x7632);
+    f1.x = __byte_perm(hi.x, hi.z, 0x5410);
+    f1.y = __byte_perm(hi.x, hi.z, 0x7632);
+    f1.z = __byte_perm(hi.y, hi.w, 0x5410);
+    f1.w = __byte_perm(hi.y, hi.w, 0x7632);
+    const int nt = m >> 3, gm = m & 7;
+    xf[gl][nt][gm * 4 + tq][0] = f0;
+    xf[gl][nt][gm * 4 + tq][1] = f1;
+    // the four quarters of (group, m) are adjacent threads: fixed-order pair sums
+    part += __shfl_xor_sync(0xffffffffu, part, 1);
+    part += __shfl_xor_sync(0xffffffffu, part, 2);
+    if (tq == 0) sxs[gl][m] = part;
+  }
+  __syncthreads();
+  if (tile >= a.tiles) return;
+
+  // ---- main loop: this warp's tile over [cg0, cg1), one 1152-byte unit per group, Q4_DEPTH units in flight
+  const unsigned char* up = a.wp + ((size_t)tile * G + cg0) * Q4_UNIT;
+  float tot[2][NT][4];
+#pragma unroll
+  for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) tot[tt][nt][e] = 0.f;
+  // a ring of Q4_DEPTH units in flight per warp (two 16-byte code loads + one scale/bias load per lane each)
+  uint4 rc0[Q4_DEPTH], rc1[Q4_DEPTH], rsb[Q4_DEPTH];
+#pragma unroll
+  for (int d = 0; d < Q4_DEPTH; d++) {
+    if (d < ng) {
+      const unsigned char* nu = up + (size_t)d * Q4_UNIT;
+      rc0[d] = q4_ld_stream(nu + lane * 32);
+      rc1[d] = q4_ld_stream(nu + lane * 32 + 16);
+      rsb[d] = __ldg(reinterpret_cast<const uint4*>(nu + 1024 + g * 16));
+    }
+  }
+#pragma unroll 1
+  for (int gl0 = 0; gl0 < ng; gl0 += Q4_DEPTH) {
+#pragma unroll
+  for (int d = 0; d < Q4_DEPTH; d++) {
+    const int gl = gl0 + d;
+    if (gl >= ng) break;
+    const uint4 c0 = rc0[d], c1 = rc1[d], sb = rsb[d];
+    if (gl + Q4_DEPTH < ng) {
+      const unsigned char* nu = up + (size_t)(gl + Q4_DEPTH) * Q4_UNIT;
+      rc0[d] = q4_ld_stream(nu + lane * 32);
+      rc1[d] = q4_ld_stream(nu + lane * 32 + 16);
+      rsb[d] = __ldg(reinterpret_cast<const uint4*>(nu + 1024 + g * 16));
+    }
+    uint32_t px[NT][8];
+    float sx[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+      const uint4 f0 = xf[gl][nt][lane][0], f1 = xf[gl][nt][lane][1];
+      px[nt][0] = f0.x; px[nt][1] = f0.y; px[nt][2] = f0.z; px[nt][3] = f0.w;
+      px[nt][4] = f1.x; px[nt][5] = f1.y; px[nt][6] = f1.z; px[nt][7] = f1.w;
+      const float2 s2 = *reinterpret_cast<const float2*>(&sxs[gl][nt * 8 + 2 * t]);
+      sx[nt][0] = s2.x;
+      sx[nt][1] = s2.y;
+    }
+    // sb: s(g), s(g+8), s(16+g), s(24+g), b(g), b(g+8), b(16+g), b(24+g)
+    const float sv[4] = {bf_lo(sb.x), bf_hi(sb.x), bf_lo(sb.y), bf_hi(sb.y)};
+    const float bv[4] = {bf_lo(sb.z), bf_hi(sb.z), bf_lo(sb.w), bf_hi(sb.w)};
+    const uint32_t wd[2][4] = {{c0.x, c0.y, c0.z, c0.w}, {c1.x, c1.y, c1.z, c1.w}};
+#pragma unroll
+    for (int tt = 0; tt < 2; tt++) {
+      uint32_t pa[8], pb[8];
+      q4_codes(wd[tt][0], pa);
+      q4_codes(wd[tt][1], pa + 4);
+      q4_codes(wd[tt][2], pb);
+      q4_codes(wd[tt][3], pb + 4);
+      float acc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[nt][e] = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+          q4_mma(acc[nt], pa[2 * q], pb[2 * q], pa[2 * q + 1], pb[2 * q + 1], px[nt][2 * q], px[nt][2 * q + 1]);
+      const float s0 = sv[2 * tt], s1 = sv[2 * tt + 1];
+      const float b0 = fmaf(-128.f, s0, bv[2 * tt]), b1 = fmaf(-128.f, s1, bv[2 * tt + 1]);
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++) {
+        tot[tt][nt][0] = fmaf(b0, sx[nt][0], fmaf(s0, acc[nt][0], tot[tt][nt][0]));
+        tot[tt][nt][1] = fmaf(b0, sx[nt][1], fmaf(s0, acc[nt][1], tot[tt][nt][1]));
+        tot[tt][nt][2] = fmaf(b1, sx[nt][0], fmaf(s1, acc[nt][2], tot[tt][nt][2]));
+        tot[tt][nt][3] = fmaf(b1, sx[nt][1], fmaf(s1, acc[nt][3], tot[tt][nt][3]));
+      }
+    }
+  }
+  }
+
+  // ---- split-K: per-warp partial, the last split of a tile sums them in split order
+  constexpr int NV = 2 * NT * 4;
+  if (a.splits > 1) {
+    float* mine = a.partial + ((size_t)tile * a.splits + split) * NV * 32;
+#pragma unroll
+    for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) __stcg(mine + ((tt * NT + nt) * 4 + e) * 32 + lane, tot[tt][nt][e]);
+    __threadfence();
+    __syncwarp();
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(a.counters + tile, 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != (unsigned)(a.splits - 1)) return;
+    __threadfence();
+#pragma unroll
+    for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) tot[tt][nt][e] = 0.f;
+    // loads of four splits at a time are issued together; the adds stay in split order
+    for (int s0 = 0; s0 < a.splits; s0 += 4) {
+      float buf[4][NV];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        if (s0 + j < a.splits) {
+          const float* src = a.partial + ((size_t)tile * a.splits + s0 + j) * NV * 32;
+#pragma unroll
+          for (int v = 0; v < NV; v++) buf[j][v] = __ldcg(src + v * 32 + lane);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        if (s0 + j < a.splits) {
+#pragma unroll
+          for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+              for (int e = 0; e < 4; e++) tot[tt][nt][e] += buf[j][(tt * NT + nt) * 4 + e];
+        }
+      }
+    }
+    if (lane == 0) a.counters[tile] = 0u;
+  }
+
+  // ---- epilogue
+  const int rbase = tile * 32;
+  if constexpr (EPI == IM_EPI_SWIGLU || EPI == IM_EPI_GEGLU) {
+    const int nout = a.N >> 1;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int f = (rbase >> 1) + g + ((e >> 1) << 3);
+        const int m = nt * 8 + 2 * t + (e & 1);
+        if (m < a.M && f < nout) {
+          const float ga = round_bf(tot[0][nt][e]), uu = round_bf(tot[1][nt][e]);
+          float o;
+          if (EPI == IM_EPI_SWIGLU) {
+            const float sig = round_bf(1.0f / (1.0f + expf(-ga)));
+            o = round_bf(ga * sig) * uu;
+          } else {
+            const float inner = 0.7978845608028654f * (ga + 0.044715f * ga * ga * ga);
+            o = round_bf(0.5f * ga * (1.0f + tanhf(inner))) * uu;
+          }
+          a.y[(size_t)m * nout + f] = to_bf(o);
+        }
+      }
+  } else {
+    float sq[NT][2] = {};
+#pragma unroll
+    for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int r = rbase + tt * 16 + g + ((e >> 1) << 3);
+          const int m = nt * 8 + 2 * t + (e & 1);
+          if (m < a.M && r < a.N) {
+            const size_t o = (size_t)m * a.N + r;
+            const uint16_t h = EPI == IM_EPI_RESIDUAL ? to_bf(bf(a.res[o]) + round_bf(tot[tt][nt][e])) : to_bf(tot[tt][nt][e]);
+            a.y[o] = h;
+            const float hv = bf(h);
+            sq[nt][e & 1] = fmaf(hv, hv, sq[nt][e & 1]);
+          }
+        }
+    if (a.out_sq) {
+      // per activation row m: the sum over this tile's 32 rows, fixed order (lanes with the same t)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          float v = sq[nt][e];
+          v += __shfl_xor_sync(0xffffffffu, v, 4);
+          v += __shfl_xor_sync(0xffffffffu, v, 8);
+          v += __shfl_xor_sync(0xffffffffu, v, 16);
+          const int m = nt * 8 + 2 * t + e;
+          if (g == 0 && m < 32) a.out_sq[(size_t)tile * 32 + m] = m < a.M ? v : 0.f;
+        }
+    }
+  }
+}
+
+struct Q4Plan {
+  int tiles, ctas_x, splits, nt;
+  size_t workspace;
+};
+
+static Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
+  Q4Plan p;
+  p.tiles = (int)((N + 31) / 32);
+  p.ctas_x = (p.tiles + Q4_WARPS - 1) / Q4_WARPS;
+  p.nt = (int)((M + 7) / 8);
+  const int G = (int)(K / 64);
+  const int rmax = Q4_RMAX;
+  const int need = (G + rmax - 1) / rmax;                // shared-memory budget
+  int s = (g_q4_target_ctas + p.ctas_x - 1) / p.ctas_x;
+  if (s > g_q4_max_split) s = g_q4_max_split;
+  const int cap = G / 4 > 0 ? G / 4 : 1;                // at least 4 groups per CTA
+  if (s > cap) s = cap;
+  if (s < need) s = need;
+  if (g_q4_split_override > 0) s = g_q4_split_override < need ? need : (g_q4_split_override > G ? G : g_q4_split_override);
+  p.splits = s;
+  p.workspace = s > 1 ? Q4_COUNTER_BYTES + (size_t)p.tiles * s * 2 * 4 * 4 * 32 * sizeof(float) : 0;
+  return p;
+}
+
+template <int NT, int EPI>
+static void q4_launch(const Q4Plan& p, const Q4Args& a, cudaStream_t st) {
+  constexpr size_t smem = q4_smem_bytes(NT);
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    configured = true;
+  }
+  dim3 grid(p.ctas_x, p.splits);
+  qgemm_packed_kernel<NT, EPI><<<grid, Q4_THREADS, smem, st>>>(a);
+}
+
+template <int EPI>
+static void q4_dispatch(const Q4Plan& p, const Q4Args& a, cudaStream_t st) {
+  switch (p.nt) {
+    case 1: q4_launch<1, EPI>(p, a, st); break;
+    case 2: q4_launch<2, EPI>(p, a, st); break;
+    case 3: q4_launch<3, EPI>(p, a, st); break;
+    default: q4_launch<4, EPI>(p, a, st); break;
+  }
+}
+
+}  // namespace im
+
+using namespace im;
+
+extern "C" int im_qgemm_packed_tune(int split_override, int target_ctas, int max_split) {
+  IM_REQUIRE(split_override >= 0 && target_ctas >= 1 && max_split >= 1, IM_INVALID, "im_qgemm_packed_tune: bad value");
+  g_q4_split_override = split_override;
+  g_q4_target_ctas = target_ctas;
+  g_q4_max_split = max_split;
+  return IM_OK;
+}
+
+extern "C" size_t im_qgemm_packed_bytes(int64_t N, int64_t K) {
+  if (N < 1 || K < 64 || K % 64) return 0;
+  return (size_t)((N + 31) / 32) * (K / 64) * Q4_UNIT;
+}
+
+extern "C" int im_qgemm_pack_w4g64(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, int64_t N,
+                                   int64_t K, void* packed, void* stream) {
+  clear_error();
+  IM_REQUIRE(N >= 1 && K >= 64 && K % 64 == 0 && N <= (1 << 30) && K <= (1 << 24), IM_INVALID,
+             "im_qgemm_pack_w4g64: bad sizes");
+  IM_REQUIRE(w && scales && biases && packed, IM_INVALID, "im_qgemm_pack_w4g64: null pointer");
+  IM_REQUIRE(aligned(packed, 16) && aligned(w, 4), IM_INVALID, "im_qgemm_pack_w4g64: misaligned buffer");
+  const long long units = ((N + 31) / 32) * (K / 64);
+  IM_REQUIRE(units < (1ll << 31), IM_UNSUPPORTED, "im_qgemm_pack_w4g64: too many units");
+  q4_pack_kernel<<<(unsigned)units, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      w, scales, biases, (int)N, (int)K, reinterpret_cast<unsigned char*>(packed));
+  return check_launch("q4_pack_kernel");
+}
+
+extern "C" size_t im_qgemm_packed_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M < 1 || M > 32 || N < 1 || K < 64 || K % 64) return 0;
+  const Q4Plan p = q4_plan(M, N, K);
+  return p.tiles <= (int)(Q4_COUNTER_BYTES / 4) ? p.workspace : 0;
+}
+
+extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* y, const uint16_t* residual,
+                               int64_t M, int64_t N, int64_t K, int epilogue, const float* norm_sq,
+                               int64_t norm_parts, const uint16_t* norm_weight, float eps, int gemma_norm,
+                               float* out_sq, void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  IM_REQUIRE(M >= 0 && M <= 32 && N >= 1 && K >= 64 && K % 64 == 0 && N <= (1 << 30) && K <= (1 << 24),
+             IM_INVALID, "im_qgemm_packed: bad sizes M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (M == 0) return IM_OK;
+  IM_REQUIRE(packed && x && y, IM_INVALID, "im_qgemm_packed: null pointer");
+  IM_REQUIRE(aligned(packed, 16) && aligned(x, 16), IM_INVALID, "im_qgemm_packed: packed and x must be 16-byte aligned");
+  IM_REQUIRE(epilogue >= IM_EPI_STORE && epilogue <= IM_EPI_GEGLU, IM_INVALID, "im_qgemm_packed: bad epilogue");
+  IM_REQUIRE(epilogue != IM_EPI_RESIDUAL || residual, IM_INVALID, "im_qgemm_packed: residual epilogue needs residual");
+  const bool glu = epilogue == IM_EPI_SWIGLU || epilogue == IM_EPI_GEGLU;
+  IM_REQUIRE(!glu || N % 32 == 0, IM_INVALID, "im_qgemm_packed: gated epilogues need N % 32 == 0");
+  IM_REQUIRE(!glu || !out_sq, IM_INVALID, "im_qgemm_packed: sums of squares come from store/residual epilogues");
+  IM_REQUIRE(!norm_weight || (norm_sq && norm_parts >= 1 && aligned(norm_weight, 2)), IM_INVALID,
+             "im_qgemm_packed: the RMSNorm prologue needs norm_sq partials and a weight");
+  const Q4Plan p = q4_plan(M, N, K);
+  IM_REQUIRE(p.tiles <= (int)(Q4_COUNTER_BYTES / 4), IM_UNSUPPORTED, "im_qgemm_packed: N too large for split-K");
+  if (p.splits > 1)
+    IM_REQUIRE(workspace && aligned(workspace, 256) && workspace_bytes >= p.workspace, IM_INVALID,
+               "im_qgemm_packed: workspace of %zu bytes (256-aligned) needed, %zu given", p.workspace,
+               workspace_bytes);
+  Q4Args a;
+  a.wp = reinterpret_cast<const unsigned char*>(packed);
+  a.x = x;
+  a.y = y;
+  a.res = residual;
+  a.norm_sq = norm_sq;
+  a.norm_w = norm_weight;
+  a.out_sq = out_sq;
+  a.counters = reinterpret_cast<unsigned*>(workspace);
+  a.partial = workspace ? reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + Q4_COUNTER_BYTES) : nullptr;
+  a.eps = eps;
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.tiles = p.tiles;
+  a.splits = p.splits;
+  a.norm_parts = (int)norm_parts;
+  a.gemma_norm = gemma_norm;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  switch (epilogue) {
+    case IM_EPI_STORE: q4_dispatch<IM_EPI_STORE>(p, a, st); break;
+    case IM_EPI_RESIDUAL: q4_dispatch<IM_EPI_RESIDUAL>(p, a, st); break;
+    case IM_EPI_SWIGLU: q4_dispatch<IM_EPI_SWIGLU>(p, a, st); break;
+    default: q4_dispatch<IM_EPI_GEGLU>(p, a, st); break;
+  }
+  return check_launch("qgemm_packed_kernel");
+}

@@ -232,7 +232,7 @@ def qk_norm_rope_kv(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tenso
 
 def embed(tokens: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *,
           mult: float = 1.0, out: torch.Tensor | None = None, rows: int | None = None,
-          stride: int = 1) -> torch.Tensor:
+          stride: int = 1, out_sq: torch.Tensor | None = None) -> torch.Tensor:
     """Rows tokens[0], tokens[stride], ... of the 4-bit table, dequantised (bf16 [rows, H])."""
     if tokens.dtype != torch.int32 or tokens.device.type != "cuda":
         raise TypeError("tokens must be an int32 CUDA tensor")
@@ -240,7 +240,7 @@ def embed(tokens: torch.Tensor, wq: torch.Tensor, scales: torch.Tensor, biases: 
     m = tokens.numel() if rows is None else rows
     out = torch.empty((m, h), dtype=torch.bfloat16, device=tokens.device) if out is None else out
     _lib.call("im_embed_w4g64", tokens.data_ptr(), stride, wq.data_ptr(), scales.data_ptr(), biases.data_ptr(), m,
-              v, h, float(mult), out.data_ptr(), _stream(tokens.device))
+              v, h, float(mult), out.data_ptr(), _ptr_or_none(out_sq), _stream(tokens.device))
     return out
 
 
@@ -326,4 +326,49 @@ def accept_stochastic(target_logits: torch.Tensor, draft_logits: torch.Tensor, d
 def philox(seed: int, offset: int, stream_id: int, n: int, device) -> torch.Tensor:
     out = torch.empty((n, 4), dtype=torch.int32, device=device)
     _lib.call("im_philox4x32_10", int(seed), int(offset), int(stream_id), int(n), out.data_ptr(), _stream(device))
+    return out
+
+
+# ---- packed weights (the engine's resident format) ------------------------------------------------------
+class Packed:
+    """A 4-bit projection repacked into MMA-fragment order (im_qgemm_pack_w4g64): n rows, k inputs."""
+
+    def __init__(self, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor):
+        _check(w, "w", (torch.int32, torch.uint32))
+        self.n, self.k = int(w.shape[0]), int(w.shape[1]) * 8
+        nbytes = int(_lib.load().im_qgemm_packed_bytes(self.n, self.k))
+        self.data = torch.empty(nbytes, dtype=torch.uint8, device=w.device)
+        _lib.call("im_qgemm_pack_w4g64", w.data_ptr(), scales.data_ptr(), biases.data_ptr(), self.n, self.k,
+                  self.data.data_ptr(), _stream(w.device))
+
+    @property
+    def tiles(self) -> int:
+        return (self.n + 31) // 32
+
+
+def qgemm_packed_workspace_bytes(m: int, n: int, k: int) -> int:
+    return int(_lib.load().im_qgemm_packed_workspace_bytes(m, n, k))
+
+
+def qgemm_packed(x: torch.Tensor, p: Packed, *, epilogue: str = "store", residual: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None, rows: int | None = None, norm_sq: torch.Tensor | None = None,
+                 norm_parts: int = 0, norm_weight: torch.Tensor | None = None, eps: float = 1e-6,
+                 gemma_norm: bool = False, out_sq: torch.Tensor | None = None,
+                 ws: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x . W^T over packed weights, with an optional fused RMSNorm prologue (norm_sq/norm_weight) and
+    per-tile sums of squares of the output (out_sq)."""
+    device = x.device
+    if x.dtype != torch.bfloat16 or device.type != "cuda" or not x.is_contiguous():
+        raise TypeError("x must be a contiguous bf16 CUDA tensor")
+    k = x.shape[-1]
+    if k != p.k:
+        raise ValueError(f"x has K={k}, the weights {p.k}")
+    m = x.numel() // k if rows is None else rows
+    epi = _EPILOGUES[epilogue]
+    n_out = p.n // 2 if epi in (_lib.EPI_SWIGLU, _lib.EPI_GEGLU) else p.n
+    out = torch.empty((m, n_out), dtype=torch.bfloat16, device=device) if out is None else out
+    ws_ptr, ws_bytes = _scratch(ws, device, qgemm_packed_workspace_bytes(m, p.n, p.k), "qgemm_packed")
+    _lib.call("im_qgemm_packed", p.data.data_ptr(), x.data_ptr(), out.data_ptr(), _ptr_or_none(residual), m, p.n, p.k,
+              epi, _ptr_or_none(norm_sq), norm_parts, _ptr_or_none(norm_weight), float(eps), int(gemma_norm),
+              _ptr_or_none(out_sq), ws_ptr, ws_bytes, _stream(device))
     return out

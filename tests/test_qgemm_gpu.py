@@ -226,3 +226,61 @@ def test_tma_epilogues_equal_the_mma_kernel_epilogue_math(cuda, epi):
         want = (om.silu_mul if epi == "swiglu" else om.gelu_mul)(bf16.from_f32(gate), bf16.from_f32(up))
         diff = np.abs(bf16.to_f32(got) - bf16.to_f32(want))
         assert np.all(diff <= 2 * (np.abs(bf16.to_f32(want)) * 2.0 ** -7 + 1e-30))
+
+
+# ---- v4: packed weights --------------------------------------------------------------------------------------
+def packed_case(cuda, n, k, m, seed):
+    wq, s, b, x = case(n, k, m, seed=seed)
+    w_t, s_t, b_t, x_t = to_device(wq, s, b, x, cuda)
+    return wq, s, b, x, kernels.Packed(w_t, s_t, b_t), x_t
+
+
+@pytest.mark.parametrize("n,k,m", [(15360, 3840, 1), (15360, 3840, 5), (6144, 2560, 5), (2560, 9728, 5),
+                                   (151936, 2560, 5), (1024, 1024, 2), (96, 256, 13), (50, 768, 32), (4104, 2048, 8)])
+def test_packed_kernel_matches_oracle(cuda, n, k, m):
+    wq, s, b, x, p, x_t = packed_case(cuda, n, k, m, n + 5 * k + m)
+    got = torch_to_bf16_bits(kernels.qgemm_packed(x_t, p))
+    mx, mean = rel_errors(got, qmv.qmv(wq, s, b, x, vpt=8))
+    assert mx <= MAX_REL and mean <= MEAN_REL, (mx, mean)
+
+
+def test_packed_row_invariance(cuda):
+    wq, s, b, x, p, x_t = packed_case(cuda, 6144, 2560, 32, 77)
+    full = {mm: torch_to_bf16_bits(kernels.qgemm_packed(x_t[:mm].contiguous(), p)) for mm in (1, 5, 8, 13, 32)}
+    for mm, y in full.items():
+        assert np.array_equal(y, full[32][:mm]), mm
+
+
+def test_packed_fused_rmsnorm_and_sums_of_squares(cuda):
+    """residual epilogue with out_sq, then a GEMM whose prologue normalises from those sums == explicit RMSNorm."""
+    from oracle import model as om
+
+    rng = np.random.default_rng(5)
+    m, h = 5, 2560
+    wq, s, b, x, p_o, x_t = packed_case(cuda, h, 1024, m, 91)       # an "o_proj": K=1024 -> N=h
+    res = torch.randn(m, h, device=cuda).to(torch.bfloat16)
+    sq = torch.zeros((p_o.tiles, 32), dtype=torch.float32, device=cuda)
+    h_new = kernels.qgemm_packed(x_t, p_o, epilogue="residual", residual=res, out_sq=sq)
+    hb = torch_to_bf16_bits(h_new)
+    want_sq = (bf16.to_f32(hb).astype(np.float64) ** 2).sum(axis=1)
+    assert np.allclose(sq.sum(0).cpu().numpy()[:m], want_sq, rtol=1e-5)
+    wq2, s2, b2, _, p_qkv, _ = packed_case(cuda, 3072, h, m, 92)
+    nw = bf16.from_f32(rng.normal(1, 0.1, h).astype(np.float32))
+    nw_t = torch.from_numpy(nw.view(np.int16)).view(torch.bfloat16).to(cuda)
+    fused = torch_to_bf16_bits(kernels.qgemm_packed(h_new, p_qkv, norm_sq=sq, norm_parts=p_o.tiles, norm_weight=nw_t))
+    normed = om.rmsnorm(hb, nw, 1e-6)
+    mx, mean = rel_errors(fused, qmv.qmv(wq2, s2, b2, normed, vpt=8))
+    assert mx <= MAX_REL and mean <= MEAN_REL, (mx, mean)
+
+
+@pytest.mark.parametrize("epi", ["swiglu", "geglu"])
+def test_packed_gated_epilogues(cuda, epi):
+    from oracle import model as om
+
+    wq, s, b, x, p, x_t = packed_case(cuda, 2048, 1024, 5, 93)
+    plain = torch_to_bf16_bits(kernels.qgemm_packed(x_t, p))
+    got = torch_to_bf16_bits(kernels.qgemm_packed(x_t, p, epilogue=epi))
+    g = plain.reshape(5, -1, 2, 16)
+    want = (om.silu_mul if epi == "swiglu" else om.gelu_mul)(g[:, :, 0, :].reshape(5, -1), g[:, :, 1, :].reshape(5, -1))
+    diff = np.abs(bf16.to_f32(got) - bf16.to_f32(want))
+    assert np.all(diff <= 2 * (np.abs(bf16.to_f32(want)) * 2.0 ** -7 + 1e-30))
