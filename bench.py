@@ -202,10 +202,11 @@ def run_reference(args, world: int, rank: int) -> None:
 
 # ---- GPU side --------------------------------------------------------------------------------------------
 def qgemm_roofline(target, peak_gbs: float, reps: int = 20) -> dict:
-    """The dominant kernel: every qGEMM of one verify pass (M = k+1 = 5 rows: 36 x [qkv, o, gate_up, down] and
-    the head), captured once as a graph and replayed; CUDA events on the launching stream give the mean
-    launch duration and the achieved bandwidth over the algorithmic bytes (4-bit weights at 0.5625 B per
-    weight + activations in + results out)."""
+    """The dominant kernel: every packed qGEMM of one verify pass (M = k+1 = 5 rows: 36 x [qkv, o, gate_up,
+    down] and the head), launched as the forward launches them (RMSNorm prologues on qkv / gate_up / head,
+    residual + sums-of-squares epilogues on o / down), captured once as a graph and replayed; CUDA events on
+    the launching stream give the mean launch duration and the achieved bandwidth over the algorithmic bytes
+    (4-bit weights at 0.5625 B per weight + activations in + results out)."""
     import torch
 
     from ironmule_b200 import kernels
@@ -213,28 +214,31 @@ def qgemm_roofline(target, peak_gbs: float, reps: int = 20) -> dict:
     m = K_DRAFTS + 1
     c = target.cfg
     x = torch.randn((m, max(c.inter, c.heads * c.head_dim, c.hidden)), device=target.device).to(torch.bfloat16)
-    res = torch.zeros((m, c.hidden), dtype=torch.bfloat16, device=target.device)
+    res = torch.randn((m, c.hidden), device=target.device).to(torch.bfloat16)
     out = torch.zeros((m, c.vocab), dtype=torch.bfloat16, device=target.device)
+    sq = torch.ones((target.h_tiles, 32), dtype=torch.float32, device=target.device)
     calls, total_bytes = [], 0
 
-    def add(lin, epi):
+    def add(lin, epi, norm):
         nonlocal total_bytes
         n_out = lin.n // 2 if epi == "swiglu" else lin.n
-        calls.append((lin, epi))
+        calls.append((lin, epi, norm))
         total_bytes += lin.n * lin.k * 9 // 16 + m * lin.k * 2 + m * n_out * 2 + (m * lin.n * 2 if epi == "residual" else 0)
 
     for layer in target.layers:
-        add(layer.qkv, "store")
-        add(layer.o, "residual")
-        add(layer.gate_up, "swiglu")
-        add(layer.down, "residual")
-    add(target.embed, "store")
+        add(layer.qkv, "store", layer.in_norm)
+        add(layer.o, "residual", None)
+        add(layer.gate_up, "swiglu", layer.post_norm)
+        add(layer.down, "residual", None)
+    add(target.embed, "store", target.final_norm)
 
     def run():
-        for lin, epi in calls:
-            xin = x.view(-1)[: m * lin.k].view(m, lin.k)
-            kernels.qgemm(xin, lin.w, lin.s, lin.b, epilogue=epi, residual=res if epi == "residual" else None,
-                          out=res if epi == "residual" else out, ws=target.ws_gemm)
+        for lin, epi, norm in calls:
+            xin = res if norm is not None else x.view(-1)[: m * lin.k].view(m, lin.k)
+            kernels.qgemm_packed(xin, lin.p, epilogue=epi, residual=res if epi == "residual" else None,
+                                 out=res if epi == "residual" else out, ws=target.ws_gemm,
+                                 norm_sq=sq if norm is not None else None, norm_parts=target.h_tiles,
+                                 norm_weight=norm, eps=c.eps, out_sq=sq if epi == "residual" else None)
 
     run()
     torch.cuda.synchronize()
@@ -259,7 +263,7 @@ def qgemm_roofline(target, peak_gbs: float, reps: int = 20) -> dict:
         traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch_mean")
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
             "frac": round(achieved / peak_gbs, 4), "traffic": traffic,
-            "kernel": "qgemm_mma_kernel (all 145 qGEMMs of one Qwen3-4B verify pass, M=5)",
+            "kernel": "qgemm_packed_kernel (all 145 qGEMMs of one Qwen3-4B verify pass, M=5)",
             "launches": launches, "us_per_launch": round(sec / launches * 1e6, 2),
             "algorithmic_bytes_per_launch": total_bytes // launches, "pass_us": round(sec * 1e6, 1)}
 
@@ -378,15 +382,15 @@ def run_verify_step(args, world: int, rank: int, local: int) -> None:
     torch.cuda.set_device(device)
     pk = peaks()
     gen = torch.Generator(device=device).manual_seed(0)
-    copies = [kernels.quantize((torch.randn((15360, 3840), generator=gen, device=device) * 0.02).to(torch.bfloat16))
-              for _ in range(8)]
+    copies = [kernels.Packed(*kernels.quantize((torch.randn((15360, 3840), generator=gen, device=device) * 0.02)
+                                               .to(torch.bfloat16))) for _ in range(8)]
     x = torch.randn((5, 3840), generator=gen, device=device).to(torch.bfloat16)
     y = torch.empty((5, 15360), dtype=torch.bfloat16, device=device)
     reps = -(-151936 // 15360)
     noise = (torch.randn((5, reps * 15360), generator=gen, device=device) * 1e-3).to(torch.bfloat16)
     logits = torch.empty((5, 151936), dtype=torch.bfloat16, device=device)
     drafts = torch.randint(0, 151936, (1, 4), generator=gen, device=device, dtype=torch.int32)
-    ws = kernels.workspace(kernels.qgemm_workspace_bytes(5, 15360, 3840), device)
+    ws = kernels.workspace(kernels.qgemm_packed_workspace_bytes(5, 15360, 3840), device)
     tokens = torch.empty((1, 5), dtype=torch.int32, device=device)
     count = torch.empty((1,), dtype=torch.int32, device=device)
     stream = torch.cuda.current_stream(device)
@@ -394,8 +398,7 @@ def run_verify_step(args, world: int, rank: int, local: int) -> None:
 
     def gemms(n):
         for i in range(n):
-            wq, s, b = copies[i % 8]
-            kernels.qgemm(x, wq, s, b, out=y, ws=ws)
+            kernels.qgemm_packed(x, copies[i % 8], out=y, ws=ws)
 
     gemms(3)
     g = torch.cuda.CUDAGraph()

@@ -47,6 +47,12 @@ enum {
 
 /* The ABI revision this library implements (IM_ABI_VERSION). */
 int im_abi_version(void);
+/* Decode-path kernels (the packed qGEMM, embedding, q/k norm + RoPE, attention, argmax/verify, sampling and
+ * the round bookkeeping) are launched with programmatic dependent launch: a kernel's CTAs may start while the
+ * previous kernel on the stream runs, load weights, and wait for the previous kernel's results before reading
+ * activations. Results are the same either way. on = 0 turns this off process-wide; returns the previous
+ * setting. */
+int im_set_launch_overlap(int on);
 
 /* The message of the last non-zero return on this thread ("" when the last call succeeded). */
 const char* im_last_error(void);

@@ -22,4 +22,10 @@ void clear_error() { g_error[0] = '\0'; }
 
 extern "C" int im_abi_version(void) { return IM_ABI_VERSION; }
 
+extern "C" int im_set_launch_overlap(int on) {
+  const int was = im::launch_overlap() ? 1 : 0;
+  im::launch_overlap() = on != 0;
+  return was;
+}
+
 extern "C" const char* im_last_error(void) { return im::g_error; }

@@ -66,6 +66,8 @@ argmax_kernel(const uint16_t* __restrict__ logits, int rows, int V, long long ld
               int32_t* argmax, int out_stride, float* conf, AmWork work, int B, int k,
               const int32_t* __restrict__ drafts, int drafts_ld,
               int32_t* out_tokens, int32_t* out_count) {
+  pdl_wait();
+  pdl_trigger();
   const int chunk = blockIdx.x, row = blockIdx.y;
   const int v0 = chunk * chunk_len;
   const int v1 = min(V, v0 + chunk_len);
@@ -172,10 +174,9 @@ static int am_launch(const uint16_t* logits, int64_t rows, int64_t V, int64_t ld
   AmWork work{reinterpret_cast<unsigned*>(workspace),
               reinterpret_cast<RowStat*>(reinterpret_cast<char*>(workspace) + 256)};
   dim3 grid(chunks, (unsigned)rows);
-  argmax_kernel<<<grid, AM_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      logits, (int)rows, (int)V, (long long)ld, chunks, len, argmax, (int)out_stride, conf, work, B, k, drafts,
-      (int)drafts_ld, out_tokens, out_count);
-  return check_launch("argmax_kernel");
+  return launch("argmax_kernel", argmax_kernel, grid, dim3(AM_THREADS), 0, reinterpret_cast<cudaStream_t>(stream),
+                logits, (int)rows, (int)V, (long long)ld, chunks, len, argmax, (int)out_stride, conf, work, B, k,
+                drafts, (int)drafts_ld, out_tokens, out_count);
 }
 
 }  // namespace im

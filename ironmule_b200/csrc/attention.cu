@@ -63,6 +63,8 @@ __global__ void __launch_bounds__(AT_THREADS)
 attn_kernel(AttnArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   AttnSmem<D, NQ>& sm = *reinterpret_cast<AttnSmem<D, NQ>*>(smem_raw);
+  pdl_wait();
+  pdl_trigger();
   const int split = blockIdx.x, kvh = blockIdx.y;
   const int b = blockIdx.z / a.qblocks, qb = blockIdx.z % a.qblocks;
   const int tid = threadIdx.x;
@@ -276,8 +278,7 @@ static int launch_attn(const AttnArgs& args, int B, cudaStream_t st) {
     configured = true;
   }
   dim3 grid(args.nsplit, args.Hkv, B * args.qblocks);
-  attn_kernel<D, NQ><<<grid, AT_THREADS, smem, st>>>(args);
-  return check_launch("attn_kernel");
+  return launch("attn_kernel", attn_kernel<D, NQ>, grid, dim3(AT_THREADS), smem, st, args);
 }
 
 static void attn_geometry(int64_t rows_per_seq, int64_t G, int* nq, int* qblocks) {

@@ -33,6 +33,43 @@ inline int check_launch(const char* what) {
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// ---- programmatic dependent launch --------------------------------------------------------------
+// Decode-path kernels are launched with programmatic stream serialisation: a kernel's CTAs may become
+// resident while the previous kernel on the stream is still running. Every such kernel calls pdl_wait()
+// before it reads anything an earlier kernel wrote and before its first global write (what comes before
+// may only read weights, which no kernel on the decode path writes), and pdl_trigger() after it, which
+// lets the next kernel's CTAs launch. pdl_wait() returns once the previous grid has completed and its
+// writes are visible; for a kernel launched without the attribute it returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Process-wide switch (im_set_launch_overlap); on by default.
+inline bool& launch_overlap() {
+  static bool on = true;
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline int launch(const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                  Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = launch_overlap() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return IM_CUDA_ERROR;
+  }
+  return IM_OK;
+}
+
 // ---- bf16 as raw 16-bit patterns --------------------------------------------------------------
 // Values cross the ABI as uint16_t bit patterns; arithmetic is float32 with one rounding to bf16
 // (nearest even) wherever the reference rounds.

@@ -31,6 +31,8 @@ __global__ void __launch_bounds__(LN_THREADS)
 rmsnorm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, uint16_t* __restrict__ out, int H,
                long long ldx, float eps, int gemma) {
   __shared__ float sh[LN_THREADS / 32];
+  pdl_wait();
+  pdl_trigger();
   const uint16_t* xr = x + (size_t)blockIdx.x * ldx;
   float ss = 0.f;
   for (int i = threadIdx.x; i < H; i += LN_THREADS) {
@@ -61,6 +63,8 @@ qk_rope_kv_kernel(const uint16_t* __restrict__ qkv, const uint16_t* __restrict__
                   uint16_t* __restrict__ vc) {
   __shared__ float sh[32];
   __shared__ float xn[D];
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   const int stride = (Hq + 2 * Hkv) * D;
   const bool is_q = h < Hq;
@@ -104,6 +108,8 @@ __global__ void embed_kernel(const int* __restrict__ tokens, int tstride, const 
                              const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, int H, int V,
                              float mult, uint16_t* __restrict__ out, float* __restrict__ out_sq) {
   __shared__ float sh[4];
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   int tok = tokens[(size_t)m * tstride];
   tok = tok < 0 ? 0 : (tok >= V ? V - 1 : tok);
@@ -143,9 +149,8 @@ extern "C" int im_rmsnorm(const uint16_t* x, int64_t ldx, const uint16_t* weight
   if (M == 0) return IM_OK;
   IM_REQUIRE(x && weight && out, IM_INVALID, "im_rmsnorm: null pointer");
   IM_REQUIRE(M < (1ll << 31), IM_UNSUPPORTED, "im_rmsnorm: too many rows");
-  rmsnorm_kernel<<<(unsigned)M, LN_THREADS, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, weight, out, (int)H, (long long)ldx, eps, gemma_style);
-  return check_launch("rmsnorm_kernel");
+  return launch("rmsnorm_kernel", rmsnorm_kernel, dim3((unsigned)M), dim3(LN_THREADS), 0,
+                reinterpret_cast<cudaStream_t>(stream), x, weight, out, (int)H, (long long)ldx, eps, gemma_style);
 }
 
 extern "C" int im_qk_norm_rope_kv(const uint16_t* qkv, const uint16_t* q_norm, const uint16_t* k_norm,
@@ -164,14 +169,12 @@ extern "C" int im_qk_norm_rope_kv(const uint16_t* qkv, const uint16_t* q_norm, c
   dim3 grid((unsigned)M, (unsigned)(Hq + Hkv));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (D == 128)
-    qk_rope_kv_kernel<128><<<grid, 128, 0, st>>>(qkv, q_norm, k_norm, inv_freq, row_pos, row_slot, row_seq, page_table,
-                                                 (int)max_pages, (int)Hq, (int)Hkv, eps, gemma_style, q_out, k_cache,
-                                                 v_cache);
-  else
-    qk_rope_kv_kernel<256><<<grid, 256, 0, st>>>(qkv, q_norm, k_norm, inv_freq, row_pos, row_slot, row_seq, page_table,
-                                                 (int)max_pages, (int)Hq, (int)Hkv, eps, gemma_style, q_out, k_cache,
-                                                 v_cache);
-  return check_launch("qk_rope_kv_kernel");
+    return launch("qk_rope_kv_kernel", qk_rope_kv_kernel<128>, grid, dim3(128), 0, st, qkv, q_norm, k_norm, inv_freq,
+                  row_pos, row_slot, row_seq, page_table, (int)max_pages, (int)Hq, (int)Hkv, eps, gemma_style, q_out,
+                  k_cache, v_cache);
+  return launch("qk_rope_kv_kernel", qk_rope_kv_kernel<256>, grid, dim3(256), 0, st, qkv, q_norm, k_norm, inv_freq,
+                row_pos, row_slot, row_seq, page_table, (int)max_pages, (int)Hq, (int)Hkv, eps, gemma_style, q_out,
+                k_cache, v_cache);
 }
 
 extern "C" int im_embed_w4g64(const int32_t* tokens, int64_t tokens_stride, const uint32_t* wq,
@@ -183,7 +186,6 @@ extern "C" int im_embed_w4g64(const int32_t* tokens, int64_t tokens_stride, cons
   if (M == 0) return IM_OK;
   IM_REQUIRE(tokens && wq && scales && biases && out, IM_INVALID, "im_embed_w4g64: null pointer");
   IM_REQUIRE(!out_sq || M <= 32, IM_INVALID, "im_embed_w4g64: row sums of squares cover at most 32 rows");
-  embed_kernel<<<(unsigned)M, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      tokens, (int)tokens_stride, wq, scales, biases, (int)H, (int)V, mult, out, out_sq);
-  return check_launch("embed_kernel");
+  return launch("embed_kernel", embed_kernel, dim3((unsigned)M), dim3(128), 0, reinterpret_cast<cudaStream_t>(stream),
+                tokens, (int)tokens_stride, wq, scales, biases, (int)H, (int)V, mult, out, out_sq);
 }

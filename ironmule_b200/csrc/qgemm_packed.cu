@@ -28,7 +28,7 @@ constexpr size_t Q4_COUNTER_BYTES = 65536;
 constexpr int Q4_DEPTH = 3;               // units in flight per warp
 static int g_q4_split_override = 0;       // sweep hook (0 = automatic)
 static int g_q4_target_ctas = 148 * 4;    // split policy: aim for this many CTAs
-static int g_q4_max_split = 8;
+static int g_q4_max_split = 64;
 constexpr uint32_t Q4_128 = 0x43004300u;
 
 __device__ __forceinline__ void q4_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -48,6 +48,11 @@ __device__ __forceinline__ void q4_codes(uint32_t u, uint32_t* p) {
 }
 
 __device__ __forceinline__ uint4 q4_ld_stream(const void* p) { return ldg_stream_u4(p); }
+// Asks the TMA unit to bring [p, p + bytes) into L2 (p 16-byte aligned, bytes a multiple of 16); no data
+// reaches the CTA and nothing waits on it.
+__device__ __forceinline__ void q4_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 // ---- repack ---------------------------------------------------------------------------------------------
 __global__ void q4_pack_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ sc,
@@ -127,6 +132,28 @@ qgemm_packed_kernel(Q4Args a) {
   const int cg1 = (int)(((long long)G * (split + 1)) / a.splits);
   const int ng = cg1 - cg0;
   const int tile = blockIdx.x * Q4_WARPS + warp;
+  const bool live = tile < a.tiles;
+
+  // ---- before the dependency wait: this warp's weights (which no earlier kernel writes). Its slice is ng
+  // consecutive 1152-byte units; the first Q4_DEPTH go to registers, the rest are prefetched into L2.
+  const unsigned char* up = a.wp + ((size_t)(live ? tile : 0) * G + cg0) * Q4_UNIT;
+  uint4 rc0[Q4_DEPTH], rc1[Q4_DEPTH], rsb[Q4_DEPTH];
+  if (live) {
+    if (lane == 0)
+      for (int u = Q4_DEPTH; u < ng; u += 16)  // pieces of at most 16 units (18 KB)
+        q4_prefetch_l2(up + (size_t)u * Q4_UNIT, (uint32_t)min(16, ng - u) * Q4_UNIT);
+#pragma unroll
+    for (int d = 0; d < Q4_DEPTH; d++) {
+      if (d < ng) {
+        const unsigned char* nu = up + (size_t)d * Q4_UNIT;
+        rc0[d] = q4_ld_stream(nu + lane * 32);
+        rc1[d] = q4_ld_stream(nu + lane * 32 + 16);
+        rsb[d] = __ldg(reinterpret_cast<const uint4*>(nu + 1024 + g * 16));
+      }
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
 
   // ---- prologue: RMSNorm factors, then the activation fragments and group sums of [cg0, cg1)
   if (a.norm_w) {
@@ -190,10 +217,9 @@ qgemm_packed_kernel(Q4Args a) {
     if (tq == 0) sxs[gl][m] = part;
   }
   __syncthreads();
-  if (tile >= a.tiles) return;
+  if (!live) return;
 
   // ---- main loop: this warp's tile over [cg0, cg1), one 1152-byte unit per group, Q4_DEPTH units in flight
-  const unsigned char* up = a.wp + ((size_t)tile * G + cg0) * Q4_UNIT;
   float tot[2][NT][4];
 #pragma unroll
   for (int tt = 0; tt < 2; tt++)
@@ -201,17 +227,7 @@ qgemm_packed_kernel(Q4Args a) {
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
       for (int e = 0; e < 4; e++) tot[tt][nt][e] = 0.f;
-  // a ring of Q4_DEPTH units in flight per warp (two 16-byte code loads + one scale/bias load per lane each)
-  uint4 rc0[Q4_DEPTH], rc1[Q4_DEPTH], rsb[Q4_DEPTH];
-#pragma unroll
-  for (int d = 0; d < Q4_DEPTH; d++) {
-    if (d < ng) {
-      const unsigned char* nu = up + (size_t)d * Q4_UNIT;
-      rc0[d] = q4_ld_stream(nu + lane * 32);
-      rc1[d] = q4_ld_stream(nu + lane * 32 + 16);
-      rsb[d] = __ldg(reinterpret_cast<const uint4*>(nu + 1024 + g * 16));
-    }
-  }
+  // the register ring: Q4_DEPTH units in flight per warp (two 16-byte code loads + one scale/bias load per lane)
 #pragma unroll 1
   for (int gl0 = 0; gl0 < ng; gl0 += Q4_DEPTH) {
 #pragma unroll
@@ -402,7 +418,7 @@ static Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
 }
 
 template <int NT, int EPI>
-static void q4_launch(const Q4Plan& p, const Q4Args& a, cudaStream_t st) {
+static int q4_launch(const Q4Plan& p, const Q4Args& a, cudaStream_t st) {
   constexpr size_t smem = q4_smem_bytes(NT);
   static bool configured = false;
   if (!configured) {
@@ -410,16 +426,16 @@ static void q4_launch(const Q4Plan& p, const Q4Args& a, cudaStream_t st) {
     configured = true;
   }
   dim3 grid(p.ctas_x, p.splits);
-  qgemm_packed_kernel<NT, EPI><<<grid, Q4_THREADS, smem, st>>>(a);
+  return launch("qgemm_packed_kernel", qgemm_packed_kernel<NT, EPI>, grid, dim3(Q4_THREADS), smem, st, a);
 }
 
 template <int EPI>
-static void q4_dispatch(const Q4Plan& p, const Q4Args& a, cudaStream_t st) {
+static int q4_dispatch(const Q4Plan& p, const Q4Args& a, cudaStream_t st) {
   switch (p.nt) {
-    case 1: q4_launch<1, EPI>(p, a, st); break;
-    case 2: q4_launch<2, EPI>(p, a, st); break;
-    case 3: q4_launch<3, EPI>(p, a, st); break;
-    default: q4_launch<4, EPI>(p, a, st); break;
+    case 1: return q4_launch<1, EPI>(p, a, st);
+    case 2: return q4_launch<2, EPI>(p, a, st);
+    case 3: return q4_launch<3, EPI>(p, a, st);
+    default: return q4_launch<4, EPI>(p, a, st);
   }
 }
 
@@ -503,10 +519,9 @@ extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* 
   a.gemma_norm = gemma_norm;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (epilogue) {
-    case IM_EPI_STORE: q4_dispatch<IM_EPI_STORE>(p, a, st); break;
-    case IM_EPI_RESIDUAL: q4_dispatch<IM_EPI_RESIDUAL>(p, a, st); break;
-    case IM_EPI_SWIGLU: q4_dispatch<IM_EPI_SWIGLU>(p, a, st); break;
-    default: q4_dispatch<IM_EPI_GEGLU>(p, a, st); break;
+    case IM_EPI_STORE: return q4_dispatch<IM_EPI_STORE>(p, a, st);
+    case IM_EPI_RESIDUAL: return q4_dispatch<IM_EPI_RESIDUAL>(p, a, st);
+    case IM_EPI_SWIGLU: return q4_dispatch<IM_EPI_SWIGLU>(p, a, st);
+    default: return q4_dispatch<IM_EPI_GEGLU>(p, a, st);
   }
-  return check_launch("qgemm_packed_kernel");
 }

@@ -96,6 +96,8 @@ row_dist_kernel(const uint16_t* __restrict__ logits, int V, long long ld, float 
   __shared__ float sh[32];
   __shared__ float hist[256];
   __shared__ uint32_t sel;
+  pdl_wait();
+  pdl_trigger();
   const uint16_t* lp = logits + (size_t)blockIdx.x * ld;
   const float inv_t = 1.0f / temperature;
   float mx = -INFINITY;
@@ -260,6 +262,8 @@ accept_stochastic_kernel(const uint16_t* __restrict__ tl, const uint16_t* __rest
                          unsigned long long offset0, const unsigned long long* __restrict__ offset_dev,
                          int32_t* __restrict__ out_tokens, int32_t* __restrict__ out_count,
                          float* __restrict__ ratios) {
+  pdl_wait();
+  pdl_trigger();
   const unsigned long long offset = offset0 + (offset_dev ? *offset_dev : 0ull);
   const int B = gridDim.x;
   __shared__ float scan[SM_THREADS + 33];
@@ -312,6 +316,8 @@ __global__ void __launch_bounds__(SM_THREADS)
 sample_kernel(const uint16_t* __restrict__ logits, int V, long long ld, const RowDist* __restrict__ dist,
               const uint32_t* __restrict__ streams, uint32_t draw, unsigned long long seed, unsigned long long offset0,
               const unsigned long long* __restrict__ offset_dev, int32_t* __restrict__ out, int out_stride) {
+  pdl_wait();
+  pdl_trigger();
   const unsigned long long offset = offset0 + (offset_dev ? *offset_dev : 0ull);
   __shared__ float scan[SM_THREADS + 33];
   __shared__ int pick;
@@ -364,13 +370,12 @@ extern "C" int im_sample_rows(const uint16_t* logits, int64_t rows, int64_t V, i
              IM_INVALID, "im_sample_rows: null output or short workspace");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   RowDist* dist = reinterpret_cast<RowDist*>(workspace);
-  row_dist_kernel<<<(unsigned)rows, SM_THREADS, 0, st>>>(logits, (int)V, ld, temperature, top_p, dist);
-  rc = check_launch("row_dist_kernel");
+  rc = launch("row_dist_kernel", row_dist_kernel, dim3((unsigned)rows), dim3(SM_THREADS), 0, st, logits, (int)V,
+              (long long)ld, temperature, top_p, dist);
   if (rc) return rc;
-  sample_kernel<<<(unsigned)rows, SM_THREADS, 0, st>>>(logits, (int)V, ld, dist, streams, draw, seed, offset,
-                                                      reinterpret_cast<const unsigned long long*>(offset_dev), out,
-                                                      (int)out_stride);
-  return check_launch("sample_kernel");
+  return launch("sample_kernel", sample_kernel, dim3((unsigned)rows), dim3(SM_THREADS), 0, st, logits, (int)V,
+                (long long)ld, (const RowDist*)dist, streams, draw, (unsigned long long)seed, (unsigned long long)offset,
+                reinterpret_cast<const unsigned long long*>(offset_dev), out, (int)out_stride);
 }
 
 extern "C" int im_accept_stochastic(const uint16_t* target_logits, const uint16_t* draft_logits, int64_t B,
@@ -390,17 +395,16 @@ extern "C" int im_accept_stochastic(const uint16_t* target_logits, const uint16_
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   RowDist* td = reinterpret_cast<RowDist*>(workspace);
   RowDist* dd = td + B * (k + 1);
-  row_dist_kernel<<<(unsigned)(B * (k + 1)), SM_THREADS, 0, st>>>(target_logits, (int)V, ld, temperature, top_p, td);
-  rc = check_launch("row_dist_kernel");
+  rc = launch("row_dist_kernel", row_dist_kernel, dim3((unsigned)(B * (k + 1))), dim3(SM_THREADS), 0, st,
+              target_logits, (int)V, (long long)ld, temperature, top_p, td);
   if (rc) return rc;
-  row_dist_kernel<<<(unsigned)(B * k), SM_THREADS, 0, st>>>(draft_logits, (int)V, ld, temperature, top_p, dd);
-  rc = check_launch("row_dist_kernel");
+  rc = launch("row_dist_kernel", row_dist_kernel, dim3((unsigned)(B * k)), dim3(SM_THREADS), 0, st, draft_logits,
+              (int)V, (long long)ld, temperature, top_p, dd);
   if (rc) return rc;
-  accept_stochastic_kernel<<<(unsigned)B, SM_THREADS, 0, st>>>(target_logits, draft_logits, (int)V, ld, td, dd, drafts,
-                                                              (int)drafts_ld, (int)k, seed, offset,
-                                                              reinterpret_cast<const unsigned long long*>(offset_dev),
-                                                              out_tokens, out_count, ratios);
-  return check_launch("accept_stochastic_kernel");
+  return launch("accept_stochastic_kernel", accept_stochastic_kernel, dim3((unsigned)B), dim3(SM_THREADS), 0, st,
+                target_logits, draft_logits, (int)V, (long long)ld, (const RowDist*)td, (const RowDist*)dd, drafts,
+                (int)drafts_ld, (int)k, (unsigned long long)seed, (unsigned long long)offset,
+                reinterpret_cast<const unsigned long long*>(offset_dev), out_tokens, out_count, ratios);
 }
 
 extern "C" int im_philox4x32_10(uint64_t seed, uint64_t offset, uint32_t stream_id, uint32_t n, uint32_t* out,

@@ -26,6 +26,8 @@ __global__ void spec_prepare_kernel(const int* __restrict__ hist, int cap, const
                                     const int* __restrict__ target, int B, int k, int slot_cap,
                                     int* __restrict__ d0_tok, int* __restrict__ d0_pos, int* __restrict__ d_pos,
                                     int* __restrict__ v_tok, int* __restrict__ v_pos) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   int nb = n[b];
@@ -44,6 +46,8 @@ __global__ void spec_prepare_kernel(const int* __restrict__ hist, int cap, const
 __global__ void spec_commit_kernel(int* __restrict__ hist, int cap, int* __restrict__ n,
                                    const int* __restrict__ target, int B, int k, const int* __restrict__ out_tokens,
                                    const int* __restrict__ out_count, long long* __restrict__ stats) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   const int nb = n[b];
@@ -72,9 +76,9 @@ extern "C" int im_spec_prepare(const int32_t* hist, int64_t cap, const int32_t* 
   IM_REQUIRE(hist && n && target && d0_tok && d0_pos && v_tok && v_pos && (k == 1 || d_pos), IM_INVALID,
              "im_spec_prepare: null pointer");
   const int threads = 128;
-  spec_prepare_kernel<<<(unsigned)((B + threads - 1) / threads), threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      hist, (int)cap, n, target, (int)B, (int)k, (int)slot_cap, d0_tok, d0_pos, d_pos, v_tok, v_pos);
-  return check_launch("spec_prepare_kernel");
+  return launch("spec_prepare_kernel", spec_prepare_kernel, dim3((unsigned)((B + threads - 1) / threads)), dim3(threads),
+                0, reinterpret_cast<cudaStream_t>(stream), hist, (int)cap, n, target, (int)B, (int)k, (int)slot_cap,
+                d0_tok, d0_pos, d_pos, v_tok, v_pos);
 }
 
 extern "C" int im_spec_commit(int32_t* hist, int64_t cap, int32_t* n, const int32_t* target, int64_t B, int64_t k,
@@ -83,7 +87,7 @@ extern "C" int im_spec_commit(int32_t* hist, int64_t cap, int32_t* n, const int3
   IM_REQUIRE(B >= 1 && k >= 0 && cap >= 1, IM_INVALID, "im_spec_commit: bad sizes");
   IM_REQUIRE(hist && n && target && out_tokens && out_count, IM_INVALID, "im_spec_commit: null pointer");
   const int threads = 128;
-  spec_commit_kernel<<<(unsigned)((B + threads - 1) / threads), threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      hist, (int)cap, n, target, (int)B, (int)k, out_tokens, out_count, reinterpret_cast<long long*>(stats));
-  return check_launch("spec_commit_kernel");
+  return launch("spec_commit_kernel", spec_commit_kernel, dim3((unsigned)((B + threads - 1) / threads)), dim3(threads),
+                0, reinterpret_cast<cudaStream_t>(stream), hist, (int)cap, n, target, (int)B, (int)k, out_tokens,
+                out_count, reinterpret_cast<long long*>(stats));
 }

@@ -11,10 +11,16 @@ gate/up interleaved in 16-row blocks (gate rows then the matching up rows, so on
 of the SwiGLU), down -- plus bf16 norm weights; the tied 4-bit embedding doubles as the LM head. KV caches are
 [layers][pages][Hkv][16][D] bf16 with a page table per sequence slot.
 
-Forward of M rows (any mix of sequences): embed -> per layer [RMSNorm, qkv qGEMM, q/k norm + RoPE + KV
-write, paged attention, o qGEMM + residual, RMSNorm, gate/up qGEMM + SwiGLU, down qGEMM + residual] ->
-final RMSNorm of the rows that need logits -> head qGEMM. Every kernel is row-invariant, so a verify row's
-logits equal those of a one-row decode bit for bit, and speculation never changes a greedy answer.
+Every projection is also held repacked for the packed qGEMM (`kernels.Packed`: 1152-byte units of 32 rows x 64
+inputs in MMA-fragment order), which is what the forward reads.
+
+Forward of M rows (any mix of sequences), six launches per layer: embed (+ each row's sum of squares) -> per
+layer [qkv qGEMM with the input RMSNorm fused into its prologue, q/k norm + RoPE + KV write, paged attention,
+o qGEMM + residual (+ per-tile sums of squares of the new h), gate/up qGEMM with the post-attention RMSNorm
+fused + SwiGLU, down qGEMM + residual (+ sums of squares)] -> head qGEMM with the final RMSNorm fused, over the
+leading rows that need logits. Every kernel is row-invariant (no arithmetic depends on M or on the other rows),
+so a verify row's logits equal those of a one-row decode bit for bit, and speculation never changes a greedy
+answer.
 """
 from __future__ import annotations
 
@@ -88,10 +94,11 @@ PRESETS = {
 
 @dataclass
 class Linear4:
-    """One 4-bit projection on the device."""
+    """One 4-bit projection on the device: MLX layout (w, s, b) and the packed copy the forward reads."""
     w: torch.Tensor
     s: torch.Tensor
     b: torch.Tensor
+    p: kernels.Packed | None = None
 
     @property
     def n(self) -> int:
@@ -158,7 +165,8 @@ class QuantModel:
         return (torch.randn((n, k), generator=gen, device=self.device) * sigma).to(torch.bfloat16)
 
     def _lin(self, w: torch.Tensor) -> Linear4:
-        return Linear4(*kernels.quantize(w.contiguous()))
+        wq, s, b = kernels.quantize(w.contiguous())
+        return Linear4(wq, s, b, kernels.Packed(wq, s, b))
 
     def _norm(self, gen, n) -> torch.Tensor:
         base = 0.0 if self.cfg.family == "gemma3" else 1.0
@@ -197,16 +205,21 @@ class QuantModel:
         c, r, dev = self.cfg, self.max_rows, self.device
         bf = torch.bfloat16
         self.h = torch.zeros((r, c.hidden), dtype=bf, device=dev)
-        self.xn = torch.zeros((r, c.hidden), dtype=bf, device=dev)
+        # row sums of squares of h for the fused RMSNorms: one part from the embedding, one per 32-row tile
+        # of the hidden dimension from the residual epilogues
+        self.h_tiles = -(-c.hidden // 32)
+        self.sq_embed = torch.zeros((32,), dtype=torch.float32, device=dev)
+        self.sq_attn = torch.zeros((self.h_tiles, 32), dtype=torch.float32, device=dev)
+        self.sq_mlp = torch.zeros((self.h_tiles, 32), dtype=torch.float32, device=dev)
         self.qkv = torch.zeros((r, c.qkv_rows), dtype=bf, device=dev)
         self.q = torch.zeros((r, c.heads, c.head_dim), dtype=bf, device=dev)
         self.attn = torch.zeros((r, c.heads * c.head_dim), dtype=bf, device=dev)  # [M, Hq, D] packed
         self.act = torch.zeros((r, c.inter), dtype=bf, device=dev)
-        self.hn = torch.zeros((self.max_logit_rows, c.hidden), dtype=bf, device=dev)
         self.logits = torch.zeros((self.max_logit_rows, c.vocab), dtype=bf, device=dev)
         # scratch: one buffer per kernel family, sized for the largest call this model makes
-        q_need = max(kernels.qgemm_workspace_bytes(min(r, MAX_QGEMM_ROWS), n, k) for n, k in self._gemm_shapes())
-        head_need = kernels.qgemm_workspace_bytes(self.max_logit_rows, c.vocab, c.hidden)
+        q_need = max(kernels.qgemm_packed_workspace_bytes(min(r, MAX_QGEMM_ROWS), n, k)
+                     for n, k in self._gemm_shapes())
+        head_need = kernels.qgemm_packed_workspace_bytes(self.max_logit_rows, c.vocab, c.hidden)
         self.ws_gemm = kernels.workspace(max(q_need, head_need), dev)
         a_need = max(kernels.attention_workspace_bytes(self.max_seqs, rows, c.heads, c.kv_heads, c.head_dim,
                                                        self.max_ctx, self.keys_per_split)
@@ -220,20 +233,23 @@ class QuantModel:
                 (c.hidden, c.inter)]
 
     # ---- forward ------------------------------------------------------------------------------------------
-    def forward(self, meta: RowMeta, max_kv_len: int, logit_rows: tuple[int, int, int] | None) -> torch.Tensor | None:
-        """Run M = meta.rows rows through the model, writing their K/V at their slots. logit_rows =
-        (first row, count, row step) selects the rows whose logits land in self.logits[:count]."""
+    def forward(self, meta: RowMeta, max_kv_len: int, logit_rows: int = 0) -> torch.Tensor | None:
+        """Run M = meta.rows rows through the model, writing their K/V at their slots; the logits of the first
+        `logit_rows` rows land in self.logits[:logit_rows] (returned; None when logit_rows is 0)."""
         c, m = self.cfg, meta.rows
         if m > min(self.max_rows, MAX_QGEMM_ROWS):
             raise ValueError(f"{m} rows exceed this model's per-forward limit")
+        if logit_rows > min(m, self.max_logit_rows):
+            raise ValueError(f"{logit_rows} logit rows exceed the rows or this model's logit buffer")
         gemma = c.family == "gemma3"
         mult = math.sqrt(c.hidden) if gemma else 1.0
-        h, xn = self.h, self.xn
+        h, ws = self.h, self.ws_gemm
         kernels.embed(meta.tokens, self.embed.w, self.embed.s, self.embed.b, mult=mult, out=h, rows=m,
-                      stride=meta.token_stride)
+                      stride=meta.token_stride, out_sq=self.sq_embed)
+        sq, parts = self.sq_embed, 1
         for li, layer in enumerate(self.layers):
-            kernels.rmsnorm(h, layer.in_norm, c.eps, gemma=gemma, out=xn, rows=m)
-            kernels.qgemm(xn, layer.qkv.w, layer.qkv.s, layer.qkv.b, out=self.qkv, rows=m, ws=self.ws_gemm)
+            kernels.qgemm_packed(h, layer.qkv.p, out=self.qkv, rows=m, norm_sq=sq, norm_parts=parts,
+                                 norm_weight=layer.in_norm, eps=c.eps, gemma_norm=gemma, ws=ws)
             glob = c.is_global(li)
             kernels.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm,
                                     self.inv_freq if glob else self.inv_freq_local, meta.pos, meta.pos, meta.seq,
@@ -244,21 +260,19 @@ class QuantModel:
                               keys_per_split=self.keys_per_split,
                               window=0 if glob else c.sliding_window, out=self.attn, rows=m, ws=self.ws_attn,
                               seq_slot=meta.seq_slot)
-            kernels.qgemm(self.attn, layer.o.w, layer.o.s, layer.o.b, epilogue="residual", residual=h, out=h,
-                          rows=m, ws=self.ws_gemm)
-            kernels.rmsnorm(h, layer.post_norm, c.eps, gemma=gemma, out=xn, rows=m)
-            kernels.qgemm(xn, layer.gate_up.w, layer.gate_up.s, layer.gate_up.b,
-                          epilogue="geglu" if gemma else "swiglu", out=self.act, rows=m, ws=self.ws_gemm)
-            kernels.qgemm(self.act, layer.down.w, layer.down.s, layer.down.b, epilogue="residual", residual=h,
-                          out=h, rows=m, ws=self.ws_gemm)
-        if logit_rows is None:
+            kernels.qgemm_packed(self.attn, layer.o.p, epilogue="residual", residual=h, out=h, rows=m,
+                                 out_sq=self.sq_attn, ws=ws)
+            kernels.qgemm_packed(h, layer.gate_up.p, epilogue="geglu" if gemma else "swiglu", out=self.act, rows=m,
+                                 norm_sq=self.sq_attn, norm_parts=self.h_tiles, norm_weight=layer.post_norm,
+                                 eps=c.eps, gemma_norm=gemma, ws=ws)
+            kernels.qgemm_packed(self.act, layer.down.p, epilogue="residual", residual=h, out=h, rows=m,
+                                 out_sq=self.sq_mlp, ws=ws)
+            sq, parts = self.sq_mlp, self.h_tiles
+        if not logit_rows:
             return None
-        first, count, step = logit_rows
-        kernels.rmsnorm(h[first:], self.final_norm, c.eps, gemma=gemma, out=self.hn, rows=count,
-                        ldx=step * c.hidden)
-        kernels.qgemm(self.hn, self.embed.w, self.embed.s, self.embed.b, out=self.logits, rows=count,
-                      ws=self.ws_gemm)
-        return self.logits[:count]
+        kernels.qgemm_packed(h, self.embed.p, out=self.logits, rows=logit_rows, norm_sq=sq, norm_parts=parts,
+                             norm_weight=self.final_norm, eps=c.eps, gemma_norm=gemma, ws=ws)
+        return self.logits[:logit_rows]
 
     # ---- eager helpers (prefill, plain decode, tests) -----------------------------------------------------
     def _meta(self, tokens: torch.Tensor, positions: list[int], seq: int) -> RowMeta:
@@ -278,13 +292,13 @@ class QuantModel:
         for off in range(0, total, step):
             part = tokens[off:off + step].contiguous()
             meta = self._meta(part, list(range(start + off, start + off + part.numel())), seq)
-            self.forward(meta, max_kv_len=self.max_ctx, logit_rows=None)
+            self.forward(meta, max_kv_len=self.max_ctx)
 
     def logits_for(self, tokens: torch.Tensor, start: int, seq: int = 0) -> torch.Tensor:
         """Feed `tokens` (one forward, rows at slots start..) and return every row's logits [M, V]."""
         m = tokens.numel()
         meta = self._meta(tokens.contiguous(), list(range(start, start + m)), seq)
-        return self.forward(meta, max_kv_len=self.max_ctx, logit_rows=(0, m, 1))
+        return self.forward(meta, max_kv_len=self.max_ctx, logit_rows=m)
 
 
 @dataclass
@@ -311,7 +325,7 @@ class SpecDecoder:
             raise ValueError("batch exceeds the models' sequence slots")
         if batch * (k + 1) > min(target.max_rows, MAX_QGEMM_ROWS) or batch * (k + 1) > target.max_logit_rows:
             raise ValueError("batch * (k + 1) verify rows exceed the target's per-forward limit")
-        if 2 * batch > draft.max_rows or batch > draft.max_logit_rows:
+        if 2 * batch > draft.max_rows or 2 * batch > draft.max_logit_rows:
             raise ValueError("draft pass rows exceed the draft model's limit")
         self.target, self.draft, self.k, self.batch = target, draft, k, batch
         dev = target.device
@@ -347,25 +361,27 @@ class SpecDecoder:
         slot_cap = self.cap
         kernels.spec_prepare(self.hist, self.n, self.target_len, b, k, slot_cap, self.d0_tok, self.d0_pos,
                              self.d_pos if k > 1 else None, self.v_tok, self.v_pos)
-        # draft pass 0: two rows per sequence; logits of the second row
+        # draft pass 0: two rows per sequence; the argmax reads the second row of each pair (the head runs over
+        # both: its cost is the weight stream, not the rows)
         meta = RowMeta(self.d0_tok, 1, self.d0_pos, self.seq_d0, self.rows_d0, 2 * b, 2)
-        logits = d.forward(meta, max_kv_len=slot_cap, logit_rows=(1, b, 2))
-        kernels.argmax_rows(logits, out=self.v_tok[1:], out_stride=k + 1, ws=d.ws_argmax, rows=b)
+        logits = d.forward(meta, max_kv_len=slot_cap, logit_rows=2 * b)
+        kernels.argmax_rows(logits[1:], out=self.v_tok[1:], out_stride=k + 1, ws=d.ws_argmax, rows=b,
+                            ld=2 * d.cfg.vocab)
         for i in range(1, k):
             meta = RowMeta(self.v_tok[i:], k + 1, self.d_pos[i - 1], self.seq_d, self.rows_d, b, 1)
-            logits = d.forward(meta, max_kv_len=slot_cap, logit_rows=(0, b, 1))
+            logits = d.forward(meta, max_kv_len=slot_cap, logit_rows=b)
             kernels.argmax_rows(logits, out=self.v_tok[i + 1:], out_stride=k + 1, ws=d.ws_argmax, rows=b)
         meta = RowMeta(self.v_tok, 1, self.v_pos, self.seq_v, self.rows_v, b * (k + 1), k + 1)
-        logits = t.forward(meta, max_kv_len=slot_cap, logit_rows=(0, b * (k + 1), 1))
+        logits = t.forward(meta, max_kv_len=slot_cap, logit_rows=b * (k + 1))
         kernels.verify_greedy(logits, self.v_tok[1:], b=b, k=k, drafts_ld=k + 1, tokens=self.out_tokens,
                               count=self.out_count, ws=self.ws_verify)
         kernels.spec_commit(self.hist, self.n, self.target_len, b, k, self.out_tokens, self.out_count, self.stats)
 
     def launches_per_round(self) -> int:
         """libimspec kernel launches in one round (counted from the round's structure)."""
-        per_layer = 8
+        per_layer = 6
         def fwd(model, logits):
-            return 1 + per_layer * model.cfg.layers + (2 if logits else 0)
+            return 1 + per_layer * model.cfg.layers + (1 if logits else 0)
         return 1 + self.k * (fwd(self.draft, True) + 1) + fwd(self.target, True) + 1 + 1
 
     # ---- state ------------------------------------------------------------------------------------------

@@ -146,18 +146,21 @@ def argmax_workspace_bytes(rows: int, v: int) -> int:
 
 def argmax_rows(logits: torch.Tensor, with_conf: bool = False, *, out: torch.Tensor | None = None,
                 out_stride: int = 1, conf_out: torch.Tensor | None = None, ws: torch.Tensor | None = None,
-                rows: int | None = None):
-    """(argmax int32, conf float32 or None) over the last axis of bf16 logits; `out` may be a strided int32
-    buffer (row r written at out[r * out_stride])."""
+                rows: int | None = None, ld: int | None = None):
+    """(argmax int32, conf float32 or None) over the last axis of bf16 logits; row r starts at element r * ld
+    (default: the vocabulary size); `out` may be a strided int32 buffer (row r written at out[r * out_stride])."""
     _check(logits, "logits", (torch.bfloat16,))
     device = logits.device
     v = logits.shape[-1]
+    ld = v if ld is None else ld
     rows = logits.numel() // v if rows is None else rows
+    if (rows - 1) * ld + v > logits.numel():
+        raise ValueError("rows * ld exceed the logits buffer")
     idx = torch.empty(rows, dtype=torch.int32, device=device) if out is None else out
     conf = conf_out if conf_out is not None else (
         torch.empty(rows, dtype=torch.float32, device=device) if with_conf else None)
     ws_ptr, ws_bytes = _scratch(ws, device, argmax_workspace_bytes(rows, v), "argmax")
-    _lib.call("im_argmax_rows", logits.data_ptr(), rows, v, v, idx.data_ptr(), out_stride,
+    _lib.call("im_argmax_rows", logits.data_ptr(), rows, v, ld, idx.data_ptr(), out_stride,
               conf.data_ptr() if conf is not None else None, ws_ptr, ws_bytes, _stream(device))
     return idx, conf
 
@@ -344,6 +347,12 @@ class Packed:
     @property
     def tiles(self) -> int:
         return (self.n + 31) // 32
+
+
+def set_launch_overlap(on: bool) -> bool:
+    """Programmatic dependent launch of the decode-path kernels on (default) or off; returns the previous
+    setting. Results are bit-identical either way."""
+    return bool(_lib.load().im_set_launch_overlap(int(bool(on))))
 
 
 def qgemm_packed_workspace_bytes(m: int, n: int, k: int) -> int:

@@ -180,6 +180,22 @@ def test_verify_rows_equal_one_row_decodes(cuda):
         assert torch.equal(many[i].view(torch.int16), one[i][0].view(torch.int16)), i
 
 
+def test_launch_overlap_changes_no_bits(cuda):
+    """Programmatic dependent launch only moves when CTAs start: logits are identical with it off."""
+    model = tiny(sigma=0.08)
+    toks = torch.from_numpy(np.random.default_rng(7).integers(0, 1000, 25).astype(np.int32)).to(cuda)
+    model.prefill(toks[:20])
+    on = model.logits_for(toks[20:25], 20).clone()
+    prev = kernels.set_launch_overlap(False)
+    try:
+        model.prefill(toks[:20])
+        off = model.logits_for(toks[20:25], 20).clone()
+    finally:
+        kernels.set_launch_overlap(prev)
+    assert prev is True
+    assert torch.equal(on.view(torch.int16), off.view(torch.int16))
+
+
 @pytest.mark.parametrize("graph", [False, True])
 def test_speculation_changes_no_answer(cuda, graph):
     target = tiny("tiny-target", seed=1, sigma=0.08)
