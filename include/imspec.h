@@ -234,6 +234,22 @@ int im_attention_paged(const uint16_t* q, const uint16_t* k_cache, const uint16_
                        float scale, uint16_t* out, void* workspace, size_t workspace_bytes, void* stream);
 size_t im_attention_workspace_bytes(int64_t B, int64_t max_rows_per_seq, int64_t Hq, int64_t Hkv, int64_t D,
                                     int64_t max_kv_len, int64_t keys_per_split);
+/*
+ * The same attention starting from the packed projection rows qkv [M, (Hq + 2 Hkv) D] (q heads, k heads,
+ * v heads): q and the new keys get RMSNorm (q_norm / k_norm; w or 1 + w when gemma_style) and RoPE at
+ * row_pos[r] inside the kernel -- bit-identical to im_qk_norm_rope_kv followed by im_attention_paged -- and
+ * every row's K and V are written to the caches at row_slot[r] of its sequence's pages. At most 32 rows
+ * per sequence. Replaces the q/k norm, RoPE and cache write of the decode step together with its
+ * attention (ironmule/paired_research.py:177-215, ironmule/dense_plan.py:337-370 then :111-195, :258-274).
+ */
+int im_attention_qkv_paged(const uint16_t* qkv, const uint16_t* q_norm, const uint16_t* k_norm,
+                           const float* inv_freq, const int32_t* row_pos, float eps, int gemma_style,
+                           uint16_t* k_cache, uint16_t* v_cache, const int32_t* page_table, int64_t max_pages,
+                           const int32_t* seq_rows, const int32_t* seq_slot, const int32_t* row_slot,
+                           const uint64_t* tree_mask, const int32_t* tree_base, int64_t B, int64_t max_rows_per_seq,
+                           int64_t Hq, int64_t Hkv, int64_t D, int64_t max_kv_len, int64_t keys_per_split,
+                           int64_t window, float scale, uint16_t* out, void* workspace, size_t workspace_bytes,
+                           void* stream);
 
 /*
  * Device bookkeeping of one speculative round with k drafts for B sequences (no host round trip).

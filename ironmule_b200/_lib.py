@@ -53,6 +53,9 @@ SIGNATURES: dict[str, tuple] = {
     "im_attention_paged": (_INT, [_P, _P, _P, _P, _I64, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64,
                                   _I64, _I64, _I64, ctypes.c_float, _P, _P, _SZ, _P]),
     "im_attention_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _I64, _I64, _I64]),
+    "im_attention_qkv_paged": (_INT, [_P, _P, _P, _P, _P, ctypes.c_float, _INT, _P, _P, _P, _I64, _P, _P, _P, _P,
+                                      _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, ctypes.c_float, _P, _P,
+                                      _SZ, _P]),
     "im_spec_prepare": (_INT, [_P, _I64, _P, _P, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P]),
     "im_spec_commit": (_INT, [_P, _I64, _P, _P, _I64, _I64, _P, _P, _P, _P]),
     "im_sampling_workspace_bytes": (_SZ, [_I64]),

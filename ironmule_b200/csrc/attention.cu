@@ -11,6 +11,13 @@
 // row was written to (its causal limit). Tree mode: slots >= tree_base[b] are draft-tree nodes and row r sees
 // node j only if bit j of tree_mask[r] is set.
 //
+// Two entry points share one kernel. im_attention_paged reads q and every key from memory.
+// im_attention_qkv_paged starts from the packed qkv rows of the projection: each CTA applies the q RMSNorm
+// + RoPE to its own query vectors and the k RMSNorm + RoPE to the new rows' keys of its split (the same
+// arithmetic, in the same order, as im_qk_norm_rope_kv), uses them from shared memory, and one CTA per
+// (row, kv head) writes them to the cache. Keys that no row of this launch writes are staged with cp.async
+// before the kernel waits for the previous kernel, so their loads overlap it.
+//
 // Work split: grid (key splits, kv heads, sequences x query blocks). A CTA owns up to NQ query vectors
 // (rows x the kv head's query heads) and one split of `kpc` keys at fixed absolute positions, walked in
 // 64-key blocks staged in shared memory with an online softmax. CTAs publish (acc, max, sum) partials; the
@@ -23,16 +30,26 @@
 namespace im {
 
 constexpr int AT_THREADS = 128;
-constexpr int AT_KB = 64;  // keys per shared-memory block
+constexpr int AT_KB = 64;       // keys per shared-memory block
+constexpr int AT_MAXNEW = 32;   // new (written by this launch) keys per split at most: rows per sequence <= 32
+constexpr int AT_MW = 64;       // splits whose merge weights are kept in shared memory
+// A split partial per query vector: D accumulators, max, sum, 2 floats of padding (16-byte rows for float4
+// reads in the merge).
+constexpr int AT_PAD = 4;
 // Workspace layout, identical for every call so calls of different shapes may share one buffer: arrival
 // counters in a fixed region (kept at zero between launches), then the split partials.
 constexpr size_t AT_COUNTER_BYTES = 65536;
 constexpr int64_t AT_MAX_GROUPS = (int64_t)(AT_COUNTER_BYTES / 4);
 
 struct AttnArgs {
-  const uint16_t* q;
-  const uint16_t* kc;
-  const uint16_t* vc;
+  const uint16_t* q;          // plain mode: [M][Hq][D]
+  const uint16_t* qkv;        // fused mode: [M][(Hq + 2 Hkv) D] packed q | k | v rows
+  const uint16_t* q_norm;     // fused: [D]
+  const uint16_t* k_norm;     // fused: [D]
+  const float* inv_freq;      // fused: [D/2]
+  const int* row_pos;         // fused: RoPE position per row
+  uint16_t* kc;
+  uint16_t* vc;
   const int* page_table;
   const int* seq_rows;
   const int* seq_slot;  // page-table row of each sequence group (NULL: group b uses row b)
@@ -42,43 +59,145 @@ struct AttnArgs {
   uint16_t* out;
   float* part;
   unsigned* counters;
-  int max_pages, Hq, Hkv, kpc, nsplit, qblocks, window;
-  float scale;
+  int max_pages, Hq, Hkv, kpc, nsplit, qblocks, window, gemma;
+  float scale, eps;
 };
 
-template <int D, int NQ>
+template <int D, int NQ, bool FUSED>
 struct AttnSmem {
-  float qs[NQ][D];
-  uint32_t ks[AT_KB][D / 2 + 1];  // bf16 pairs, odd row stride in words: conflict-free per-key reads
-  uint16_t vs[AT_KB][D];
-  float s[NQ][AT_KB];
-  float m[NQ], l[NQ], alpha[NQ];
+  static constexpr int NEW = FUSED ? AT_MAXNEW : 1;
+  static constexpr int QM = NQ < 16 ? 16 : NQ;  // rows of the m16 MMA tiles (rows >= nq stay zero)
+  // Row strides are padded by 16 bytes so the MMA fragment loads (and ldmatrix rows) hit distinct banks.
+  uint16_t qs[QM][D + 8];         // bf16 queries
+  uint32_t ks[AT_KB][D / 2 + 4];  // keys as bf16 pairs
+  uint16_t vs[AT_KB][D + 8];      // values
+  float s[NQ][AT_KB + 4];         // scores; in the merge, the splits' sums
+  uint16_t ph[QM][AT_KB + 8];     // probabilities split into bf16 high and low parts: p = ph + pl
+  uint16_t pl[QM][AT_KB + 8];
+  uint16_t nk[NEW][D];  // fused: keys (normed, roped) and values of the rows this launch writes in this split
+  uint16_t nv[NEW][D];
+  float m[NQ], l[NQ], alpha[QM];
   int row_slot[NQ];
   unsigned long long tmask[NQ];
+  int new_row[NEW], new_slot[NEW];
+  int nnew, kv_len;
+  int page[AT_KB / 16];  // pages of the block being staged
+  int newidx[AT_KB];  // per key of the block being staged: index into nk/nv, or -1
+  float mw[NQ][AT_MW];  // merge: per (query vector, split) weights
   int last;
 };
 
-template <int D, int NQ>
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  const unsigned dst = (unsigned)__cvta_generic_to_shared(smem);
+  const int n = valid ? 16 : 0;  // 0 source bytes: the 16 bytes are zero-filled
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Four 8x8 bf16 matrices from shared memory, transposed: rows given by lanes 0-7, 8-15, 16-23, 24-31.
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
+  const unsigned addr = (unsigned)__cvta_generic_to_shared(p);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+// RMSNorm (weight w: w or 1 + w) + RoPE of one head vector by one warp; lane owns elements lane + 32 e.
+// The sum of squares is the per-32-element xor-tree sums added in element order, and the RoPE pairs
+// (i, i + D/2) sit in the same lane: the arithmetic of qk_rope_kv_kernel, value for value.
+template <int D>
+__device__ __forceinline__ void norm_rope_vals(const float (&v)[D / 32], const uint16_t* __restrict__ w, int gemma,
+                                               float eps, int pos, const float* __restrict__ inv_freq,
+                                               uint16_t (&outv)[D / 32]) {
+  constexpr int E = D / 32, H = E / 2;
+  const int lane = threadIdx.x & 31;
+  float total = 0.f;
+#pragma unroll
+  for (int e = 0; e < E; e++) total += warp_sum(v[e] * v[e]);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(total, (float)D) + eps));
+  float xn[E];
+#pragma unroll
+  for (int e = 0; e < E; e++) {
+    const float wd = gemma ? 1.0f + bf(w[lane + 32 * e]) : bf(w[lane + 32 * e]);
+    xn[e] = round_bf((v[e] * inv) * wd);
+  }
+#pragma unroll
+  for (int e = 0; e < H; e++) {
+    const float ang = (float)pos * inv_freq[lane + 32 * e];
+    float sn, cs;
+    sincosf(ang, &sn, &cs);
+    const float x1 = xn[e], x2 = xn[e + H];
+    outv[e] = to_bf(x1 * cs - x2 * sn);
+    outv[e + H] = to_bf(x1 * sn + x2 * cs);
+  }
+}
+
+template <int D, int NQ, bool FUSED>
 __global__ void __launch_bounds__(AT_THREADS)
 attn_kernel(AttnArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  AttnSmem<D, NQ>& sm = *reinterpret_cast<AttnSmem<D, NQ>*>(smem_raw);
-  pdl_wait();
-  pdl_trigger();
+  using Smem = AttnSmem<D, NQ, FUSED>;
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  if constexpr (!FUSED) {
+    pdl_wait();  // q and every key were written by earlier kernels
+    pdl_trigger();
+  }
+  // Before the wait (fused mode) only data that the previous kernel (the qkv projection) does not write is
+  // read: the row metadata, the page table and the keys of slots no row of this launch writes.
   const int split = blockIdx.x, kvh = blockIdx.y;
   const int b = blockIdx.z / a.qblocks, qb = blockIdx.z % a.qblocks;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = a.Hq / a.Hkv;
   const int r0 = a.seq_rows[b], nr = a.seq_rows[b + 1] - r0;
   const int prow = a.seq_slot ? a.seq_slot[b] : b;
   const int q0 = qb * NQ;
   const int nq = max(0, min(NQ, nr * G - q0));
 
-  // kv length of the sequence: one past the largest slot any of its rows was written to
-  int kv_len = 0;
-  for (int r = 0; r < nr; r++) kv_len = max(kv_len, a.row_slot[r0 + r] + 1);
   const int tbase = a.tree_mask ? a.tree_base[b] : 0;
-
+  const int k_begin = split * a.kpc;
+  // Row metadata with every load in flight at once: warp 0 reads the rows' slots (kv length = one past the
+  // largest; the rows whose slot falls in this split are this launch's new keys there), the other threads the
+  // query vectors' limits and masks.
+  if (warp == 0) {
+    int mx = -1, n = 0;
+    for (int r0l = 0; r0l < nr; r0l += 32) {
+      const int r = r0l + lane;
+      const int slot = r < nr ? a.row_slot[r0 + r] : -1;
+      int m2 = slot;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m2 = max(m2, __shfl_xor_sync(0xffffffffu, m2, o));
+      mx = max(mx, m2);
+      if constexpr (FUSED) {
+        const bool isnew = slot >= k_begin && slot < k_begin + a.kpc;
+        const unsigned ball = __ballot_sync(0xffffffffu, isnew);
+        const int idx = n + __popc(ball & ((1u << lane) - 1u));
+        if (isnew && idx < AT_MAXNEW) {
+          sm.new_row[idx] = r0 + r;
+          sm.new_slot[idx] = slot;
+        }
+        n += __popc(ball);
+      }
+    }
+    if (lane == 0) {
+      sm.kv_len = mx + 1;
+      sm.nnew = min(n, AT_MAXNEW);
+    }
+  }
+  for (int i = tid; i < Smem::QM * (D + 8) / 2; i += AT_THREADS) reinterpret_cast<uint32_t*>(&sm.qs[0][0])[i] = 0u;
+  for (int i = tid; i < Smem::QM * (AT_KB + 8) / 2; i += AT_THREADS) {
+    reinterpret_cast<uint32_t*>(&sm.ph[0][0])[i] = 0u;
+    reinterpret_cast<uint32_t*>(&sm.pl[0][0])[i] = 0u;
+  }
+  for (int i = tid; i < Smem::QM; i += AT_THREADS) sm.alpha[i] = 0.f;
   for (int i = tid; i < NQ; i += AT_THREADS) {
     sm.m[i] = -INFINITY;
     sm.l[i] = 0.f;
@@ -88,139 +207,283 @@ attn_kernel(AttnArgs a) {
       sm.tmask[i] = a.tree_mask ? a.tree_mask[row] : 0ull;
     }
   }
-  for (int i = tid; i < nq * D; i += AT_THREADS) {
-    const int qi = i / D, d = i % D;
-    const int row = r0 + (q0 + qi) / G, head = kvh * G + (q0 + qi) % G;
-    sm.qs[qi][d] = bf(a.q[((size_t)row * a.Hq + head) * D + d]);
-  }
-  constexpr int DPT = D / AT_THREADS;  // output dims per thread in the P.V step
-  float acc[NQ][DPT];
-#pragma unroll
-  for (int i = 0; i < NQ; i++)
-#pragma unroll
-    for (int e = 0; e < DPT; e++) acc[i][e] = 0.f;
-
-  const int k_begin = split * a.kpc;
+  __syncthreads();
+  const int kv_len = sm.kv_len;
   const int k_end = min(kv_len, k_begin + a.kpc);
-  for (int kb0 = k_begin; kb0 < k_end && nq > 0; kb0 += AT_KB) {
+  const bool active = nq > 0 && k_begin < k_end;
+
+  // stage keys [kb0, kb0 + 64): K as bf16 pairs and V; slots written by this launch come from nk/nv later
+  auto stage_old = [&](int kb0) {
+    if (tid < AT_KB / 16) {
+      const int slot = kb0 + tid * 16;
+      sm.page[tid] = slot < k_end ? a.page_table[(size_t)prow * a.max_pages + (slot >> 4)] : 0;
+    }
+    if constexpr (FUSED) {
+      for (int j = tid; j < AT_KB; j += AT_THREADS) {
+        int idx = -1;
+        for (int n = 0; n < sm.nnew; n++)
+          if (sm.new_slot[n] == kb0 + j) idx = n;
+        sm.newidx[j] = idx;
+      }
+    }
     __syncthreads();
-    // stage K (as bf16 pairs) and V for keys [kb0, kb0 + 64)
-    for (int i = tid; i < AT_KB * (D / 8); i += AT_THREADS) {
+    constexpr int PER = AT_KB * (D / 8) / AT_THREADS;
+#pragma unroll
+    for (int t = 0; t < PER; t++) {
+      const int i = tid + t * AT_THREADS;
       const int j = i / (D / 8), c = i % (D / 8);
       const int slot = kb0 + j;
-      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (slot < k_end) {
-        const int page = a.page_table[(size_t)prow * a.max_pages + (slot >> 4)];
-        const size_t off = (((size_t)page * a.Hkv + kvh) * 16 + (slot & 15)) * D + c * 8;
-        kv = ldg_u4(a.kc + off);
-        vv = ldg_u4(a.vc + off);
+      bool skip = false;
+      if constexpr (FUSED) skip = sm.newidx[j] >= 0;  // filled from nk/nv by plain stores: no async copy here
+      if (!skip) {
+        const bool load = slot < k_end;  // past the end: zero-filled
+        const size_t off = load ? (((size_t)sm.page[j >> 4] * a.Hkv + kvh) * 16 + (slot & 15)) * D + c * 8 : 0;
+        cp_async16(&sm.ks[j][c * 4], a.kc + off, load);
+        cp_async16(&sm.vs[j][c * 8], a.vc + off, load);
       }
-      sm.ks[j][c * 4 + 0] = kv.x;
-      sm.ks[j][c * 4 + 1] = kv.y;
-      sm.ks[j][c * 4 + 2] = kv.z;
-      sm.ks[j][c * 4 + 3] = kv.w;
-      *reinterpret_cast<uint4*>(&sm.vs[j][c * 8]) = vv;
     }
-    __syncthreads();
-    // scores: thread -> key j, query vectors h, h+2, h+4, ...
-    {
-      const int j = tid & (AT_KB - 1), h = tid >> 6;
-      constexpr int PER = NQ / 2;
-      float sc[PER];
-#pragma unroll
-      for (int i = 0; i < PER; i++) sc[i] = 0.f;
-#pragma unroll 4
-      for (int d2 = 0; d2 < D / 2; d2++) {
-        const uint32_t kk = sm.ks[j][d2];
-        const float k0 = bf_lo(kk), k1 = bf_hi(kk);
-#pragma unroll
-        for (int i = 0; i < PER; i++) {
-          const float2 qq = *reinterpret_cast<const float2*>(&sm.qs[h + 2 * i][2 * d2]);
-          sc[i] = fmaf(qq.y, k1, fmaf(qq.x, k0, sc[i]));
-        }
-      }
-      const int slot = kb0 + j;
-#pragma unroll
-      for (int i = 0; i < PER; i++) {
-        const int qi = h + 2 * i;
-        if (qi < nq) {
-          const int lim = sm.row_slot[qi];
-          bool vis = slot < k_end && slot <= lim;
-          if (a.window > 0) vis = vis && slot > lim - a.window;
-          if (a.tree_mask && slot >= tbase) {
-            const int node = slot - tbase;
-            vis = vis && node < 64 && ((sm.tmask[qi] >> node) & 1ull);
-          }
-          sm.s[qi][j] = vis ? sc[i] * a.scale : -INFINITY;
+  };
+  auto fill_new = [&]() {
+    if constexpr (FUSED) {
+      for (int i = tid; i < AT_KB * (D / 8); i += AT_THREADS) {
+        const int j = i / (D / 8), c = i % (D / 8);
+        const int idx = sm.newidx[j];
+        if (idx >= 0) {
+          *reinterpret_cast<uint4*>(&sm.ks[j][c * 4]) = *reinterpret_cast<const uint4*>(&sm.nk[idx][c * 8]);
+          *reinterpret_cast<uint4*>(&sm.vs[j][c * 8]) = *reinterpret_cast<const uint4*>(&sm.nv[idx][c * 8]);
         }
       }
     }
-    __syncthreads();
-    // online softmax per query vector: warp w takes w, w+4, ...
-    {
-      const int warp = tid >> 5, lane = tid & 31;
-      for (int qi = warp; qi < nq; qi += AT_THREADS / 32) {
-        const float s0 = sm.s[qi][lane], s1 = sm.s[qi][lane + 32];
-        float bm = fmaxf(s0, s1);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
-        const float mo = sm.m[qi];
-        const float mn = fmaxf(mo, bm);
-        const float p0 = mn == -INFINITY ? 0.f : expf(s0 - mn);
-        const float p1 = mn == -INFINITY ? 0.f : expf(s1 - mn);
-        const float ps = warp_sum(p0 + p1);
-        sm.s[qi][lane] = p0;
-        sm.s[qi][lane + 32] = p1;
-        if (lane == 0) {
-          const float al = mo == -INFINITY ? 0.f : expf(mo - mn);
-          sm.alpha[qi] = al;
-          sm.l[qi] = sm.l[qi] * al + ps;
-          sm.m[qi] = mn;
-        }
-      }
-    }
-    __syncthreads();
-    // P.V: thread owns dims tid, tid + 128, ...
-#pragma unroll
-    for (int i = 0; i < NQ; i++) {
-      if (i < nq) {
-        const float al = sm.alpha[i];
-#pragma unroll
-        for (int e = 0; e < DPT; e++) acc[i][e] *= al;
-      }
-    }
-    for (int j = 0; j < AT_KB; j += 4) {
-      float v[4][DPT];
-#pragma unroll
-      for (int jj = 0; jj < 4; jj++)
-#pragma unroll
-        for (int e = 0; e < DPT; e++) v[jj][e] = bf(sm.vs[j + jj][tid + e * AT_THREADS]);
-#pragma unroll
-      for (int i = 0; i < NQ; i++) {
-        if (i < nq) {
-          const float4 p = *reinterpret_cast<const float4*>(&sm.s[i][j]);
-#pragma unroll
-          for (int e = 0; e < DPT; e++)
-            acc[i][e] = fmaf(p.w, v[3][e], fmaf(p.z, v[2][e], fmaf(p.y, v[1][e], fmaf(p.x, v[0][e], acc[i][e]))));
-        }
-      }
-    }
-  }
-  __syncthreads();
+  };
 
-  // publish this split's partial: acc[D], max, sum per query vector
-  const size_t group = ((size_t)b * a.Hkv + kvh) * a.qblocks + qb;
-  float* mine = a.part + (group * a.nsplit + split) * (size_t)NQ * (D + 2);
+  if (active) stage_old(k_begin);
+
+  if constexpr (FUSED) {
+    pdl_wait();
+    pdl_trigger();
+    if (active) {
+      const int stride = (a.Hq + 2 * a.Hkv) * D;
+      // this CTA's query vectors: RMSNorm + RoPE, rounded to bf16 as the unfused path stores them; a warp
+      // loads all of its vectors before computing any
+      {
+        constexpr int VPW = NQ / (AT_THREADS / 32);
+        float v[VPW][D / 32];
+        int pos[VPW];
 #pragma unroll
-  for (int i = 0; i < NQ; i++) {
-    if (i < nq) {
+        for (int t = 0; t < VPW; t++) {
+          const int qi = warp + t * (AT_THREADS / 32);
+          if (qi < nq) {
+            const int row = r0 + (q0 + qi) / G, head = kvh * G + (q0 + qi) % G;
+            const uint16_t* src = a.qkv + (size_t)row * stride + head * D;
 #pragma unroll
-      for (int e = 0; e < DPT; e++) __stcg(mine + (size_t)i * (D + 2) + tid + e * AT_THREADS, acc[i][e]);
+            for (int e = 0; e < D / 32; e++) v[t][e] = bf(src[lane + 32 * e]);
+            pos[t] = a.row_pos[row];
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < VPW; t++) {
+          const int qi = warp + t * (AT_THREADS / 32);
+          if (qi < nq) {
+            uint16_t o[D / 32];
+            norm_rope_vals<D>(v[t], a.q_norm, a.gemma, a.eps, pos[t], a.inv_freq, o);
+#pragma unroll
+            for (int e = 0; e < D / 32; e++) sm.qs[qi][lane + 32 * e] = o[e];
+          }
+        }
+      }
+      // the new rows' keys and values of this split (the first query block's CTA also writes them out)
+      for (int n = warp; n < sm.nnew; n += AT_THREADS / 32) {
+        const int row = sm.new_row[n], slot = sm.new_slot[n];
+        const uint16_t* src = a.qkv + (size_t)row * stride + (a.Hq + kvh) * D;
+        uint16_t o[D / 32];
+        float v[D / 32];
+#pragma unroll
+        for (int e = 0; e < D / 32; e++) v[e] = bf(src[lane + 32 * e]);
+        norm_rope_vals<D>(v, a.k_norm, a.gemma, a.eps, a.row_pos[row], a.inv_freq, o);
+        const int page = a.page_table[(size_t)prow * a.max_pages + (slot >> 4)];
+        const size_t off = (((size_t)page * a.Hkv + kvh) * 16 + (slot & 15)) * D;
+#pragma unroll
+        for (int e = 0; e < D / 32; e++) {
+          const int d = lane + 32 * e;
+          const uint16_t v = src[(size_t)a.Hkv * D + d];
+          sm.nk[n][d] = o[e];
+          sm.nv[n][d] = v;
+          if (qb == 0) {
+            a.kc[off + d] = o[e];
+            a.vc[off + d] = v;
+          }
+        }
+      }
+      __syncthreads();
+      fill_new();
+    }
+  } else {
+    for (int i = tid; i < nq * D; i += AT_THREADS) {
+      const int qi = i / D, d = i % D;
+      const int row = r0 + (q0 + qi) / G, head = kvh * G + (q0 + qi) % G;
+      sm.qs[qi][d] = a.q[((size_t)row * a.Hq + head) * D + d];
     }
   }
-  for (int i = tid; i < nq; i += AT_THREADS) {
-    __stcg(mine + (size_t)i * (D + 2) + D, sm.m[i]);
-    __stcg(mine + (size_t)i * (D + 2) + D + 1, sm.l[i]);
+
+  // Tensor-core tiles (mma.sync m16n8k16, bf16 in, fp32 accumulate). Scores S[q][key] = Q K^T: warp w owns
+  // keys 16w..16w+15 (two n8 tiles) for all query rows. Output O[q][d] = P V: warp w owns dims
+  // [w D/4, (w+1) D/4); P enters as two bf16 operands (high and low parts), so it keeps ~16 bits.
+  constexpr int MT = Smem::QM / 16;     // m16 tiles of query rows
+  constexpr int DW = D / 4;             // output dims per warp
+  constexpr int NTO = DW / 8;           // n8 tiles of output dims per warp
+  float o_acc[MT][NTO][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+    for (int nt = 0; nt < NTO; nt++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) o_acc[mt][nt][e] = 0.f;
+  const int g = lane >> 2, t = lane & 3;
+
+  for (int kb0 = k_begin; kb0 < k_end && active; kb0 += AT_KB) {
+    if (kb0 != k_begin) {
+      __syncthreads();  // the previous block's K/V and probabilities are consumed
+      stage_old(kb0);
+      fill_new();
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    // scores
+    {
+      float sacc[MT][2][4];
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+          for (int e = 0; e < 4; e++) sacc[mt][nt][e] = 0.f;
+      const int n0 = warp * 16;
+#pragma unroll 4
+      for (int kk = 0; kk < D / 16; kk++) {
+        uint32_t bk[2][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++) {
+          bk[nt][0] = sm.ks[n0 + nt * 8 + g][kk * 8 + t];
+          bk[nt][1] = sm.ks[n0 + nt * 8 + g][kk * 8 + 4 + t];
+        }
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++) {
+          const uint32_t* q0r = reinterpret_cast<const uint32_t*>(&sm.qs[mt * 16 + g][kk * 16 + 2 * t]);
+          const uint32_t* q8r = reinterpret_cast<const uint32_t*>(&sm.qs[mt * 16 + g + 8][kk * 16 + 2 * t]);
+          const uint32_t a0 = q0r[0], a1 = q8r[0], a2 = q0r[4], a3 = q8r[4];
+#pragma unroll
+          for (int nt = 0; nt < 2; nt++) mma_bf16(sacc[mt][nt], a0, a1, a2, a3, bk[nt][0], bk[nt][1]);
+        }
+      }
+      // scale and mask into sm.s
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const int qi = mt * 16 + g + (e >> 1) * 8;
+            const int j = n0 + nt * 8 + 2 * t + (e & 1);
+            if (qi < nq) {
+              const int slot = kb0 + j;
+              const int lim = sm.row_slot[qi];
+              bool vis = slot < k_end && slot <= lim;
+              if (a.window > 0) vis = vis && slot > lim - a.window;
+              if (a.tree_mask && slot >= tbase) {
+                const int node = slot - tbase;
+                vis = vis && node < 64 && ((sm.tmask[qi] >> node) & 1ull);
+              }
+              sm.s[qi][j] = vis ? sacc[mt][nt][e] * a.scale : -INFINITY;
+            }
+          }
+    }
+    __syncthreads();
+    // online softmax per query vector: warp w takes w, w+4, ...; p goes out as bf16 high + low parts
+    for (int qi = warp; qi < nq; qi += AT_THREADS / 32) {
+      const float s0 = sm.s[qi][lane], s1 = sm.s[qi][lane + 32];
+      float bm = fmaxf(s0, s1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+      const float mo = sm.m[qi];
+      const float mn = fmaxf(mo, bm);
+      const float p0 = mn == -INFINITY ? 0.f : expf(s0 - mn);
+      const float p1 = mn == -INFINITY ? 0.f : expf(s1 - mn);
+      const float ps = warp_sum(p0 + p1);
+      const uint16_t h0 = to_bf(p0), h1 = to_bf(p1);
+      sm.ph[qi][lane] = h0;
+      sm.ph[qi][lane + 32] = h1;
+      sm.pl[qi][lane] = to_bf(p0 - bf(h0));
+      sm.pl[qi][lane + 32] = to_bf(p1 - bf(h1));
+      if (lane == 0) {
+        const float al = mo == -INFINITY ? 0.f : expf(mo - mn);
+        sm.alpha[qi] = al;
+        sm.l[qi] = sm.l[qi] * al + ps;
+        sm.m[qi] = mn;
+      }
+    }
+    __syncthreads();
+    // O = alpha O + P V
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++) {
+      const float al0 = sm.alpha[mt * 16 + g], al8 = sm.alpha[mt * 16 + g + 8];
+#pragma unroll
+      for (int nt = 0; nt < NTO; nt++) {
+        o_acc[mt][nt][0] *= al0;
+        o_acc[mt][nt][1] *= al0;
+        o_acc[mt][nt][2] *= al8;
+        o_acc[mt][nt][3] *= al8;
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < AT_KB / 16; kk++) {
+      uint32_t bv[NTO][2];
+#pragma unroll
+      for (int nt = 0; nt < NTO; nt += 2) {
+        const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int d0 = warp * DW + nt * 8 + (lane >> 4) * 8;
+        ldsm_x4_trans(bv[nt][0], bv[nt][1], bv[nt + 1][0], bv[nt + 1][1], &sm.vs[key][d0]);
+      }
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++) {
+        const int r0w = mt * 16 + g;
+        const uint32_t h0 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w][kk * 16 + 2 * t]);
+        const uint32_t h1 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w + 8][kk * 16 + 2 * t]);
+        const uint32_t h2 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w][kk * 16 + 2 * t + 8]);
+        const uint32_t h3 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w + 8][kk * 16 + 2 * t + 8]);
+        const uint32_t l0 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w][kk * 16 + 2 * t]);
+        const uint32_t l1 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w + 8][kk * 16 + 2 * t]);
+        const uint32_t l2 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w][kk * 16 + 2 * t + 8]);
+        const uint32_t l3 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w + 8][kk * 16 + 2 * t + 8]);
+#pragma unroll
+        for (int nt = 0; nt < NTO; nt++) {
+          mma_bf16(o_acc[mt][nt], h0, h1, h2, h3, bv[nt][0], bv[nt][1]);
+          mma_bf16(o_acc[mt][nt], l0, l1, l2, l3, bv[nt][0], bv[nt][1]);
+        }
+      }
+    }
+  }
+
+  // publish this split's partial (empty splits publish nothing: the merge stops at the last non-empty one)
+  const size_t group = ((size_t)b * a.Hkv + kvh) * a.qblocks + qb;
+  float* mine = a.part + (group * a.nsplit + split) * (size_t)NQ * (D + AT_PAD);
+  if (active) {
+#pragma unroll
+    for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+      for (int nt = 0; nt < NTO; nt++)
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const int qi = mt * 16 + g + h * 8;
+          if (qi < nq) {
+            const int d = warp * DW + nt * 8 + 2 * t;
+            __stcg(reinterpret_cast<float2*>(mine + (size_t)qi * (D + AT_PAD) + d),
+                   make_float2(o_acc[mt][nt][2 * h], o_acc[mt][nt][2 * h + 1]));
+          }
+        }
+    for (int i = tid; i < nq; i += AT_THREADS) {
+      __stcg(mine + (size_t)i * (D + AT_PAD) + D, sm.m[i]);
+      __stcg(mine + (size_t)i * (D + AT_PAD) + D + 1, sm.l[i]);
+    }
   }
   __threadfence();
   __syncthreads();
@@ -228,49 +491,107 @@ attn_kernel(AttnArgs a) {
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
-  // merge the splits in split order: warp w takes query vectors w, w+4, ...; lane owns D/32 dims
-  {
-    const int warp = tid >> 5, lane = tid & 31;
-    constexpr int DPL = D / 32;
-    int used = a.nsplit;
-    while (used > 1 && (used - 1) * a.kpc >= kv_len) used--;
-    for (int i = warp; i < nq; i += AT_THREADS / 32) {
-      float mx = -INFINITY;
-      for (int s0 = lane; s0 < used; s0 += 32)
-        mx = fmaxf(mx, __ldcg(a.part + ((group * a.nsplit + s0) * NQ + i) * (D + 2) + D));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      float L = 0.f, O[DPL];
-#pragma unroll
-      for (int e = 0; e < DPL; e++) O[e] = 0.f;
-#pragma unroll 4
-      for (int s = 0; s < used; s++) {
-        const float* p = a.part + ((group * a.nsplit + s) * NQ + i) * (D + 2);
-        const float ms = __ldcg(p + D);
-        const float ls = __ldcg(p + D + 1);
-        float v[DPL];
-#pragma unroll
-        for (int e = 0; e < DPL; e++) v[e] = __ldcg(p + lane + 32 * e);
-        const float w = (ms == -INFINITY || mx == -INFINITY) ? 0.f : expf(ms - mx);
-        L = fmaf(ls, w, L);
-#pragma unroll
-        for (int e = 0; e < DPL; e++) O[e] = fmaf(v[e], w, O[e]);
-      }
-      const int row = r0 + (q0 + i) / G, head = kvh * G + (q0 + i) % G;
-#pragma unroll
-      for (int e = 0; e < DPL; e++)
-        a.out[((size_t)row * a.Hq + head) * D + lane + 32 * e] = to_bf(L > 0.f ? __fdiv_rn(O[e], L) : 0.f);
+  // merge the splits in split order. Pass 1: per query vector, the max over splits and the split weights
+  // w_s = exp(m_s - max) (one warp per vector, lane per split); pass 2: every thread owns (vector, 4 dims)
+  // and sums its splits in order with all loads issued first.
+  int used = a.nsplit;
+  while (used > 1 && (used - 1) * a.kpc >= kv_len) used--;
+  if (nq == 0) {
+    if (tid == 0) a.counters[group] = 0u;
+    return;
+  }
+  float* L = &sm.alpha[0];  // reuse: per-vector denominators
+  if (used <= AT_MW) {
+    // every (vector, split) max and sum loaded at once into shared memory (mw: maxima then weights, s: sums)
+    for (int job = tid; job < nq * used; job += AT_THREADS) {
+      const int i = job / used, sp = job % used;
+      const float* p = a.part + ((group * a.nsplit + sp) * NQ + i) * (D + AT_PAD);
+      sm.mw[i][sp] = __ldcg(p + D);
+      sm.s[i][sp] = __ldcg(p + D + 1);
     }
+    __syncthreads();
+  }
+  for (int i = warp; i < nq; i += AT_THREADS / 32) {
+    auto m_of = [&](int sp) {
+      return used <= AT_MW ? sm.mw[i][sp] : __ldcg(a.part + ((group * a.nsplit + sp) * NQ + i) * (D + AT_PAD) + D);
+    };
+    auto l_of = [&](int sp) {
+      return used <= AT_MW ? sm.s[i][sp] : __ldcg(a.part + ((group * a.nsplit + sp) * NQ + i) * (D + AT_PAD) + D + 1);
+    };
+    float mx = -INFINITY;
+    for (int s0 = lane; s0 < used; s0 += 32) mx = fmaxf(mx, m_of(s0));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float lsum = 0.f;
+    // weights of 32 splits per pass (lane per split); the denominator adds them in split order
+    for (int s0 = 0; s0 < used; s0 += 32) {
+      const int sp = s0 + lane;
+      float w = 0.f, ls = 0.f;
+      if (sp < used) {
+        const float ms = m_of(sp);
+        ls = l_of(sp);
+        w = (ms == -INFINITY || mx == -INFINITY) ? 0.f : expf(ms - mx);
+      }
+      __syncwarp();
+      if (sp < AT_MW) sm.mw[i][sp] = w;
+      for (int t = 0; t < 32 && s0 + t < used; t++) {
+        const float wt = __shfl_sync(0xffffffffu, w, t), lt = __shfl_sync(0xffffffffu, ls, t);
+        lsum = fmaf(lt, wt, lsum);
+      }
+    }
+    if (lane == 0) {
+      L[i] = lsum;
+      sm.m[i] = mx;
+    }
+  }
+  __syncthreads();
+  constexpr int C4 = D / 4;
+  for (int job = tid; job < nq * C4; job += AT_THREADS) {
+    const int i = job / C4, d4 = (job % C4) * 4;
+    const float mx = sm.m[i];
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < used; s0 += 8) {
+      float4 v[8];
+      float ms[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        if (s0 + j < used) {
+          const float* p = a.part + ((group * a.nsplit + s0 + j) * NQ + i) * (D + AT_PAD);
+          v[j] = __ldcg(reinterpret_cast<const float4*>(p + d4));
+          ms[j] = s0 + j < AT_MW ? 0.f : __ldcg(p + D);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        if (s0 + j < used) {
+          const int s = s0 + j;
+          const float w = s < AT_MW ? sm.mw[i][s]
+                                    : ((ms[j] == -INFINITY || mx == -INFINITY) ? 0.f : expf(ms[j] - mx));
+          o.x = fmaf(v[j].x, w, o.x);
+          o.y = fmaf(v[j].y, w, o.y);
+          o.z = fmaf(v[j].z, w, o.z);
+          o.w = fmaf(v[j].w, w, o.w);
+        }
+      }
+    }
+    const float den = L[i];
+    const int row = r0 + (q0 + i) / G, head = kvh * G + (q0 + i) % G;
+    uint16_t* dst = a.out + ((size_t)row * a.Hq + head) * D + d4;
+    dst[0] = to_bf(den > 0.f ? __fdiv_rn(o.x, den) : 0.f);
+    dst[1] = to_bf(den > 0.f ? __fdiv_rn(o.y, den) : 0.f);
+    dst[2] = to_bf(den > 0.f ? __fdiv_rn(o.z, den) : 0.f);
+    dst[3] = to_bf(den > 0.f ? __fdiv_rn(o.w, den) : 0.f);
   }
   if (tid == 0) a.counters[group] = 0u;
 }
 
-template <int D, int NQ>
+template <int D, int NQ, bool FUSED>
 static int launch_attn(const AttnArgs& args, int B, cudaStream_t st) {
-  const size_t smem = sizeof(AttnSmem<D, NQ>);
+  const size_t smem = sizeof(AttnSmem<D, NQ, FUSED>);
   static bool configured = false;  // per instantiation
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel<D, NQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_kernel<D, NQ, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) {
       set_error("attention: cannot reserve %zu bytes of shared memory: %s", smem, cudaGetErrorString(e));
       return IM_CUDA_ERROR;
@@ -278,7 +599,13 @@ static int launch_attn(const AttnArgs& args, int B, cudaStream_t st) {
     configured = true;
   }
   dim3 grid(args.nsplit, args.Hkv, B * args.qblocks);
-  return launch("attn_kernel", attn_kernel<D, NQ>, grid, dim3(AT_THREADS), smem, st, args);
+  return launch("attn_kernel", attn_kernel<D, NQ, FUSED>, grid, dim3(AT_THREADS), smem, st, args);
+}
+
+template <bool FUSED>
+static int dispatch_attn(const AttnArgs& args, int64_t D, int nq, int B, cudaStream_t st) {
+  if (D == 128) return nq == 8 ? launch_attn<128, 8, FUSED>(args, B, st) : launch_attn<128, 32, FUSED>(args, B, st);
+  return nq == 8 ? launch_attn<256, 8, FUSED>(args, B, st) : launch_attn<256, 32, FUSED>(args, B, st);
 }
 
 static void attn_geometry(int64_t rows_per_seq, int64_t G, int* nq, int* qblocks) {
@@ -286,6 +613,13 @@ static void attn_geometry(int64_t rows_per_seq, int64_t G, int* nq, int* qblocks
   *nq = qv <= 8 ? 8 : 32;
   *qblocks = (int)((qv + *nq - 1) / *nq);
 }
+
+// Shared argument checks and setup of both entry points.
+static int attn_setup(const char* who, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* page_table,
+                      int64_t max_pages, const int32_t* seq_rows, const int32_t* seq_slot, const int32_t* row_slot,
+                      const uint64_t* tree_mask, const int32_t* tree_base, int64_t B, int64_t max_rows_per_seq,
+                      int64_t Hq, int64_t Hkv, int64_t D, int64_t max_kv_len, int64_t keys_per_split, int64_t window,
+                      float scale, uint16_t* out, void* workspace, size_t workspace_bytes, AttnArgs* args, int* nq);
 
 }  // namespace im
 
@@ -300,56 +634,100 @@ extern "C" size_t im_attention_workspace_bytes(int64_t B, int64_t max_rows_per_s
   const int64_t nsplit = (max_kv_len + keys_per_split - 1) / keys_per_split;
   const int64_t groups = B * Hkv * qblocks;
   if (groups > AT_MAX_GROUPS) return 0;
-  return AT_COUNTER_BYTES + (size_t)groups * nsplit * nq * (D + 2) * sizeof(float);
+  return AT_COUNTER_BYTES + (size_t)groups * nsplit * nq * (D + AT_PAD) * sizeof(float);
 }
+
+namespace im {
+static int attn_setup(const char* who, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* page_table,
+                      int64_t max_pages, const int32_t* seq_rows, const int32_t* seq_slot, const int32_t* row_slot,
+                      const uint64_t* tree_mask, const int32_t* tree_base, int64_t B, int64_t max_rows_per_seq,
+                      int64_t Hq, int64_t Hkv, int64_t D, int64_t max_kv_len, int64_t keys_per_split, int64_t window,
+                      float scale, uint16_t* out, void* workspace, size_t workspace_bytes, AttnArgs* args, int* nq) {
+  IM_REQUIRE(B >= 1 && max_rows_per_seq >= 1 && Hq >= 1 && Hkv >= 1 && Hq % Hkv == 0, IM_INVALID, "%s: bad sizes",
+             who);
+  IM_REQUIRE(D == 128 || D == 256, IM_UNSUPPORTED, "%s: head_dim %lld", who, (long long)D);
+  IM_REQUIRE(keys_per_split >= AT_KB && keys_per_split % AT_KB == 0, IM_INVALID,
+             "%s: keys_per_split must be a positive multiple of 64", who);
+  IM_REQUIRE(max_kv_len >= 1 && max_kv_len <= max_pages * 16, IM_INVALID, "%s: max_kv_len %lld exceeds the page table",
+             who, (long long)max_kv_len);
+  IM_REQUIRE(k_cache && v_cache && page_table && seq_rows && row_slot && out && workspace, IM_INVALID,
+             "%s: null pointer", who);
+  IM_REQUIRE(!tree_mask || tree_base, IM_INVALID, "%s: tree_mask needs tree_base", who);
+  IM_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(workspace, 256), IM_INVALID,
+             "%s: caches must be 16-byte and the workspace 256-byte aligned", who);
+  const size_t need = im_attention_workspace_bytes(B, max_rows_per_seq, Hq, Hkv, D, max_kv_len, keys_per_split);
+  IM_REQUIRE(need > 0, IM_UNSUPPORTED, "%s: too many (sequence, kv head, query block) groups", who);
+  IM_REQUIRE(workspace_bytes >= need, IM_INVALID, "%s: workspace of %zu bytes needed, %zu given", who, need,
+             workspace_bytes);
+  int qblocks;
+  attn_geometry(max_rows_per_seq, Hq / Hkv, nq, &qblocks);
+  AttnArgs& A = *args;
+  A = AttnArgs{};
+  A.kc = const_cast<uint16_t*>(k_cache);
+  A.vc = const_cast<uint16_t*>(v_cache);
+  A.page_table = page_table;
+  A.seq_rows = seq_rows;
+  A.seq_slot = seq_slot;
+  A.row_slot = row_slot;
+  A.tree_mask = reinterpret_cast<const unsigned long long*>(tree_mask);
+  A.tree_base = tree_base;
+  A.out = out;
+  A.counters = reinterpret_cast<unsigned*>(workspace);
+  A.part = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + AT_COUNTER_BYTES);
+  A.max_pages = (int)max_pages;
+  A.Hq = (int)Hq;
+  A.Hkv = (int)Hkv;
+  A.kpc = (int)keys_per_split;
+  A.nsplit = (int)((max_kv_len + keys_per_split - 1) / keys_per_split);
+  A.qblocks = qblocks;
+  A.window = (int)window;
+  A.scale = scale;
+  return IM_OK;
+}
+}  // namespace im
 
 extern "C" int im_attention_paged(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache,
                                   const int32_t* page_table, int64_t max_pages, const int32_t* seq_rows,
-                                  const int32_t* seq_slot, const int32_t* row_slot, const uint64_t* tree_mask, const int32_t* tree_base,
-                                  int64_t B, int64_t max_rows_per_seq, int64_t Hq, int64_t Hkv, int64_t D,
-                                  int64_t max_kv_len, int64_t keys_per_split, int64_t window, float scale,
-                                  uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+                                  const int32_t* seq_slot, const int32_t* row_slot, const uint64_t* tree_mask,
+                                  const int32_t* tree_base, int64_t B, int64_t max_rows_per_seq, int64_t Hq,
+                                  int64_t Hkv, int64_t D, int64_t max_kv_len, int64_t keys_per_split, int64_t window,
+                                  float scale, uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
   clear_error();
-  IM_REQUIRE(B >= 1 && max_rows_per_seq >= 1 && Hq >= 1 && Hkv >= 1 && Hq % Hkv == 0, IM_INVALID,
-             "im_attention_paged: bad sizes");
-  IM_REQUIRE(D == 128 || D == 256, IM_UNSUPPORTED, "im_attention_paged: head_dim %lld", (long long)D);
-  IM_REQUIRE(keys_per_split >= AT_KB && keys_per_split % AT_KB == 0, IM_INVALID,
-             "im_attention_paged: keys_per_split must be a positive multiple of 64");
-  IM_REQUIRE(max_kv_len >= 1 && max_kv_len <= max_pages * 16, IM_INVALID,
-             "im_attention_paged: max_kv_len %lld exceeds the page table", (long long)max_kv_len);
-  IM_REQUIRE(q && k_cache && v_cache && page_table && seq_rows && row_slot && out && workspace, IM_INVALID,
-             "im_attention_paged: null pointer");
-  IM_REQUIRE(!tree_mask || tree_base, IM_INVALID, "im_attention_paged: tree_mask needs tree_base");
-  IM_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(workspace, 256), IM_INVALID,
-             "im_attention_paged: caches must be 16-byte and the workspace 256-byte aligned");
-  const size_t need = im_attention_workspace_bytes(B, max_rows_per_seq, Hq, Hkv, D, max_kv_len, keys_per_split);
-  IM_REQUIRE(need > 0, IM_UNSUPPORTED, "im_attention_paged: too many (sequence, kv head, query block) groups");
-  IM_REQUIRE(workspace_bytes >= need, IM_INVALID, "im_attention_paged: workspace of %zu bytes needed, %zu given",
-             need, workspace_bytes);
-  int nq, qblocks;
-  attn_geometry(max_rows_per_seq, Hq / Hkv, &nq, &qblocks);
   AttnArgs args;
+  int nq;
+  int rc = attn_setup("im_attention_paged", k_cache, v_cache, page_table, max_pages, seq_rows, seq_slot, row_slot,
+                      tree_mask, tree_base, B, max_rows_per_seq, Hq, Hkv, D, max_kv_len, keys_per_split, window, scale,
+                      out, workspace, workspace_bytes, &args, &nq);
+  if (rc) return rc;
+  IM_REQUIRE(q, IM_INVALID, "im_attention_paged: null q");
   args.q = q;
-  args.kc = k_cache;
-  args.vc = v_cache;
-  args.page_table = page_table;
-  args.seq_rows = seq_rows;
-  args.seq_slot = seq_slot;
-  args.row_slot = row_slot;
-  args.tree_mask = reinterpret_cast<const unsigned long long*>(tree_mask);
-  args.tree_base = tree_base;
-  args.out = out;
-  args.counters = reinterpret_cast<unsigned*>(workspace);
-  args.part = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + AT_COUNTER_BYTES);
-  args.max_pages = (int)max_pages;
-  args.Hq = (int)Hq;
-  args.Hkv = (int)Hkv;
-  args.kpc = (int)keys_per_split;
-  args.nsplit = (int)((max_kv_len + keys_per_split - 1) / keys_per_split);
-  args.qblocks = qblocks;
-  args.window = (int)window;
-  args.scale = scale;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (D == 128) return nq == 8 ? launch_attn<128, 8>(args, (int)B, st) : launch_attn<128, 32>(args, (int)B, st);
-  return nq == 8 ? launch_attn<256, 8>(args, (int)B, st) : launch_attn<256, 32>(args, (int)B, st);
+  return dispatch_attn<false>(args, D, nq, (int)B, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int im_attention_qkv_paged(const uint16_t* qkv, const uint16_t* q_norm, const uint16_t* k_norm,
+                                      const float* inv_freq, const int32_t* row_pos, float eps, int gemma_style,
+                                      uint16_t* k_cache, uint16_t* v_cache, const int32_t* page_table,
+                                      int64_t max_pages, const int32_t* seq_rows, const int32_t* seq_slot,
+                                      const int32_t* row_slot, const uint64_t* tree_mask, const int32_t* tree_base,
+                                      int64_t B, int64_t max_rows_per_seq, int64_t Hq, int64_t Hkv, int64_t D,
+                                      int64_t max_kv_len, int64_t keys_per_split, int64_t window, float scale,
+                                      uint16_t* out, void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  AttnArgs args;
+  int nq;
+  int rc = attn_setup("im_attention_qkv_paged", k_cache, v_cache, page_table, max_pages, seq_rows, seq_slot,
+                      row_slot, tree_mask, tree_base, B, max_rows_per_seq, Hq, Hkv, D, max_kv_len, keys_per_split,
+                      window, scale, out, workspace, workspace_bytes, &args, &nq);
+  if (rc) return rc;
+  IM_REQUIRE(max_rows_per_seq <= AT_MAXNEW, IM_UNSUPPORTED, "im_attention_qkv_paged: at most %d rows per sequence",
+             AT_MAXNEW);
+  IM_REQUIRE(qkv && q_norm && k_norm && inv_freq && row_pos, IM_INVALID, "im_attention_qkv_paged: null pointer");
+  args.qkv = qkv;
+  args.q_norm = q_norm;
+  args.k_norm = k_norm;
+  args.inv_freq = inv_freq;
+  args.row_pos = row_pos;
+  args.eps = eps;
+  args.gemma = gemma_style;
+  return dispatch_attn<true>(args, D, nq, (int)B, reinterpret_cast<cudaStream_t>(stream));
 }

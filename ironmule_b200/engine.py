@@ -14,9 +14,9 @@ of the SwiGLU), down -- plus bf16 norm weights; the tied 4-bit embedding doubles
 Every projection is also held repacked for the packed qGEMM (`kernels.Packed`: 1152-byte units of 32 rows x 64
 inputs in MMA-fragment order), which is what the forward reads.
 
-Forward of M rows (any mix of sequences), six launches per layer: embed (+ each row's sum of squares) -> per
-layer [qkv qGEMM with the input RMSNorm fused into its prologue, q/k norm + RoPE + KV write, paged attention,
-o qGEMM + residual (+ per-tile sums of squares of the new h), gate/up qGEMM with the post-attention RMSNorm
+Forward of M rows (any mix of sequences), five launches per layer: embed (+ each row's sum of squares) -> per
+layer [qkv qGEMM with the input RMSNorm fused into its prologue, paged attention with the q/k norm + RoPE +
+KV write fused into it, o qGEMM + residual (+ per-tile sums of squares of the new h), gate/up qGEMM with the post-attention RMSNorm
 fused + SwiGLU, down qGEMM + residual (+ sums of squares)] -> head qGEMM with the final RMSNorm fused, over the
 leading rows that need logits. Every kernel is row-invariant (no arithmetic depends on M or on the other rows),
 so a verify row's logits equal those of a one-row decode bit for bit, and speculation never changes a greedy
@@ -212,7 +212,6 @@ class QuantModel:
         self.sq_attn = torch.zeros((self.h_tiles, 32), dtype=torch.float32, device=dev)
         self.sq_mlp = torch.zeros((self.h_tiles, 32), dtype=torch.float32, device=dev)
         self.qkv = torch.zeros((r, c.qkv_rows), dtype=bf, device=dev)
-        self.q = torch.zeros((r, c.heads, c.head_dim), dtype=bf, device=dev)
         self.attn = torch.zeros((r, c.heads * c.head_dim), dtype=bf, device=dev)  # [M, Hq, D] packed
         self.act = torch.zeros((r, c.inter), dtype=bf, device=dev)
         self.logits = torch.zeros((self.max_logit_rows, c.vocab), dtype=bf, device=dev)
@@ -251,15 +250,12 @@ class QuantModel:
             kernels.qgemm_packed(h, layer.qkv.p, out=self.qkv, rows=m, norm_sq=sq, norm_parts=parts,
                                  norm_weight=layer.in_norm, eps=c.eps, gemma_norm=gemma, ws=ws)
             glob = c.is_global(li)
-            kernels.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm,
-                                    self.inv_freq if glob else self.inv_freq_local, meta.pos, meta.pos, meta.seq,
-                                    self.page_table, c.heads, c.kv_heads, c.head_dim, c.eps, self.k_cache[li],
-                                    self.v_cache[li], gemma=gemma, q_out=self.q, rows=m)
-            kernels.attention(self.q, self.k_cache[li], self.v_cache[li], self.page_table, meta.seq_rows, meta.pos,
-                              max_rows_per_seq=meta.max_rows_per_seq, max_kv_len=max_kv_len, scale=c.scale,
-                              keys_per_split=self.keys_per_split,
-                              window=0 if glob else c.sliding_window, out=self.attn, rows=m, ws=self.ws_attn,
-                              seq_slot=meta.seq_slot)
+            kernels.attention_qkv(self.qkv, layer.q_norm, layer.k_norm, self.inv_freq if glob else self.inv_freq_local,
+                                  meta.pos, self.k_cache[li], self.v_cache[li], self.page_table, meta.seq_rows,
+                                  meta.pos, hq=c.heads, hkv=c.kv_heads, d=c.head_dim, eps=c.eps, gemma=gemma,
+                                  max_rows_per_seq=meta.max_rows_per_seq, max_kv_len=max_kv_len, scale=c.scale,
+                                  keys_per_split=self.keys_per_split, window=0 if glob else c.sliding_window,
+                                  out=self.attn, rows=m, ws=self.ws_attn, seq_slot=meta.seq_slot)
             kernels.qgemm_packed(self.attn, layer.o.p, epilogue="residual", residual=h, out=h, rows=m,
                                  out_sq=self.sq_attn, ws=ws)
             kernels.qgemm_packed(h, layer.gate_up.p, epilogue="geglu" if gemma else "swiglu", out=self.act, rows=m,
@@ -379,7 +375,7 @@ class SpecDecoder:
 
     def launches_per_round(self) -> int:
         """libimspec kernel launches in one round (counted from the round's structure)."""
-        per_layer = 6
+        per_layer = 5
         def fwd(model, logits):
             return 1 + per_layer * model.cfg.layers + (1 if logits else 0)
         return 1 + self.k * (fwd(self.draft, True) + 1) + fwd(self.target, True) + 1 + 1

@@ -274,6 +274,33 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pag
     return out
 
 
+def attention_qkv(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor, inv_freq: torch.Tensor,
+                  row_pos: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, page_table: torch.Tensor,
+                  seq_rows: torch.Tensor, row_slot: torch.Tensor, *, hq: int, hkv: int, d: int, eps: float,
+                  max_rows_per_seq: int, max_kv_len: int, scale: float, gemma: bool = False,
+                  keys_per_split: int = 64, window: int = 0, tree_mask: torch.Tensor | None = None,
+                  tree_base: torch.Tensor | None = None, out: torch.Tensor | None = None, rows: int | None = None,
+                  ws: torch.Tensor | None = None, seq_slot: torch.Tensor | None = None) -> torch.Tensor:
+    """Attention from the packed qkv projection rows [M, (Hq + 2 Hkv) D]: q/k RMSNorm + RoPE and the K/V cache
+    write happen inside the kernel; returns out [M, Hq, D] (bf16)."""
+    if qkv.dtype != torch.bfloat16 or not qkv.is_contiguous():
+        raise TypeError("qkv must be a contiguous bf16 tensor")
+    m = qkv.shape[0] if rows is None else rows
+    b = seq_rows.numel() - 1
+    out = torch.empty((m, hq, d), dtype=torch.bfloat16, device=qkv.device) if out is None else out
+    need = attention_workspace_bytes(b, max_rows_per_seq, hq, hkv, d, max_kv_len, keys_per_split)
+    if need == 0:
+        raise ValueError("attention shape not supported")
+    ws_ptr, ws_bytes = _scratch(ws, qkv.device, need, "attention")
+    _lib.call("im_attention_qkv_paged", qkv.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(), inv_freq.data_ptr(),
+              row_pos.data_ptr(), float(eps), int(gemma), k_cache.data_ptr(), v_cache.data_ptr(),
+              page_table.data_ptr(), page_table.shape[-1], seq_rows.data_ptr(), _ptr_or_none(seq_slot),
+              row_slot.data_ptr(), _ptr_or_none(tree_mask), _ptr_or_none(tree_base), b, max_rows_per_seq, hq, hkv,
+              d, max_kv_len, keys_per_split, window, float(scale), out.data_ptr(), ws_ptr, ws_bytes,
+              _stream(qkv.device))
+    return out
+
+
 def spec_prepare(hist, n, target, b: int, k: int, slot_cap: int, d0_tok, d0_pos, d_pos, v_tok, v_pos) -> None:
     _lib.call("im_spec_prepare", hist.data_ptr(), hist.shape[-1], n.data_ptr(), target.data_ptr(), b, k, slot_cap,
               d0_tok.data_ptr(), d0_pos.data_ptr(), d_pos.data_ptr() if d_pos is not None else None,

@@ -147,6 +147,55 @@ def test_attention_tree_mask(cuda):
     assert err.max() <= 1e-2 * np.abs(bf16.to_f32(want)).max() + 1e-3
 
 
+@pytest.mark.parametrize("d,hq,hkv,rows,window,kpc,tree,gemma", [
+    (128, 32, 8, 5, 0, 64, False, False), (128, 16, 8, 2, 0, 64, False, False), (128, 4, 1, 32, 0, 128, False, False),
+    (256, 16, 8, 5, 100, 64, False, True), (128, 8, 2, 6, 0, 64, True, False)])
+def test_fused_attention_equals_rope_then_attention(cuda, d, hq, hkv, rows, window, kpc, tree, gemma):
+    """im_attention_qkv_paged == im_qk_norm_rope_kv + im_attention_paged, bit for bit: outputs and the K/V it
+    writes. The fused path must not read the new rows' slots from the cache, so they start as garbage there."""
+    rng = np.random.default_rng(d + hq + rows + 7 * tree)
+    b, max_pages = 3, 48
+    lens = [700, 130, 17 + rows]
+    table = rng.permutation(b * max_pages).reshape(b, max_pages).astype(np.int32)
+    shape = (b * max_pages, hkv, 16, d)
+    kc0, vc0 = rand_bits(rng, shape), rand_bits(rng, shape)
+    m = b * rows
+    qkv = rand_bits(rng, (m, (hq + 2 * hkv) * d))
+    qn, kn = rand_bits(rng, (d,), 0.5), rand_bits(rng, (d,), 0.5)
+    inv_freq = torch.from_numpy((1e6 ** (-2.0 * np.arange(d // 2) / d)).astype(np.float32)).to(cuda)
+    slots = np.concatenate([np.arange(n - rows, n) for n in lens]).astype(np.int32)
+    pos = slots.copy()
+    masks = tb = None
+    if tree:  # rows are draft-tree nodes: a chain per sequence off node 0, RoPE positions by depth
+        parents = [-1] + list(range(rows - 1))
+        mk = []
+        for i in range(rows):
+            mm, j = 0, i
+            while j >= 0:
+                mm |= 1 << j
+                j = parents[j]
+            mk.append(mm)
+        masks = torch.tensor(mk * b, dtype=torch.int64, device=cuda)
+        tb = torch.tensor([n - rows for n in lens], dtype=torch.int32, device=cuda)
+        pos = np.concatenate([np.arange(n - rows, n) - 3 for n in lens]).astype(np.int32)
+    seq_rows = torch.arange(0, m + 1, rows, dtype=torch.int32, device=cuda)
+    row_seq = torch.arange(b, dtype=torch.int32, device=cuda).repeat_interleave(rows)
+    tbl, sl, ps = torch.from_numpy(table).to(cuda), torch.from_numpy(slots).to(cuda), torch.from_numpy(pos).to(cuda)
+    qkv_t, qn_t, kn_t = bf16_bits_to_torch(qkv, cuda), bf16_bits_to_torch(qn, cuda), bf16_bits_to_torch(kn, cuda)
+    kw = dict(max_rows_per_seq=rows, max_kv_len=max_pages * 16, scale=d ** -0.5, keys_per_split=kpc, window=window,
+              tree_mask=masks, tree_base=tb)
+    kc_a, vc_a = bf16_bits_to_torch(kc0, cuda), bf16_bits_to_torch(vc0, cuda)
+    q = kernels.qk_norm_rope_kv(qkv_t, qn_t, kn_t, inv_freq, ps, sl, row_seq, tbl, hq, hkv, d, 1e-6, kc_a, vc_a,
+                                gemma=gemma)
+    want = kernels.attention(q, kc_a, vc_a, tbl, seq_rows, sl, **kw)
+    kc_b, vc_b = bf16_bits_to_torch(kc0, cuda), bf16_bits_to_torch(vc0, cuda)
+    got = kernels.attention_qkv(qkv_t, qn_t, kn_t, inv_freq, ps, kc_b, vc_b, tbl, seq_rows, sl, hq=hq, hkv=hkv, d=d,
+                                eps=1e-6, gemma=gemma, **kw)
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    assert torch.equal(kc_a.view(torch.int16), kc_b.view(torch.int16))
+    assert torch.equal(vc_a.view(torch.int16), vc_b.view(torch.int16))
+
+
 def tiny(name="tiny-target", seed=0, **kw):
     return engine.QuantModel(engine.PRESETS[name], "cuda", seed=seed, max_ctx=256, **kw)
 
