@@ -304,17 +304,37 @@ class SpecStats:
     accepted: int = 0
 
 
+@dataclass(frozen=True)
+class Sampling:
+    """Stochastic speculative decoding: temperature, top-p, and the Philox seed of the whole run."""
+    temperature: float = 0.7
+    top_p: float = 0.95
+    seed: int = 0
+
+
+DRAFT_DRAW = 1000  # Philox draw of draft pass i is DRAFT_DRAW + i; acceptance uses draws 0 .. 2k
+
+
 class SpecDecoder:
-    """Greedy speculative decoding of `batch` sequences with `k` drafts per round, the round on the device.
+    """Speculative decoding of `batch` sequences with `k` drafts per round, the round on the device.
 
     Each sequence slot b holds its committed tokens on the device. A round is: prepare the row buffers; draft
     pass 0 (the last two committed tokens) and passes 1..k-1 (one draft each) through the draft model, each
-    followed by a device argmax that writes the next draft straight into the verify rows; one verify forward of
-    the target over k+1 rows per sequence; greedy acceptance on the device; commit. `capture()` records one
-    round as a CUDA graph; `run_rounds(n)` replays it n times with no host synchronisation.
+    followed by a device pick that writes the next draft straight into the verify rows; one verify forward of
+    the target over k+1 rows per sequence; acceptance on the device; commit. `capture()` records one round as a
+    CUDA graph; `run_rounds(n)` replays it n times with no host synchronisation.
+
+    Greedy (sampling=None): the picks are argmaxes and acceptance keeps the drafts equal to the target's argmax
+    (the reference's rule, ironmule/speculation.py:103-108). Stochastic (sampling=Sampling(...)): draft i of
+    sequence b is sampled from the draft's temperature/top-p distribution with Philox (seed, offset = round,
+    stream = b, draw = DRAFT_DRAW + i), the draft distributions are kept, and acceptance is the p/q rejection
+    rule with residual resampling on draws 0 .. 2k of the same stream -- so a round is reproducible from
+    (seed, round) and its decisions can be replayed on the CPU. The reference has no stochastic path (its
+    product refuses sampling, ironmule_product/worker.py:485-486).
     """
 
-    def __init__(self, target: QuantModel, draft: QuantModel, *, k: int = 4, batch: int = 1):
+    def __init__(self, target: QuantModel, draft: QuantModel, *, k: int = 4, batch: int = 1,
+                 sampling: Sampling | None = None):
         if target.cfg.vocab != draft.cfg.vocab:
             raise ValueError("draft and target must share a vocabulary")
         if batch > min(target.max_seqs, draft.max_seqs):
@@ -348,6 +368,14 @@ class SpecDecoder:
         self.seq_v = ar.repeat_interleave(k + 1)
         self.rows_v = torch.arange(0, b * (k + 1) + 1, k + 1, **i32)
         self.ws_verify = kernels.workspace(kernels.argmax_workspace_bytes(b * (k + 1), target.cfg.vocab), dev)
+        self.sampling = sampling
+        if sampling is not None:
+            v = target.cfg.vocab
+            self.dlog = torch.zeros((k, b, v), dtype=torch.bfloat16, device=dev)  # draft pass i's logits per sequence
+            self.offset = torch.zeros((1,), dtype=torch.int64, device=dev)         # rounds so far (the Philox offset)
+            self.streams = torch.arange(b, dtype=torch.int32, device=dev)
+            self.ws_draw = kernels.workspace(kernels.sampling_workspace_bytes(b), dev)
+            self.ws_accept = kernels.workspace(kernels.sampling_workspace_bytes(b * (2 * k + 1)), dev)
         self.graph: torch.cuda.CUDAGraph | None = None
         self.gpu_launches_per_round = 0
 
@@ -361,24 +389,46 @@ class SpecDecoder:
         # both: its cost is the weight stream, not the rows)
         meta = RowMeta(self.d0_tok, 1, self.d0_pos, self.seq_d0, self.rows_d0, 2 * b, 2)
         logits = d.forward(meta, max_kv_len=slot_cap, logit_rows=2 * b)
-        kernels.argmax_rows(logits[1:], out=self.v_tok[1:], out_stride=k + 1, ws=d.ws_argmax, rows=b,
-                            ld=2 * d.cfg.vocab)
+        self._pick(0, logits[1:], 2 * d.cfg.vocab)
         for i in range(1, k):
             meta = RowMeta(self.v_tok[i:], k + 1, self.d_pos[i - 1], self.seq_d, self.rows_d, b, 1)
             logits = d.forward(meta, max_kv_len=slot_cap, logit_rows=b)
-            kernels.argmax_rows(logits, out=self.v_tok[i + 1:], out_stride=k + 1, ws=d.ws_argmax, rows=b)
+            self._pick(i, logits, d.cfg.vocab)
         meta = RowMeta(self.v_tok, 1, self.v_pos, self.seq_v, self.rows_v, b * (k + 1), k + 1)
         logits = t.forward(meta, max_kv_len=slot_cap, logit_rows=b * (k + 1))
-        kernels.verify_greedy(logits, self.v_tok[1:], b=b, k=k, drafts_ld=k + 1, tokens=self.out_tokens,
-                              count=self.out_count, ws=self.ws_verify)
+        if self.sampling is None:
+            kernels.verify_greedy(logits, self.v_tok[1:], b=b, k=k, drafts_ld=k + 1, tokens=self.out_tokens,
+                                  count=self.out_count, ws=self.ws_verify)
+        else:
+            sp = self.sampling
+            kernels.accept_stochastic(logits, self.dlog, self.v_tok[1:], b=b, k=k, drafts_ld=k + 1,
+                                      temperature=sp.temperature, top_p=sp.top_p, seed=sp.seed,
+                                      offset_dev=self.offset, tokens=self.out_tokens, count=self.out_count,
+                                      ws=self.ws_accept)
+            self.offset.add_(1)
         kernels.spec_commit(self.hist, self.n, self.target_len, b, k, self.out_tokens, self.out_count, self.stats)
+
+    def _pick(self, i: int, logits: torch.Tensor, ld: int) -> None:
+        """Draft i of every sequence from the draft logits rows (row b at logits[b * ld]) into the verify rows."""
+        b, k = self.batch, self.k
+        if self.sampling is None:
+            kernels.argmax_rows(logits, out=self.v_tok[i + 1:], out_stride=k + 1, ws=self.draft.ws_argmax, rows=b,
+                                ld=ld)
+            return
+        v = self.draft.cfg.vocab
+        self.dlog[i].copy_(logits.as_strided((b, v), (ld, 1)))
+        sp = self.sampling
+        kernels.sample_rows(self.dlog[i], sp.temperature, sp.top_p, sp.seed, offset_dev=self.offset,
+                            streams=self.streams, draw=DRAFT_DRAW + i, out=self.v_tok[i + 1:], out_stride=k + 1,
+                            rows=b, ws=self.ws_draw)
 
     def launches_per_round(self) -> int:
         """libimspec kernel launches in one round (counted from the round's structure)."""
         per_layer = 5
         def fwd(model, logits):
             return 1 + per_layer * model.cfg.layers + (1 if logits else 0)
-        return 1 + self.k * (fwd(self.draft, True) + 1) + fwd(self.target, True) + 1 + 1
+        pick, accept = (1, 1) if self.sampling is None else (2, 3)  # argmax | row distributions + sample
+        return 1 + self.k * (fwd(self.draft, True) + pick) + fwd(self.target, True) + accept + 1
 
     # ---- state ------------------------------------------------------------------------------------------
     def start(self, prompts: list[torch.Tensor], max_new: int) -> None:
@@ -396,6 +446,8 @@ class SpecDecoder:
             self.target.prefill(p[:-1].to(torch.int32), seq=b)
             self.draft.prefill(p[:-1].to(torch.int32), seq=b)
         self.stats.zero_()
+        if self.sampling is not None:
+            self.offset.zero_()
 
     def capture(self) -> None:
         """Record one round as a CUDA graph (after one eager round has loaded every kernel)."""
