@@ -186,6 +186,15 @@ int im_quantize_w4g64(const uint16_t* w, int64_t N, int64_t K, uint32_t* wq, uin
  */
 int im_rmsnorm(const uint16_t* x, int64_t ldx, const uint16_t* weight, uint16_t* out, int64_t M, int64_t H,
                float eps, int gemma_style, void* stream);
+/*
+ * Gemma-3's post-attention / post-feedforward norm fused with its residual add: per row m < M,
+ * h[m] = bf16(h[m] + bf16((y[m] * inv_rms(y[m])) * w')), w' = 1 + weight (gemma_style) or weight, and, when
+ * out_sq != NULL (M <= 32), out_sq[m] = the sum of squares of the new h[m] for the RMSNorm that the next
+ * im_qgemm_packed fuses (norm_parts = 1). y, h [M, H] bf16. Replaces the post_attention_layernorm /
+ * post_feedforward_layernorm steps of the Gemma-3 decode layer (ironmule/paired_research.py:177-215).
+ */
+int im_rmsnorm_residual(const uint16_t* y, const uint16_t* weight, uint16_t* h, int64_t M, int64_t H, float eps,
+                        int gemma_style, float* out_sq, void* stream);
 
 /*
  * The per-head step between the qkv projection and attention, fused: for each row m of the packed projection

@@ -48,6 +48,36 @@ rmsnorm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, u
   }
 }
 
+// Gemma-3's output norms: h[m] = bf16(h + bf16((y * inv_rms(y)) * (1 + w))) (w' = w for Qwen3-style weights),
+// and out_sq[m] = the new row's sum of squares (block order: thread sums, warp xor-trees, warps in order) for the
+// RMSNorm that the next qGEMM fuses. One CTA per row.
+__global__ void __launch_bounds__(LN_THREADS)
+rmsnorm_residual_kernel(const uint16_t* __restrict__ y, const uint16_t* __restrict__ w, uint16_t* __restrict__ h,
+                        int H, float eps, int gemma, float* __restrict__ out_sq) {
+  __shared__ float sh[LN_THREADS / 32];
+  pdl_wait();
+  pdl_trigger();
+  const uint16_t* yr = y + (size_t)blockIdx.x * H;
+  uint16_t* hr = h + (size_t)blockIdx.x * H;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += LN_THREADS) {
+    const float v = bf(yr[i]);
+    ss = fmaf(v, v, ss);
+  }
+  const float total = block_sum_256(ss, sh);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(total, (float)H) + eps));
+  float s2 = 0.f;
+  for (int i = threadIdx.x; i < H; i += LN_THREADS) {
+    const float wi = gemma ? 1.0f + bf(w[i]) : bf(w[i]);
+    const float o = round_bf((bf(yr[i]) * inv) * wi);
+    const uint16_t hn = to_bf(bf(hr[i]) + o);
+    hr[i] = hn;
+    s2 = fmaf(bf(hn), bf(hn), s2);
+  }
+  const float t2 = block_sum_256(s2, sh);
+  if (out_sq && threadIdx.x == 0) out_sq[blockIdx.x] = t2;
+}
+
 // One CTA per (row, head) over the packed qkv row [Hq*D | Hkv*D | Hkv*D]:
 //  q heads: RMSNorm over D with qn, RoPE at the row's position -> q_out[m, h, :]
 //  k heads: RMSNorm with kn, RoPE -> the paged K cache; the matching v head copied to the V cache.
@@ -151,6 +181,17 @@ extern "C" int im_rmsnorm(const uint16_t* x, int64_t ldx, const uint16_t* weight
   IM_REQUIRE(M < (1ll << 31), IM_UNSUPPORTED, "im_rmsnorm: too many rows");
   return launch("rmsnorm_kernel", rmsnorm_kernel, dim3((unsigned)M), dim3(LN_THREADS), 0,
                 reinterpret_cast<cudaStream_t>(stream), x, weight, out, (int)H, (long long)ldx, eps, gemma_style);
+}
+
+extern "C" int im_rmsnorm_residual(const uint16_t* y, const uint16_t* weight, uint16_t* h, int64_t M, int64_t H,
+                                   float eps, int gemma_style, float* out_sq, void* stream) {
+  clear_error();
+  IM_REQUIRE(M >= 0 && H >= 1 && H <= (1 << 20), IM_INVALID, "im_rmsnorm_residual: bad sizes");
+  if (M == 0) return IM_OK;
+  IM_REQUIRE(y && weight && h, IM_INVALID, "im_rmsnorm_residual: null pointer");
+  IM_REQUIRE(!out_sq || M <= 32, IM_INVALID, "im_rmsnorm_residual: row sums of squares cover at most 32 rows");
+  return launch("rmsnorm_residual_kernel", rmsnorm_residual_kernel, dim3((unsigned)M), dim3(LN_THREADS), 0,
+                reinterpret_cast<cudaStream_t>(stream), y, weight, h, (int)H, eps, gemma_style, out_sq);
 }
 
 extern "C" int im_qk_norm_rope_kv(const uint16_t* qkv, const uint16_t* q_norm, const uint16_t* k_norm,

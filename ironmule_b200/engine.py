@@ -14,7 +14,8 @@ of the SwiGLU), down -- plus bf16 norm weights; the tied 4-bit embedding doubles
 Every projection is also held repacked for the packed qGEMM (`kernels.Packed`: 1152-byte units of 32 rows x 64
 inputs in MMA-fragment order), which is what the forward reads.
 
-Forward of M rows (any mix of sequences), five launches per layer: embed (+ each row's sum of squares) -> per
+Forward of M rows (any mix of sequences), five launches per layer (seven for Gemma-3, whose attention and MLP
+outputs get their own RMSNorm before the residual add: o / down store, then im_rmsnorm_residual): embed (+ each row's sum of squares) -> per
 layer [qkv qGEMM with the input RMSNorm fused into its prologue, paged attention with the q/k norm + RoPE +
 KV write fused into it, o qGEMM + residual (+ per-tile sums of squares of the new h), gate/up qGEMM with the post-attention RMSNorm
 fused + SwiGLU, down qGEMM + residual (+ sums of squares)] -> head qGEMM with the final RMSNorm fused, over the
@@ -89,6 +90,8 @@ PRESETS = {
     # small shapes for tests
     "tiny-target": ModelConfig("tiny-target", 256, 2, 4, 2, 128, 512, 1000),
     "tiny-draft": ModelConfig("tiny-draft", 128, 2, 2, 1, 128, 256, 1000),
+    "tiny-gemma": ModelConfig("tiny-gemma", 256, 3, 4, 2, 128, 512, 1000, family="gemma3", sliding_window=16,
+                              global_every=3, query_scale=128 ** -0.5),
 }
 
 
@@ -116,9 +119,11 @@ class Layer:
     gate_up: Linear4
     down: Linear4
     in_norm: torch.Tensor
-    post_norm: torch.Tensor
+    post_norm: torch.Tensor      # the norm before the MLP (Gemma-3: pre_feedforward_layernorm)
     q_norm: torch.Tensor
     k_norm: torch.Tensor
+    post_attn_norm: torch.Tensor | None = None  # Gemma-3: on the attention output before its residual add
+    post_ff_norm: torch.Tensor | None = None    # Gemma-3: on the MLP output before its residual add
 
 
 def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
@@ -183,8 +188,11 @@ class QuantModel:
             gate_up = self._lin(interleave_gate_up(gate, up))
             del gate, up
             down = self._lin(self._rand(gen, c.hidden, c.inter, sigma))
-            self.layers.append(Layer(qkv, o, gate_up, down, self._norm(gen, c.hidden), self._norm(gen, c.hidden),
-                                     self._norm(gen, c.head_dim), self._norm(gen, c.head_dim)))
+            layer = Layer(qkv, o, gate_up, down, self._norm(gen, c.hidden), self._norm(gen, c.hidden),
+                          self._norm(gen, c.head_dim), self._norm(gen, c.head_dim))
+            if c.family == "gemma3":
+                layer.post_attn_norm, layer.post_ff_norm = self._norm(gen, c.hidden), self._norm(gen, c.hidden)
+            self.layers.append(layer)
         self.final_norm = self._norm(gen, c.hidden)
         d = c.head_dim
         idx = torch.arange(0, d // 2, dtype=torch.float64)
@@ -214,6 +222,7 @@ class QuantModel:
         self.qkv = torch.zeros((r, c.qkv_rows), dtype=bf, device=dev)
         self.attn = torch.zeros((r, c.heads * c.head_dim), dtype=bf, device=dev)  # [M, Hq, D] packed
         self.act = torch.zeros((r, c.inter), dtype=bf, device=dev)
+        self.y = torch.zeros((r, c.hidden), dtype=bf, device=dev)  # Gemma-3: projection output before its norm
         self.logits = torch.zeros((self.max_logit_rows, c.vocab), dtype=bf, device=dev)
         # scratch: one buffer per kernel family, sized for the largest call this model makes
         q_need = max(kernels.qgemm_packed_workspace_bytes(min(r, MAX_QGEMM_ROWS), n, k)
@@ -256,9 +265,20 @@ class QuantModel:
                                   max_rows_per_seq=meta.max_rows_per_seq, max_kv_len=max_kv_len, scale=c.scale,
                                   keys_per_split=self.keys_per_split, window=0 if glob else c.sliding_window,
                                   out=self.attn, rows=m, ws=self.ws_attn, seq_slot=meta.seq_slot)
+            if gemma:  # Gemma-3: output norms before each residual add; one sum-of-squares part per row
+                kernels.qgemm_packed(self.attn, layer.o.p, out=self.y, rows=m, ws=ws)
+                kernels.rmsnorm_residual(self.y, layer.post_attn_norm, h, c.eps, gemma=True, rows=m,
+                                         out_sq=self.sq_attn)
+                kernels.qgemm_packed(h, layer.gate_up.p, epilogue="geglu", out=self.act, rows=m, norm_sq=self.sq_attn,
+                                     norm_parts=1, norm_weight=layer.post_norm, eps=c.eps, gemma_norm=True, ws=ws)
+                kernels.qgemm_packed(self.act, layer.down.p, out=self.y, rows=m, ws=ws)
+                kernels.rmsnorm_residual(self.y, layer.post_ff_norm, h, c.eps, gemma=True, rows=m,
+                                         out_sq=self.sq_mlp)
+                sq, parts = self.sq_mlp, 1
+                continue
             kernels.qgemm_packed(self.attn, layer.o.p, epilogue="residual", residual=h, out=h, rows=m,
                                  out_sq=self.sq_attn, ws=ws)
-            kernels.qgemm_packed(h, layer.gate_up.p, epilogue="geglu" if gemma else "swiglu", out=self.act, rows=m,
+            kernels.qgemm_packed(h, layer.gate_up.p, epilogue="swiglu", out=self.act, rows=m,
                                  norm_sq=self.sq_attn, norm_parts=self.h_tiles, norm_weight=layer.post_norm,
                                  eps=c.eps, gemma_norm=gemma, ws=ws)
             kernels.qgemm_packed(self.act, layer.down.p, epilogue="residual", residual=h, out=h, rows=m,
@@ -424,8 +444,8 @@ class SpecDecoder:
 
     def launches_per_round(self) -> int:
         """libimspec kernel launches in one round (counted from the round's structure)."""
-        per_layer = 5
         def fwd(model, logits):
+            per_layer = 7 if model.cfg.family == "gemma3" else 5
             return 1 + per_layer * model.cfg.layers + (1 if logits else 0)
         pick, accept = (1, 1) if self.sampling is None else (2, 3)  # argmax | row distributions + sample
         return 1 + self.k * (fwd(self.draft, True) + pick) + fwd(self.target, True) + accept + 1

@@ -220,6 +220,16 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, *, gemma: bool = 
     return out
 
 
+def rmsnorm_residual(y: torch.Tensor, weight: torch.Tensor, h: torch.Tensor, eps: float, *, gemma: bool = False,
+                     rows: int | None = None, out_sq: torch.Tensor | None = None) -> torch.Tensor:
+    """h += rmsnorm(y) * w' per row, in place (Gemma-3's output norms); out_sq gets the new rows' sums of squares."""
+    hsz = h.shape[-1]
+    m = h.numel() // hsz if rows is None else rows
+    _lib.call("im_rmsnorm_residual", y.data_ptr(), weight.data_ptr(), h.data_ptr(), m, hsz, float(eps), int(gemma),
+              _ptr_or_none(out_sq), _stream(h.device))
+    return h
+
+
 def qk_norm_rope_kv(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor, inv_freq: torch.Tensor,
                     row_pos: torch.Tensor, row_slot: torch.Tensor, row_seq: torch.Tensor, page_table: torch.Tensor,
                     hq: int, hkv: int, d: int, eps: float, k_cache: torch.Tensor, v_cache: torch.Tensor, *,

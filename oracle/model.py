@@ -8,6 +8,7 @@ Layer math (numpy, float32 with bf16 rounding at every op boundary, float64 atte
   swiglu        bf16(bf16(a * bf16(sigmoid(a))) * u), a = bf16(gate), u = bf16(up)
   residual      bf16(h + bf16(y))
   embedding     bf16(scale * q + bias) of the token's row (x bf16(sqrt(H)) for Gemma-3)
+  Gemma-3       RMSNorm of the attention output and of the MLP output ((1 + w) weights) before each residual add
 Projections go through `oracle.qmv.qmv`, the pinned restatement of the reference's qmv arithmetic
 (IronMule ironmule/qmv_k3840.py:62-244). The decode-layer order follows mlx_lm's Qwen3 as the reference's
 runtime drives it (ironmule/runtime.py:505-545) and the Gemma-3 decode step of
@@ -105,6 +106,8 @@ class HostLayer:
     post_norm: np.ndarray
     q_norm: np.ndarray
     k_norm: np.ndarray
+    post_attn_norm: np.ndarray | None = None   # Gemma-3 only
+    post_ff_norm: np.ndarray | None = None
 
 
 class OracleModel:
@@ -132,7 +135,9 @@ class OracleModel:
             return t.view(torch.int16).cpu().numpy().view(np.uint16)
 
         layers = [HostLayer(host_lin(l.qkv), host_lin(l.o), host_lin(l.gate_up), host_lin(l.down), host_vec(l.in_norm),
-                            host_vec(l.post_norm), host_vec(l.q_norm), host_vec(l.k_norm)) for l in model.layers]
+                            host_vec(l.post_norm), host_vec(l.q_norm), host_vec(l.k_norm),
+                            host_vec(l.post_attn_norm) if l.post_attn_norm is not None else None,
+                            host_vec(l.post_ff_norm) if l.post_ff_norm is not None else None) for l in model.layers]
         return cls(model.cfg, host_lin(model.embed), layers, host_vec(model.final_norm),
                    model.inv_freq.cpu().numpy(), model.inv_freq_local.cpu().numpy(), fast=fast)
 
@@ -165,12 +170,17 @@ class OracleModel:
             self.v[li][pos] = v
             att = attention(q_rot, self.k[li], self.v[li], pos, c.scale, 0 if glob else c.sliding_window)
             y = self.proj(*layer.o, att.reshape(m, -1))
+            if gemma:  # Gemma-3: post_attention_layernorm on the attention output
+                y = rmsnorm(y, layer.post_attn_norm, c.eps, gemma)
             h = residual(h, y)
             xn = rmsnorm(h, layer.post_norm, c.eps, gemma)
             gu = self.proj(*layer.gate_up, xn).reshape(m, -1, 2, 16)
             gate, up = gu[:, :, 0, :].reshape(m, -1), gu[:, :, 1, :].reshape(m, -1)
             act = gelu_mul(gate, up) if gemma else silu_mul(gate, up)
-            h = residual(h, self.proj(*layer.down, act))
+            y = self.proj(*layer.down, act)
+            if gemma:  # Gemma-3: post_feedforward_layernorm on the MLP output
+                y = rmsnorm(y, layer.post_ff_norm, c.eps, gemma)
+            h = residual(h, y)
         if not logits:
             return None
         hn = rmsnorm(h, self.final_norm, c.eps, gemma)

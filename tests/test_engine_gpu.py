@@ -218,6 +218,55 @@ def test_tiny_forward_matches_oracle(cuda):
     assert agree.mean() > 0.8
 
 
+def test_rmsnorm_residual_matches_oracle(cuda):
+    rng = np.random.default_rng(11)
+    y, h = rand_bits(rng, (5, 640)), rand_bits(rng, (5, 640))
+    w = rand_bits(rng, (640,), 0.3)
+    ht = bf16_bits_to_torch(h, cuda)
+    sq = torch.zeros(32, dtype=torch.float32, device=cuda)
+    kernels.rmsnorm_residual(bf16_bits_to_torch(y, cuda), bf16_bits_to_torch(w, cuda), ht, 1e-6, gemma=True,
+                             out_sq=sq)
+    want = om.residual(h, om.rmsnorm(y, w, 1e-6, True))
+    got = torch_to_bf16_bits(ht)
+    assert np.mean(got == want) > 0.99
+    assert np.max(np.abs(bf16.to_f32(got) - bf16.to_f32(want))) <= 2 ** -6 * np.max(np.abs(bf16.to_f32(want)))
+    ref = (bf16.to_f32(got).astype(np.float64) ** 2).sum(axis=1)
+    assert np.allclose(sq[:5].cpu().numpy(), ref, rtol=1e-5)
+
+
+def test_tiny_gemma_forward_matches_oracle(cuda):
+    """Gemma-3 shapes: (1 + w) norms, post-attention / post-feedforward norms, sqrt(H) embedding scale, GeGLU,
+    sliding-window layers with the local RoPE base and a global layer."""
+    model = engine.QuantModel(engine.PRESETS["tiny-gemma"], "cuda", seed=4, sigma=0.08, max_ctx=256)
+    assert model.layers[0].post_attn_norm is not None
+    oracle = om.OracleModel.from_device(model)
+    oracle.reset(model.max_ctx)
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, model.cfg.vocab, 28).astype(np.int32)
+    got = torch_to_bf16_bits(model.logits_for(torch.from_numpy(prompt).to(cuda), 0))
+    want = oracle.forward(prompt.tolist(), list(range(28)))
+    a, b = bf16.to_f32(got), bf16.to_f32(want)
+    assert np.max(np.abs(a - b)) <= 2e-2 * np.max(np.abs(b))
+    top2 = np.sort(b, axis=1)[:, -2:]
+    agree = a.argmax(1) == b.argmax(1)
+    assert np.all(agree | (top2[:, 1] - top2[:, 0] < 2e-2 * np.abs(b).max()))
+
+
+def test_gemma_speculation_changes_no_answer(cuda):
+    target = engine.QuantModel(engine.PRESETS["tiny-gemma"], "cuda", seed=4, sigma=0.08, max_ctx=256)
+    draft = engine.QuantModel(engine.PRESETS["tiny-gemma"], "cuda", seed=6, sigma=0.08, max_ctx=256)
+    prompt = torch.randint(0, 1000, (20,), generator=torch.Generator().manual_seed(8)).to(torch.int32).to(cuda)
+    solo = engine.QuantModel(engine.PRESETS["tiny-gemma"], "cuda", seed=4, sigma=0.08, max_ctx=256)
+    plain = engine.greedy_decode(solo, prompt, 30)
+    dec = engine.SpecDecoder(target, draft, k=4)
+    dec.start([prompt], max_new=30)
+    dec.round()
+    dec.capture()
+    while not dec.done():
+        dec.run_rounds(3)
+    assert dec.generated(0, prompt.numel()) == plain
+
+
 def test_verify_rows_equal_one_row_decodes(cuda):
     model = tiny(sigma=0.08)
     rng = np.random.default_rng(4)
