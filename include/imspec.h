@@ -261,6 +261,36 @@ int im_attention_qkv_paged(const uint16_t* qkv, const uint16_t* q_norm, const ui
                            void* stream);
 
 /*
+ * Tree speculation (the reference's speculation is linear, ironmule/speculation.py:39-108,
+ * so these have no reference counterpart beyond its greedy rule). The tree has `levels` levels below the root
+ * with branching branch[0..levels-1] (total nodes <= 63), nodes numbered level by level, children of a node
+ * consecutive. Node j of a sequence with n committed tokens sits in KV slot n + j (tree_base[b] = n) at RoPE
+ * position n - 1 + depth(j); verify row 0 is the root (slot n - 1), row 1 + j node j, with tree_mask bits of the
+ * node's ancestors and itself (im_attention_paged's tree mode).
+ *
+ * im_topk_rows: the k (<= 8) largest of each row (ties: lower index first; NaN lowest), row r's indices at
+ * out[r * out_stride ..]; workspace >= im_topk_workspace_bytes, 256-byte aligned, zero-filled once.
+ * im_tree_prepare: the first draft pass's two re-fed rows (d0_*) and the verify rows' slot, position, mask
+ * (v_*, [B][1 + nodes]; v_tok[b][0] = the root token, node tokens come from im_topk_rows) and tree_base.
+ * im_tree_accept: from the target's argmax of each verify row, the longest path whose node tokens equal the
+ * argmax of their parent's row, then the target's token there: out_tokens [B][levels + 1], out_count [B],
+ * acc_node [B][levels] (accepted node per depth, -1 after).
+ * im_tree_compact: copies the accepted nodes' K/V (depth < max_depth) to slots tree_base + depth, for every layer
+ * of a [layers][pages][Hkv][16][D] cache (layer_stride elements apart).
+ */
+size_t im_topk_workspace_bytes(int64_t rows, int64_t V, int64_t k);
+int im_topk_rows(const uint16_t* logits, int64_t rows, int64_t V, int64_t ld, int64_t k, int32_t* out,
+                 int64_t out_stride, void* workspace, size_t workspace_bytes, void* stream);
+int im_tree_prepare(const int32_t* hist, int64_t cap, const int32_t* n, int64_t B, const int32_t* branch,
+                    int64_t levels, int64_t slot_cap, int32_t* d0_tok, int32_t* d0_pos, int32_t* v_tok, int32_t* v_pos,
+                    int32_t* v_slot, uint64_t* v_mask, int32_t* tree_base, void* stream);
+int im_tree_accept(const int32_t* argmax, const int32_t* v_tok, int64_t B, const int32_t* branch, int64_t levels,
+                   int32_t* out_tokens, int32_t* out_count, int32_t* acc_node, void* stream);
+int im_tree_compact(uint16_t* k_cache, uint16_t* v_cache, int64_t layers, int64_t layer_stride,
+                    const int32_t* page_table, int64_t max_pages, const int32_t* tree_base, const int32_t* acc_node,
+                    int64_t levels, int64_t max_depth, int64_t B, int64_t Hkv, int64_t D, void* stream);
+
+/*
  * Device bookkeeping of one speculative round with k drafts for B sequences (no host round trip).
  * hist int32 [B, cap] holds each sequence's committed tokens, n int32 [B] their count, target int32 [B] the
  * length at which a sequence stops committing; slot_cap = pages * 16 bounds every KV slot.

@@ -41,6 +41,11 @@ SIGNATURES: dict[str, tuple] = {
     "im_qgemm_packed_tune": (_INT, [_INT, _INT, _INT]),
     "im_set_launch_overlap": (_INT, [_INT]),
     "im_rmsnorm_residual": (_INT, [_P, _P, _P, _I64, _I64, ctypes.c_float, _INT, _P, _P]),
+    "im_topk_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
+    "im_topk_rows": (_INT, [_P, _I64, _I64, _I64, _I64, _P, _I64, _P, _SZ, _P]),
+    "im_tree_prepare": (_INT, [_P, _I64, _P, _I64, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "im_tree_accept": (_INT, [_P, _P, _I64, _P, _I64, _P, _P, _P, _P]),
+    "im_tree_compact": (_INT, [_P, _P, _I64, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "im_qgemm_packed": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _INT, _P, _I64, _P, ctypes.c_float, _INT, _P, _P,
                                _SZ, _P]),
     "im_argmax_rows": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _P, _P, _SZ, _P]),

@@ -146,6 +146,9 @@ class RowMeta:
     rows: int
     max_rows_per_seq: int
     seq_slot: torch.Tensor | None = None  # page-table row per sequence group (None: group b is slot b)
+    slot: torch.Tensor | None = None      # KV slot per row when it differs from the position (draft trees)
+    tree_mask: torch.Tensor | None = None  # int64 per row: ancestor bits over the tree slots
+    tree_base: torch.Tensor | None = None  # int32 per sequence group: the first tree slot
 
 
 class QuantModel:
@@ -261,7 +264,8 @@ class QuantModel:
             glob = c.is_global(li)
             kernels.attention_qkv(self.qkv, layer.q_norm, layer.k_norm, self.inv_freq if glob else self.inv_freq_local,
                                   meta.pos, self.k_cache[li], self.v_cache[li], self.page_table, meta.seq_rows,
-                                  meta.pos, hq=c.heads, hkv=c.kv_heads, d=c.head_dim, eps=c.eps, gemma=gemma,
+                                  meta.pos if meta.slot is None else meta.slot, tree_mask=meta.tree_mask,
+                                  tree_base=meta.tree_base, hq=c.heads, hkv=c.kv_heads, d=c.head_dim, eps=c.eps, gemma=gemma,
                                   max_rows_per_seq=meta.max_rows_per_seq, max_kv_len=max_kv_len, scale=c.scale,
                                   keys_per_split=self.keys_per_split, window=0 if glob else c.sliding_window,
                                   out=self.attn, rows=m, ws=self.ws_attn, seq_slot=meta.seq_slot)
@@ -364,6 +368,7 @@ class SpecDecoder:
         if 2 * batch > draft.max_rows or 2 * batch > draft.max_logit_rows:
             raise ValueError("draft pass rows exceed the draft model's limit")
         self.target, self.draft, self.k, self.batch = target, draft, k, batch
+        self.reserve = k  # cache slots a round may write past the committed tokens
         dev = target.device
         self.device = dev
         b = batch
@@ -458,7 +463,7 @@ class SpecDecoder:
             raise ValueError("one prompt per sequence slot")
         for b, p in enumerate(prompts):
             length = p.numel()
-            if length < 2 or length + max_new + self.k + 1 > self.cap:
+            if length < 2 or length + max_new + self.reserve + 1 > self.cap:
                 raise ValueError("prompt too short or too long for the cache")
             self.hist[b, :length] = p.to(torch.int32)
             self.n[b] = length
@@ -527,6 +532,78 @@ class SpecDecoder:
         n = int(self.n[b].item())
         end = min(n, int(self.target_len[b].item()))
         return self.hist[b, prompt_len:end].tolist()
+
+
+class TreeDecoder(SpecDecoder):
+    """Greedy tree speculation of one sequence, the round on the device.
+
+    The draft tree has a static shape: `branch[L]` children per node at depth L + 1 (default 4 x 2 x 2: 4 + 8 +
+    16 = 28 nodes). A round: prepare the rows (im_tree_prepare); draft pass 0 re-feeds the last two committed
+    tokens and its top-branch[0] tokens become depth-1 nodes; each further draft pass runs one level's nodes
+    (tree-masked attention: a node sees the committed prefix and its own ancestors) and its rows' top-k become
+    the next level; one verify forward of the target over the root and every node (1 + 28 = 29 rows); the
+    target's argmax per row and the walk down the tree (im_tree_accept) keep the longest agreeing path plus the
+    target's own token; the accepted nodes' K/V move to the committed slots in both models (im_tree_compact);
+    commit. Every kernel is row-invariant and a node sees exactly its path, so the tokens equal plain greedy
+    decoding's. BASELINE's "16-node ... M=16" cannot describe a 4 x 2 x 2 tree; this build verifies the whole
+    tree (29 rows per sequence, within the 32 rows of one qGEMM call), so one sequence per decoder.
+    """
+
+    def __init__(self, target: QuantModel, draft: QuantModel, *, branch: tuple[int, ...] = (4, 2, 2)):
+        levels = len(branch)
+        counts = [math.prod(branch[:i + 1]) for i in range(levels)]
+        nodes = sum(counts)
+        rows = 1 + nodes
+        if rows > min(target.max_rows, MAX_QGEMM_ROWS, target.max_logit_rows):
+            raise ValueError(f"a {rows}-row tree exceeds the target's per-forward limit")
+        if max(counts[:-1] + [2]) > min(draft.max_rows, draft.max_logit_rows):
+            raise ValueError("a tree level exceeds the draft model's per-forward limit")
+        super().__init__(target, draft, k=levels, batch=1)
+        self.branch, self.counts, self.nodes, self.rows = tuple(branch), counts, nodes, rows
+        self.first = [sum(counts[:i]) for i in range(levels)]
+        self.reserve = nodes
+        dev, i32 = self.device, dict(dtype=torch.int32, device=self.device)
+        self.t_tok = torch.zeros((rows,), **i32)
+        self.t_pos = torch.zeros((rows,), **i32)
+        self.t_slot = torch.zeros((rows,), **i32)
+        self.t_mask = torch.zeros((rows,), dtype=torch.int64, device=dev)
+        self.t_base = torch.zeros((1,), **i32)
+        self.t_argmax = torch.zeros((rows,), **i32)
+        self.acc_node = torch.zeros((levels,), **i32)
+        self.seq_t = torch.zeros((rows,), **i32)
+        self.rows_t = torch.tensor([0, rows], **i32)
+        self.rows_l = [torch.tensor([0, c], **i32) for c in counts]
+        self.ws_topk = kernels.workspace(kernels.topk_workspace_bytes(max(counts), target.cfg.vocab, max(branch)), dev)
+
+    def round(self) -> None:
+        t, d, br = self.target, self.draft, self.branch
+        cap = self.cap
+        kernels.tree_prepare(self.hist, self.n, br, cap, self.d0_tok, self.d0_pos, self.t_tok, self.t_pos, self.t_slot,
+                             self.t_mask, self.t_base)
+        meta = RowMeta(self.d0_tok, 1, self.d0_pos, self.seq_d0, self.rows_d0, 2, 2)
+        logits = d.forward(meta, max_kv_len=cap, logit_rows=2)
+        kernels.topk_rows(logits[1:], br[0], rows=1, out=self.t_tok[1:], ws=self.ws_topk)
+        for lv in range(1, len(br)):
+            s0, cnt = 1 + self.first[lv - 1], self.counts[lv - 1]
+            meta = RowMeta(self.t_tok[s0:], 1, self.t_pos[s0:], self.seq_t, self.rows_l[lv - 1], cnt, cnt,
+                           slot=self.t_slot[s0:], tree_mask=self.t_mask[s0:], tree_base=self.t_base)
+            logits = d.forward(meta, max_kv_len=cap, logit_rows=cnt)
+            kernels.topk_rows(logits, br[lv], rows=cnt, out=self.t_tok[1 + self.first[lv]:], ws=self.ws_topk)
+        meta = RowMeta(self.t_tok, 1, self.t_pos, self.seq_t, self.rows_t, self.rows, self.rows, slot=self.t_slot,
+                       tree_mask=self.t_mask, tree_base=self.t_base)
+        logits = t.forward(meta, max_kv_len=cap, logit_rows=self.rows)
+        kernels.argmax_rows(logits, out=self.t_argmax, ws=t.ws_argmax, rows=self.rows)
+        kernels.tree_accept(self.t_argmax, self.t_tok, 1, br, self.out_tokens, self.out_count, self.acc_node)
+        kernels.tree_compact(t.k_cache, t.v_cache, t.page_table, self.t_base, self.acc_node, len(br), len(br), 1)
+        kernels.tree_compact(d.k_cache, d.v_cache, d.page_table, self.t_base, self.acc_node, len(br), len(br) - 1, 1)
+        kernels.spec_commit(self.hist, self.n, self.target_len, 1, len(br), self.out_tokens, self.out_count,
+                            self.stats)
+
+    def launches_per_round(self) -> int:
+        def fwd(model):
+            return 2 + (7 if model.cfg.family == "gemma3" else 5) * model.cfg.layers
+        levels = len(self.branch)
+        return 1 + levels * (fwd(self.draft) + 1) + fwd(self.target) + 1 + 1 + 2 + 1
 
 
 def greedy_decode(model: QuantModel, prompt: torch.Tensor, max_new: int, seq: int = 0) -> list[int]:

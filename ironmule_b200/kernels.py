@@ -10,6 +10,7 @@ otherwise a shared per-device buffer is used.
 """
 from __future__ import annotations
 
+import ctypes
 import threading
 
 import torch
@@ -361,6 +362,50 @@ def accept_stochastic(target_logits: torch.Tensor, draft_logits: torch.Tensor, d
               _ptr_or_none(offset_dev), tokens.data_ptr(), count.data_ptr(), _ptr_or_none(ratios), ws_ptr,
               ws_bytes, _stream(device))
     return tokens, count
+
+
+def topk_workspace_bytes(rows: int, v: int, k: int) -> int:
+    return int(_lib.load().im_topk_workspace_bytes(rows, v, k))
+
+
+def topk_rows(logits: torch.Tensor, k: int, *, rows: int | None = None, ld: int | None = None,
+              out: torch.Tensor | None = None, out_stride: int | None = None,
+              ws: torch.Tensor | None = None) -> torch.Tensor:
+    """The k largest entries of each row (indices, largest first, ties to the lower index)."""
+    _check(logits, "logits", (torch.bfloat16,))
+    v = logits.shape[-1]
+    ld = v if ld is None else ld
+    rows = logits.numel() // v if rows is None else rows
+    out_stride = k if out_stride is None else out_stride
+    out = torch.empty((rows, k), dtype=torch.int32, device=logits.device) if out is None else out
+    ws_ptr, ws_bytes = _scratch(ws, logits.device, topk_workspace_bytes(rows, v, k), "topk")
+    _lib.call("im_topk_rows", logits.data_ptr(), rows, v, ld, k, out.data_ptr(), out_stride, ws_ptr, ws_bytes,
+              _stream(logits.device))
+    return out
+
+
+def _branch(branch) -> ctypes.Array:
+    return (ctypes.c_int32 * len(branch))(*branch)
+
+
+def tree_prepare(hist, n, branch, slot_cap: int, d0_tok, d0_pos, v_tok, v_pos, v_slot, v_mask, tree_base) -> None:
+    _lib.call("im_tree_prepare", hist.data_ptr(), hist.shape[-1], n.data_ptr(), n.numel(), _branch(branch),
+              len(branch), slot_cap, d0_tok.data_ptr(), d0_pos.data_ptr(), v_tok.data_ptr(), v_pos.data_ptr(),
+              v_slot.data_ptr(), v_mask.data_ptr(), tree_base.data_ptr(), _stream(hist.device))
+
+
+def tree_accept(argmax, v_tok, b: int, branch, out_tokens, out_count, acc_node) -> None:
+    _lib.call("im_tree_accept", argmax.data_ptr(), v_tok.data_ptr(), b, _branch(branch), len(branch),
+              out_tokens.data_ptr(), out_count.data_ptr(), acc_node.data_ptr(), _stream(argmax.device))
+
+
+def tree_compact(k_cache: torch.Tensor, v_cache: torch.Tensor, page_table, tree_base, acc_node, levels: int,
+                 max_depth: int, b: int) -> None:
+    """k_cache / v_cache [layers, pages, Hkv, 16, D]."""
+    layers, _, hkv, _, d = k_cache.shape
+    _lib.call("im_tree_compact", k_cache.data_ptr(), v_cache.data_ptr(), layers, k_cache.stride(0),
+              page_table.data_ptr(), page_table.shape[-1], tree_base.data_ptr(), acc_node.data_ptr(), levels,
+              max_depth, b, hkv, d, _stream(k_cache.device))
 
 
 def philox(seed: int, offset: int, stream_id: int, n: int, device) -> torch.Tensor:
