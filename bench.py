@@ -10,7 +10,15 @@ is committed tokens per second over all ranks (replicas, one independent sequenc
 the data path), timed with CUDA events over K rounds replayed from one captured CUDA graph. Every round
 streams the full 3.6 GB of weights, far more than the 126 MB L2, so no flush is needed.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload spec_decode|verify_step]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload spec_decode|verify_step|stochastic|tree]
+
+--workload stochastic: BASELINE config 3's round -- Qwen3-4B + 0.6B, temperature 0.7, top-p 0.95, k = 4,
+rejection sampling with residual resampling on Philox -- over 6 concurrent sequences with prompt lengths drawn
+uniformly from [128, 2048] (seed 0): 6 x 5 = 30 verify rows, the most one qGEMM call takes (the configuration's
+32 sequences need 160 rows). --workload tree: config 4's tree verification on Gemma-3-12B shapes (48 layers,
+hidden 3840, 16/8 heads, head_dim 256, GeGLU 15360, vocab 262144) with a Gemma-3-1B-shaped draft, a 4 x 2 x 2
+draft tree verified as root + 28 nodes = 29 rows, one sequence, a 1024-token prompt.
 
 --impl reference times the CPU implementation of the same round (the oracle port in oracle/spec.py: the
 reference's greedy round with projections dequantised and dotted in float32 by OpenMP C code) on the box's host
@@ -42,7 +50,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["spec_decode", "verify_step"], default="spec_decode")
+    ap.add_argument("--workload", choices=["spec_decode", "verify_step", "stochastic", "tree"], default="spec_decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -424,6 +432,81 @@ def run_verify_step(args, world: int, rank: int, local: int) -> None:
         print(json.dumps(line), flush=True)
 
 
+def run_rounds_workload(args, world: int, rank: int, local: int, kind: str) -> None:
+    """Config 3 (stochastic, batched) or config 4 (tree) rounds: timed like the default workload."""
+    import torch
+
+    from ironmule_b200.engine import PRESETS, QuantModel, Sampling, SpecDecoder, TreeDecoder
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pk = peaks()
+    gen = torch.Generator().manual_seed(rank)
+    if kind == "stochastic":
+        b, ctx = 6, 2048 + 256
+        lens = torch.randint(128, 2049, (b,), generator=gen).tolist()
+        target = QuantModel(PRESETS["qwen3-4b"], device, seed=0, max_ctx=ctx, max_seqs=b, max_rows=32,
+                            max_logit_rows=32)
+        draft = QuantModel(PRESETS["qwen3-0.6b"], device, seed=1, max_ctx=ctx, max_seqs=b, max_rows=16,
+                           max_logit_rows=16)
+        dec = SpecDecoder(target, draft, k=K_DRAFTS, batch=b, sampling=Sampling(0.7, 0.95, 0))
+        prompts = [torch.randint(0, target.cfg.vocab, (n,), generator=gen, dtype=torch.int32) for n in lens]
+        round_bytes = K_DRAFTS * draft.cfg.weight_bytes() + target.cfg.weight_bytes()
+        workload = ("BASELINE config 3: stochastic speculative decoding (T 0.7, top-p 0.95, k 4, rejection sampling "
+                    "with residual resample on Philox), Qwen3-4B + Qwen3-0.6B 4-bit, 6 sequences (30 verify rows; "
+                    "the configuration's 32 need 160 rows per qGEMM call), prompts U[128, 2048]")
+        metric = "accepted tokens/s (stochastic spec decode, Qwen3-4B + 0.6B, k=4, 6 sequences)"
+    else:
+        ctx = 1024 + 128 + 64
+        target = QuantModel(PRESETS["gemma3-12b"], device, seed=0, max_ctx=ctx, max_rows=32, max_logit_rows=32)
+        draft = QuantModel(PRESETS["gemma3-1b"], device, seed=1, max_ctx=ctx, max_rows=32, max_logit_rows=32)
+        dec = TreeDecoder(target, draft, branch=(4, 2, 2))
+        prompts = [torch.randint(0, target.cfg.vocab, (1024,), generator=gen, dtype=torch.int32)]
+        round_bytes = 3 * draft.cfg.weight_bytes() + target.cfg.weight_bytes()
+        workload = ("BASELINE config 4: greedy tree verification, Gemma-3-12B shapes (4-bit) with a Gemma-3-1B-shaped "
+                    "draft, 4 x 2 x 2 draft tree verified as root + 28 nodes (29 rows), 1 sequence, 1024-token prompt")
+        metric = "accepted tokens/s (tree spec decode, Gemma-3-12B + 1B draft, 4x2x2 tree, 1 sequence)"
+    room = max(8, ctx - max(p.numel() for p in prompts) - dec.reserve - 8)
+    dec.start([p.to(device) for p in prompts], max_new=room)
+    dec.round()
+    torch.cuda.synchronize()
+    dec.capture()
+    dec.run_rounds(args.warmup)
+    torch.cuda.synchronize()
+    before = dec.read_stats()
+    stream = torch.cuda.current_stream(device)
+    clocks = Clocks(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    dec.run_rounds(args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1)
+    after = dec.read_stats()
+    tokens = after.tokens - before.tokens
+    max_ms = reduce_max(ms, world)
+    value = reduce_sum(float(tokens), world) / (max_ms / 1000)
+    step_s = max_ms / args.steps / 1000
+    if rank == 0:
+        line = {"metric": metric, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, 4-bit weights (MLX affine g64)",
+                "data": "synthetic (random-init weights, uniform random prompts)",
+                "config": {"workload": workload, "parallelism": f"replicas x{world}",
+                           "accepted_per_round": round((after.accepted - before.accepted) / args.steps, 4),
+                           "round_weight_bytes": round_bytes},
+                "roofline": {"bound": "hbm", "achieved": round(round_bytes / step_s / 1e9, 1), "peak": pk["hbm_gbs"],
+                             "unit": "GB/s", "frac": round(round_bytes / step_s / 1e9 / pk["hbm_gbs"], 4),
+                             "traffic": None, "kernel": "whole round (weights streamed per round / round time)"},
+                "clocks": clk, "gpu_launches": dec.launches_per_round() * args.steps, "peak_source": pk["source"]}
+        print(json.dumps(line), flush=True)
+
+
 def main() -> int:
     args = parse()
     if args.impl == "reference":
@@ -434,6 +517,8 @@ def main() -> int:
     try:
         if args.workload == "verify_step":
             run_verify_step(args, world, rank, local)
+        elif args.workload in ("stochastic", "tree"):
+            run_rounds_workload(args, world, rank, local, args.workload)
         else:
             run_spec_decode(args, world, rank, local)
     finally:

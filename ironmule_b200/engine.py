@@ -87,6 +87,9 @@ PRESETS = {
                               sliding_window=1024, global_every=6, query_scale=256 ** -0.5),
     "gemma3-27b": ModelConfig("gemma3-27b", 5376, 62, 32, 16, 128, 21504, 262144, family="gemma3",
                               sliding_window=1024, global_every=6, query_scale=168 ** -0.5),
+    # a Gemma-3-1B-shaped draft for the Gemma-3 tree workload (the configuration leaves the draft open)
+    "gemma3-1b": ModelConfig("gemma3-1b", 1152, 26, 4, 1, 256, 6912, 262144, family="gemma3", sliding_window=512,
+                             global_every=6, query_scale=256 ** -0.5),
     # small shapes for tests
     "tiny-target": ModelConfig("tiny-target", 256, 2, 4, 2, 128, 512, 1000),
     "tiny-draft": ModelConfig("tiny-draft", 128, 2, 2, 1, 128, 256, 1000),
