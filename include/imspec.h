@@ -190,7 +190,8 @@ int im_rmsnorm(const uint16_t* x, int64_t ldx, const uint16_t* weight, uint16_t*
  * Gemma-3's post-attention / post-feedforward norm fused with its residual add: per row m < M,
  * h[m] = bf16(h[m] + bf16((y[m] * inv_rms(y[m])) * w')), w' = 1 + weight (gemma_style) or weight, and, when
  * out_sq != NULL (M <= 32), out_sq[m] = the sum of squares of the new h[m] for the RMSNorm that the next
- * im_qgemm_packed fuses (norm_parts = 1). y, h [M, H] bf16. Replaces the post_attention_layernorm /
+ * im_qgemm_packed fuses (norm_parts = 1). y, h [M, H] bf16. weight == NULL: the plain residual add
+ * h[m] = bf16(h[m] + y[m]) (after an all-reduce of tensor-parallel partial projections). Replaces the post_attention_layernorm /
  * post_feedforward_layernorm steps of the Gemma-3 decode layer (ironmule/paired_research.py:177-215).
  */
 int im_rmsnorm_residual(const uint16_t* y, const uint16_t* weight, uint16_t* h, int64_t M, int64_t H, float eps,

@@ -48,9 +48,10 @@ rmsnorm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w, u
   }
 }
 
-// Gemma-3's output norms: h[m] = bf16(h + bf16((y * inv_rms(y)) * (1 + w))) (w' = w for Qwen3-style weights),
-// and out_sq[m] = the new row's sum of squares (block order: thread sums, warp xor-trees, warps in order) for the
-// RMSNorm that the next qGEMM fuses. One CTA per row.
+// Gemma-3's output norms: h[m] = bf16(h + bf16((y * inv_rms(y)) * (1 + w))) (w' = w for Qwen3-style weights);
+// with w == NULL the plain residual add h[m] = bf16(h + y) (a tensor-parallel projection whose partial sums were
+// all-reduced). out_sq[m] = the new row's sum of squares (block order: thread sums, warp xor-trees, warps in
+// order) for the RMSNorm that the next qGEMM fuses. One CTA per row.
 __global__ void __launch_bounds__(LN_THREADS)
 rmsnorm_residual_kernel(const uint16_t* __restrict__ y, const uint16_t* __restrict__ w, uint16_t* __restrict__ h,
                         int H, float eps, int gemma, float* __restrict__ out_sq) {
@@ -68,8 +69,11 @@ rmsnorm_residual_kernel(const uint16_t* __restrict__ y, const uint16_t* __restri
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(total, (float)H) + eps));
   float s2 = 0.f;
   for (int i = threadIdx.x; i < H; i += LN_THREADS) {
-    const float wi = gemma ? 1.0f + bf(w[i]) : bf(w[i]);
-    const float o = round_bf((bf(yr[i]) * inv) * wi);
+    float o = bf(yr[i]);
+    if (w) {
+      const float wi = gemma ? 1.0f + bf(w[i]) : bf(w[i]);
+      o = round_bf((o * inv) * wi);
+    }
     const uint16_t hn = to_bf(bf(hr[i]) + o);
     hr[i] = hn;
     s2 = fmaf(bf(hn), bf(hn), s2);
@@ -188,7 +192,7 @@ extern "C" int im_rmsnorm_residual(const uint16_t* y, const uint16_t* weight, ui
   clear_error();
   IM_REQUIRE(M >= 0 && H >= 1 && H <= (1 << 20), IM_INVALID, "im_rmsnorm_residual: bad sizes");
   if (M == 0) return IM_OK;
-  IM_REQUIRE(y && weight && h, IM_INVALID, "im_rmsnorm_residual: null pointer");
+  IM_REQUIRE(y && h, IM_INVALID, "im_rmsnorm_residual: null pointer");
   IM_REQUIRE(!out_sq || M <= 32, IM_INVALID, "im_rmsnorm_residual: row sums of squares cover at most 32 rows");
   return launch("rmsnorm_residual_kernel", rmsnorm_residual_kernel, dim3((unsigned)M), dim3(LN_THREADS), 0,
                 reinterpret_cast<cudaStream_t>(stream), y, weight, h, (int)H, eps, gemma_style, out_sq);

@@ -7,7 +7,7 @@
 //    CTAs ("stream-K"): a CTA streams a contiguous run of units, so tiles may span two CTAs;
 //  * the producer's lane 0 copies each unit's 32 rows x 512 bytes of codes into a 6-stage shared-memory ring
 //    with cp.async.bulk (one bulk copy per row, completion counted on the stage's mbarrier); rows are padded to
-//    544 bytes so the consumers' 8-byte fragment reads are bank-conflict free. No multicast anywhere;
+//    544 bytes so the consumers' 8-byte fragment reads are bank-conflict free. Every copy targets only this CTA;
 //  * consumer warp w takes groups 2w and 2w+1 of every unit for both 16-row halves, reads scales and biases
 //    with 4-byte loads and activations (L1-resident) with 16-byte loads straight from global memory;
 //  * at the end of a tile's run in a CTA the 8 consumers reduce in warp order; a tile covered by one CTA is

@@ -25,6 +25,7 @@ answer.
 """
 from __future__ import annotations
 
+import dataclasses
 import math
 from dataclasses import dataclass, field
 
@@ -137,6 +138,18 @@ def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return torch.stack([gate.view(inter // 16, 16, k), up.view(inter // 16, 16, k)], dim=1).reshape(2 * inter, k)
 
 
+def tp_shard(cfg: ModelConfig, tp: int, r: int) -> dict[str, tuple[int, int]]:
+    """Rank r's slices of a tp-way tensor-parallel model, as [start, end) ranges of the full matrices: rows of
+    the q, k and v blocks of qkv, columns of o (= its q heads' outputs), rows of gate and of up, columns of down,
+    rows of the tied embedding used as the head."""
+    d = cfg.head_dim
+    hq, hkv, il, vl = cfg.heads // tp, cfg.kv_heads // tp, cfg.inter // tp, cfg.vocab // tp
+    q0, k0, v0 = r * hq * d, cfg.heads * d + r * hkv * d, (cfg.heads + cfg.kv_heads) * d + r * hkv * d
+    return {"q": (q0, q0 + hq * d), "k": (k0, k0 + hkv * d), "v": (v0, v0 + hkv * d),
+            "o_cols": (r * hq * d, (r + 1) * hq * d), "inter": (r * il, (r + 1) * il),
+            "vocab": (r * vl, (r + 1) * vl)}
+
+
 @dataclass
 class RowMeta:
     """Device metadata for a forward of M rows: token ids (with a stride), slot / position / sequence per row,
@@ -155,12 +168,30 @@ class RowMeta:
 
 
 class QuantModel:
-    """A random-init 4-bit model resident on one GPU, with its paged KV cache and preallocated activations."""
+    """A random-init 4-bit model resident on one GPU, with its paged KV cache and preallocated activations.
+
+    Tensor parallelism (tp > 1, one process per GPU, `group` a NCCL process group of tp ranks): rank r holds
+    heads [r Hq/tp, (r+1) Hq/tp) of q and of k/v (column shards of qkv), the matching columns of o (a row
+    shard along K), rows [r I/tp, (r+1) I/tp) of gate and up (column shards, still 16-row interleaved) and the
+    matching columns of down, its kv heads' cache, and vocabulary rows [r V/tp, (r+1) V/tp) of the tied head;
+    the embedding table (for the gather) and the norms are replicated. The shards are cut from the same seeded
+    full matrices a tp = 1 model of the same seed holds, and 64-element groups never straddle a cut, so the
+    quantised shards are slices of the tp = 1 model's weights. Forward: o and down store their partial sums,
+    an all-reduce (sum, bf16) adds them, then the (post-)norm + residual kernel; the head's vocabulary slices are
+    all-gathered into full logits, so acceptance sees the whole vocabulary on every rank (BASELINE config 5a;
+    the reference has no tensor parallelism).
+    """
 
     def __init__(self, cfg: ModelConfig, device: torch.device | str = "cuda", *, seed: int = 0,
                  sigma: float = 0.02, max_seqs: int = 1, max_ctx: int = 1024, max_rows: int = 32,
-                 max_logit_rows: int = 32, keys_per_split: int = 64):
+                 max_logit_rows: int = 32, keys_per_split: int = 64, tp: int = 1, rank: int = 0, group=None):
         self.cfg = cfg
+        if tp > 1 and (cfg.heads % tp or cfg.kv_heads % tp or cfg.inter % (64 * tp) or (cfg.inter // tp) % 16
+                       or cfg.vocab % tp or (cfg.heads * cfg.head_dim // tp) % 64):
+            raise ValueError(f"{cfg.name} does not split {tp} ways (heads, kv heads, 64-groups of K, vocabulary)")
+        self.tp, self.rank, self.group = tp, rank, group
+        # the rank's shapes: its heads and its slice of the intermediate size (the full model when tp == 1)
+        self.lc = dataclasses.replace(cfg, heads=cfg.heads // tp, kv_heads=cfg.kv_heads // tp, inter=cfg.inter // tp)
         self.device = torch.device(device)
         self.max_seqs, self.max_rows, self.max_logit_rows = max_seqs, max_rows, max_logit_rows
         self.pages_per_seq = -(-max_ctx // PAGE)
@@ -184,16 +215,34 @@ class QuantModel:
         return (base + 0.02 * torch.randn((n,), generator=gen, device=self.device)).to(torch.bfloat16)
 
     def _build_weights(self, gen, sigma) -> None:
-        c = self.cfg
-        self.embed = self._lin(self._rand(gen, c.vocab, c.hidden, sigma))
+        c, tp = self.cfg, self.tp
+        sh = tp_shard(c, tp, self.rank)
+        cut = lambda a, key: a[slice(*sh[key])]  # noqa: E731
+        table = self._rand(gen, c.vocab, c.hidden, sigma)
+        if tp == 1:
+            self.embed = self._lin(table)
+            self.head = self.embed
+        else:
+            wq, s, b = kernels.quantize(table.contiguous())
+            self.embed = Linear4(wq, s, b)  # the gather reads the whole table; the head is this rank's slice
+            self.head = self._lin(cut(table, "vocab"))
+        del table
         self.layers: list[Layer] = []
         for _ in range(c.layers):
-            qkv = self._lin(self._rand(gen, c.qkv_rows, c.hidden, sigma))
-            o = self._lin(self._rand(gen, c.hidden, c.heads * c.head_dim, sigma))
+            qkv_full = self._rand(gen, c.qkv_rows, c.hidden, sigma)
+            if tp > 1:
+                qkv_full = torch.cat([cut(qkv_full, "q"), cut(qkv_full, "k"), cut(qkv_full, "v")])
+            qkv = self._lin(qkv_full)
+            o_full = self._rand(gen, c.hidden, c.heads * c.head_dim, sigma)
+            o = self._lin(o_full[:, slice(*sh["o_cols"])] if tp > 1 else o_full)
             gate, up = self._rand(gen, c.inter, c.hidden, sigma), self._rand(gen, c.inter, c.hidden, sigma)
-            gate_up = self._lin(interleave_gate_up(gate, up))
-            del gate, up
-            down = self._lin(self._rand(gen, c.hidden, c.inter, sigma))
+            if tp > 1:
+                gate, up = cut(gate, "inter"), cut(up, "inter")
+            gate_up = self._lin(interleave_gate_up(gate.contiguous(), up.contiguous()))
+            del gate, up, qkv_full, o_full
+            down_full = self._rand(gen, c.hidden, c.inter, sigma)
+            down = self._lin(down_full[:, slice(*sh["inter"])] if tp > 1 else down_full)
+            del down_full
             layer = Layer(qkv, o, gate_up, down, self._norm(gen, c.hidden), self._norm(gen, c.hidden),
                           self._norm(gen, c.head_dim), self._norm(gen, c.head_dim))
             if c.family == "gemma3":
@@ -207,7 +256,7 @@ class QuantModel:
 
     # ---- cache and buffers ------------------------------------------------------------------------------
     def _build_cache(self) -> None:
-        c = self.cfg
+        c = self.lc
         pages = self.max_seqs * self.pages_per_seq
         shape = (c.layers, pages, c.kv_heads, PAGE, c.head_dim)
         self.k_cache = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
@@ -216,7 +265,7 @@ class QuantModel:
         self.page_table = torch.arange(pages, dtype=torch.int32, device=self.device).view(self.max_seqs, -1)
 
     def _build_buffers(self) -> None:
-        c, r, dev = self.cfg, self.max_rows, self.device
+        c, r, dev = self.lc, self.max_rows, self.device
         bf = torch.bfloat16
         self.h = torch.zeros((r, c.hidden), dtype=bf, device=dev)
         # row sums of squares of h for the fused RMSNorms: one part from the embedding, one per 32-row tile
@@ -230,10 +279,14 @@ class QuantModel:
         self.act = torch.zeros((r, c.inter), dtype=bf, device=dev)
         self.y = torch.zeros((r, c.hidden), dtype=bf, device=dev)  # Gemma-3: projection output before its norm
         self.logits = torch.zeros((self.max_logit_rows, c.vocab), dtype=bf, device=dev)
+        if self.tp > 1:  # this rank's vocabulary slice, and the all-gather target [tp][rows][V/tp]
+            vl = c.vocab // self.tp
+            self.logits_local = torch.zeros((self.max_logit_rows, vl), dtype=bf, device=dev)
+            self.logits_gather = torch.zeros((self.tp * self.max_logit_rows * vl,), dtype=bf, device=dev)
         # scratch: one buffer per kernel family, sized for the largest call this model makes
         q_need = max(kernels.qgemm_packed_workspace_bytes(min(r, MAX_QGEMM_ROWS), n, k)
                      for n, k in self._gemm_shapes())
-        head_need = kernels.qgemm_packed_workspace_bytes(self.max_logit_rows, c.vocab, c.hidden)
+        head_need = kernels.qgemm_packed_workspace_bytes(self.max_logit_rows, c.vocab // self.tp, c.hidden)
         self.ws_gemm = kernels.workspace(max(q_need, head_need), dev)
         a_need = max(kernels.attention_workspace_bytes(self.max_seqs, rows, c.heads, c.kv_heads, c.head_dim,
                                                        self.max_ctx, self.keys_per_split)
@@ -242,7 +295,7 @@ class QuantModel:
         self.ws_argmax = kernels.workspace(kernels.argmax_workspace_bytes(self.max_logit_rows, c.vocab), dev)
 
     def _gemm_shapes(self):
-        c = self.cfg
+        c = self.lc
         return [(c.qkv_rows, c.hidden), (c.hidden, c.heads * c.head_dim), (2 * c.inter, c.hidden),
                 (c.hidden, c.inter)]
 
@@ -250,7 +303,7 @@ class QuantModel:
     def forward(self, meta: RowMeta, max_kv_len: int, logit_rows: int = 0) -> torch.Tensor | None:
         """Run M = meta.rows rows through the model, writing their K/V at their slots; the logits of the first
         `logit_rows` rows land in self.logits[:logit_rows] (returned; None when logit_rows is 0)."""
-        c, m = self.cfg, meta.rows
+        c, m = self.lc, meta.rows
         if m > min(self.max_rows, MAX_QGEMM_ROWS):
             raise ValueError(f"{m} rows exceed this model's per-forward limit")
         if logit_rows > min(m, self.max_logit_rows):
@@ -272,6 +325,19 @@ class QuantModel:
                                   max_rows_per_seq=meta.max_rows_per_seq, max_kv_len=max_kv_len, scale=c.scale,
                                   keys_per_split=self.keys_per_split, window=0 if glob else c.sliding_window,
                                   out=self.attn, rows=m, ws=self.ws_attn, seq_slot=meta.seq_slot)
+            if self.tp > 1:  # partial sums of the row-sharded o and down, all-reduced before the residual add
+                kernels.qgemm_packed(self.attn, layer.o.p, out=self.y, rows=m, ws=ws)
+                self._all_reduce(self.y[:m])
+                kernels.rmsnorm_residual(self.y, layer.post_attn_norm, h, c.eps, gemma=gemma, rows=m,
+                                         out_sq=self.sq_attn)
+                kernels.qgemm_packed(h, layer.gate_up.p, epilogue="geglu" if gemma else "swiglu", out=self.act,
+                                     rows=m, norm_sq=self.sq_attn, norm_parts=1, norm_weight=layer.post_norm,
+                                     eps=c.eps, gemma_norm=gemma, ws=ws)
+                kernels.qgemm_packed(self.act, layer.down.p, out=self.y, rows=m, ws=ws)
+                self._all_reduce(self.y[:m])
+                kernels.rmsnorm_residual(self.y, layer.post_ff_norm, h, c.eps, gemma=gemma, rows=m, out_sq=self.sq_mlp)
+                sq, parts = self.sq_mlp, 1
+                continue
             if gemma:  # Gemma-3: output norms before each residual add; one sum-of-squares part per row
                 kernels.qgemm_packed(self.attn, layer.o.p, out=self.y, rows=m, ws=ws)
                 kernels.rmsnorm_residual(self.y, layer.post_attn_norm, h, c.eps, gemma=True, rows=m,
@@ -293,9 +359,22 @@ class QuantModel:
             sq, parts = self.sq_mlp, self.h_tiles
         if not logit_rows:
             return None
-        kernels.qgemm_packed(h, self.embed.p, out=self.logits, rows=logit_rows, norm_sq=sq, norm_parts=parts,
+        if self.tp == 1:
+            kernels.qgemm_packed(h, self.head.p, out=self.logits, rows=logit_rows, norm_sq=sq, norm_parts=parts,
+                                 norm_weight=self.final_norm, eps=c.eps, gemma_norm=gemma, ws=ws)
+            return self.logits[:logit_rows]
+        lr, vl = logit_rows, c.vocab // self.tp
+        kernels.qgemm_packed(h, self.head.p, out=self.logits_local, rows=lr, norm_sq=sq, norm_parts=parts,
                              norm_weight=self.final_norm, eps=c.eps, gemma_norm=gemma, ws=ws)
-        return self.logits[:logit_rows]
+        import torch.distributed as dist
+        gathered = self.logits_gather[:self.tp * lr * vl]
+        dist.all_gather_into_tensor(gathered, self.logits_local[:lr], group=self.group)
+        self.logits[:lr].view(lr, self.tp, vl).copy_(gathered.view(self.tp, lr, vl).permute(1, 0, 2))
+        return self.logits[:lr]
+
+    def _all_reduce(self, t: torch.Tensor) -> None:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
     # ---- eager helpers (prefill, plain decode, tests) -----------------------------------------------------
     def _meta(self, tokens: torch.Tensor, positions: list[int], seq: int) -> RowMeta:

@@ -221,12 +221,12 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, *, gemma: bool = 
     return out
 
 
-def rmsnorm_residual(y: torch.Tensor, weight: torch.Tensor, h: torch.Tensor, eps: float, *, gemma: bool = False,
+def rmsnorm_residual(y: torch.Tensor, weight: torch.Tensor | None, h: torch.Tensor, eps: float, *, gemma: bool = False,
                      rows: int | None = None, out_sq: torch.Tensor | None = None) -> torch.Tensor:
     """h += rmsnorm(y) * w' per row, in place (Gemma-3's output norms); out_sq gets the new rows' sums of squares."""
     hsz = h.shape[-1]
     m = h.numel() // hsz if rows is None else rows
-    _lib.call("im_rmsnorm_residual", y.data_ptr(), weight.data_ptr(), h.data_ptr(), m, hsz, float(eps), int(gemma),
+    _lib.call("im_rmsnorm_residual", y.data_ptr(), _ptr_or_none(weight), h.data_ptr(), m, hsz, float(eps), int(gemma),
               _ptr_or_none(out_sq), _stream(h.device))
     return h
 
