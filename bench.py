@@ -11,14 +11,17 @@ the data path), timed with CUDA events over K rounds replayed from one captured 
 streams the full 3.6 GB of weights, far more than the 126 MB L2, so no flush is needed.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload spec_decode|verify_step|stochastic|tree]
+                    [--workload spec_decode|verify_step|stochastic|tree|tp]
 
 --workload stochastic: BASELINE config 3's round -- Qwen3-4B + 0.6B, temperature 0.7, top-p 0.95, k = 4,
 rejection sampling with residual resampling on Philox -- over 6 concurrent sequences with prompt lengths drawn
 uniformly from [128, 2048] (seed 0): 6 x 5 = 30 verify rows, the most one qGEMM call takes (the configuration's
 32 sequences need 160 rows). --workload tree: config 4's tree verification on Gemma-3-12B shapes (48 layers,
 hidden 3840, 16/8 heads, head_dim 256, GeGLU 15360, vocab 262144) with a Gemma-3-1B-shaped draft, a 4 x 2 x 2
-draft tree verified as root + 28 nodes = 29 rows, one sequence, a 1024-token prompt.
+draft tree verified as root + 28 nodes = 29 rows, one sequence, a 1024-token prompt. --workload tp (under
+torchrun, N ranks): config 5a -- Gemma-3-27B shapes tensor-parallel over the N GPUs (NCCL all-reduce after o and
+down, all-gathered vocabulary-sharded head) with a replicated Gemma-3-1B-shaped draft, greedy, k = 4, 6
+sequences with 512-token prompts; one job over all ranks, so `value` is that job's tokens/s (strong scaling).
 
 --impl reference times the CPU implementation of the same round (the oracle port in oracle/spec.py: the
 reference's greedy round with projections dequantised and dotted in float32 by OpenMP C code) on the box's host
@@ -50,7 +53,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["spec_decode", "verify_step", "stochastic", "tree"], default="spec_decode")
+    ap.add_argument("--workload", choices=["spec_decode", "verify_step", "stochastic", "tree", "tp"],
+                    default="spec_decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -442,7 +446,26 @@ def run_rounds_workload(args, world: int, rank: int, local: int, kind: str) -> N
     torch.cuda.set_device(device)
     pk = peaks()
     gen = torch.Generator().manual_seed(rank)
-    if kind == "stochastic":
+    tp_group = None
+    if kind == "tp" and world > 1:
+        import torch.distributed as dist
+        tp_group = dist.group.WORLD
+    if kind == "tp":
+        b, ctx = 6, 512 + 512
+        gen = torch.Generator().manual_seed(0)  # the same sequences on every rank: one tensor-parallel job
+        target = QuantModel(PRESETS["gemma3-27b"], device, seed=0, max_ctx=ctx, max_seqs=b, max_rows=32,
+                            max_logit_rows=32, tp=world, rank=rank, group=tp_group)
+        draft = QuantModel(PRESETS["gemma3-1b"], device, seed=1, max_ctx=ctx, max_seqs=b, max_rows=16,
+                           max_logit_rows=16)
+        dec = SpecDecoder(target, draft, k=K_DRAFTS, batch=b)
+        prompts = [torch.randint(0, target.cfg.vocab, (512,), generator=gen, dtype=torch.int32) for _ in range(b)]
+        round_bytes = K_DRAFTS * draft.cfg.weight_bytes() + target.cfg.weight_bytes() // world
+        workload = (f"BASELINE config 5a: Gemma-3-27B shapes (4-bit) tensor-parallel over {world} GPU(s), NCCL "
+                    "all-reduce after o and down, vocabulary-sharded head all-gathered; replicated Gemma-3-1B-shaped "
+                    "draft; greedy, k 4, 6 sequences (30 verify rows; the configuration's batch 64 needs 320 rows "
+                    "per qGEMM call), 512-token prompts")
+        metric = "accepted tokens/s (spec decode, Gemma-3-27B tensor-parallel + 1B draft, k=4, 6 sequences)"
+    elif kind == "stochastic":
         b, ctx = 6, 2048 + 256
         lens = torch.randint(128, 2049, (b,), generator=gen).tolist()
         target = QuantModel(PRESETS["qwen3-4b"], device, seed=0, max_ctx=ctx, max_seqs=b, max_rows=32,
@@ -490,14 +513,19 @@ def run_rounds_workload(args, world: int, rank: int, local: int, kind: str) -> N
     after = dec.read_stats()
     tokens = after.tokens - before.tokens
     max_ms = reduce_max(ms, world)
-    value = reduce_sum(float(tokens), world) / (max_ms / 1000)
+    # replicas add their sequences; a tensor-parallel job's ranks share the same ones
+    total = float(tokens) if kind == "tp" else reduce_sum(float(tokens), world)
+    value = total / (max_ms / 1000)
     step_s = max_ms / args.steps / 1000
+    dec.graph = None  # a graph holding NCCL calls goes before the process group
     if rank == 0:
         line = {"metric": metric, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, 4-bit weights (MLX affine g64)",
+                "scaling": "strong" if kind == "tp" else "weak", "vs_baseline": None,
+                "dtype": "bf16 activations, 4-bit weights (MLX affine g64)",
                 "data": "synthetic (random-init weights, uniform random prompts)",
-                "config": {"workload": workload, "parallelism": f"replicas x{world}",
+                "config": {"workload": workload,
+                           "parallelism": f"tp{world}" if kind == "tp" else f"replicas x{world}",
                            "accepted_per_round": round((after.accepted - before.accepted) / args.steps, 4),
                            "round_weight_bytes": round_bytes},
                 "roofline": {"bound": "hbm", "achieved": round(round_bytes / step_s / 1e9, 1), "peak": pk["hbm_gbs"],
@@ -517,7 +545,7 @@ def main() -> int:
     try:
         if args.workload == "verify_step":
             run_verify_step(args, world, rank, local)
-        elif args.workload in ("stochastic", "tree"):
+        elif args.workload in ("stochastic", "tree", "tp"):
             run_rounds_workload(args, world, rank, local, args.workload)
         else:
             run_spec_decode(args, world, rank, local)
