@@ -123,12 +123,13 @@ int im_qgemm_tma_status(const void* workspace, uint32_t* status);
  * im_qgemm_pack_w4g64 converts MLX-layout w/scales/biases [N, K] into `packed` (16-byte aligned,
  * im_qgemm_packed_bytes(N, K) bytes): rows padded to 32-row tiles, one contiguous 1152-byte unit per
  * (tile, 64-group) holding that tile's codes in lane order and its 32 scales/biases.
- * im_qgemm_packed computes the same product and epilogues as im_qgemm_w4g64_ex (M <= 32) from it, and can fuse
- * the RMSNorm that precedes a projection: with norm_weight != NULL, x is the raw residual stream and each row
- * is normalised on the way in (x * 1/sqrt(sum(x^2)/K + eps) * w', w' = w or 1 + w when gemma_norm), its sum of
- * squares taken from norm_sq[p * 32 + m] summed over p < norm_parts (per-tile partial sums). With
- * out_sq != NULL, a store/residual epilogue writes those per-tile partial sums of its own output rows
- * ([ceil(N/32)][32] floats) for the next normalised GEMM. workspace >= im_qgemm_packed_workspace_bytes(M, N, K)
+ * im_qgemm_packed computes the same product and epilogues as im_qgemm_w4g64_ex from it for M <= 320 rows (in
+ * chunks of 32, each computed exactly as a call of those rows alone), and can fuse the RMSNorm that precedes a
+ * projection: with norm_weight != NULL, x is the raw residual stream and each row is normalised on the way in
+ * (x * 1/sqrt(sum(x^2)/K + eps) * w', w' = w or 1 + w when gemma_norm), its sum of squares taken from
+ * norm_sq[p * sq_ld + m] summed over p < norm_parts (per-tile partial sums). With out_sq != NULL, a
+ * store/residual epilogue writes those per-tile partial sums of its own output rows (out_sq[tile * sq_ld + m],
+ * ceil(N/32) tiles) for the next normalised GEMM. sq_ld = 0 means M rounded up to 32. workspace >= im_qgemm_packed_workspace_bytes(M, N, K)
  * (256-byte aligned, zero-filled before first use) when that is non-zero; calls sharing it must not overlap.
  * Replaces the same reference interfaces as im_qgemm_w4g64, plus the RMSNorm before each projection of the
  * decode layer (ironmule/paired_research.py:177-215).
@@ -142,7 +143,8 @@ size_t im_qgemm_packed_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int im_qgemm_packed_tune(int split_override, int target_ctas, int max_split);
 int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* y, const uint16_t* residual, int64_t M, int64_t N,
                     int64_t K, int epilogue, const float* norm_sq, int64_t norm_parts, const uint16_t* norm_weight,
-                    float eps, int gemma_norm, float* out_sq, void* workspace, size_t workspace_bytes, void* stream);
+                    float eps, int gemma_norm, float* out_sq, int64_t sq_ld, void* workspace, size_t workspace_bytes,
+                    void* stream);
 
 /*
  * Row statistics over a logits matrix: for each row r of logits[rows, V] (bf16, row stride ld elements)
@@ -189,7 +191,7 @@ int im_rmsnorm(const uint16_t* x, int64_t ldx, const uint16_t* weight, uint16_t*
 /*
  * Gemma-3's post-attention / post-feedforward norm fused with its residual add: per row m < M,
  * h[m] = bf16(h[m] + bf16((y[m] * inv_rms(y[m])) * w')), w' = 1 + weight (gemma_style) or weight, and, when
- * out_sq != NULL (M <= 32), out_sq[m] = the sum of squares of the new h[m] for the RMSNorm that the next
+ * out_sq != NULL, out_sq[m] = the sum of squares of the new h[m] for the RMSNorm that the next
  * im_qgemm_packed fuses (norm_parts = 1). y, h [M, H] bf16. weight == NULL: the plain residual add
  * h[m] = bf16(h[m] + y[m]) (after an all-reduce of tensor-parallel partial projections). Replaces the post_attention_layernorm /
  * post_feedforward_layernorm steps of the Gemma-3 decode layer (ironmule/paired_research.py:177-215).
@@ -214,7 +216,7 @@ int im_qk_norm_rope_kv(const uint16_t* qkv, const uint16_t* q_norm, const uint16
 
 /*
  * Embedding gather from a 4-bit table: out[m, :] = bf16(scale * q + bias) of row tokens[m * tokens_stride] (int32;
- * clamped to [0, V)), times bf16(mult) when mult != 1 (Gemma-3 scales by sqrt(hidden)); out_sq (M <= 32 floats, may
+ * clamped to [0, V)), times bf16(mult) when mult != 1 (Gemma-3 scales by sqrt(hidden)); out_sq (M floats, may
  * be NULL) receives each row's sum of squares, the norm_sq input of a fused-RMSNorm im_qgemm_packed. The tied table
  * doubles as the LM head through im_qgemm_w4g64 (nn.QuantizedEmbedding / as_linear,
  * ironmule/cuda_native.py:227-229).

@@ -46,8 +46,8 @@ SIGNATURES: dict[str, tuple] = {
     "im_tree_prepare": (_INT, [_P, _I64, _P, _I64, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P, _P]),
     "im_tree_accept": (_INT, [_P, _P, _I64, _P, _I64, _P, _P, _P, _P]),
     "im_tree_compact": (_INT, [_P, _P, _I64, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
-    "im_qgemm_packed": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _INT, _P, _I64, _P, ctypes.c_float, _INT, _P, _P,
-                               _SZ, _P]),
+    "im_qgemm_packed": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _INT, _P, _I64, _P, ctypes.c_float, _INT, _P, _I64,
+                               _P, _SZ, _P]),
     "im_argmax_rows": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _P, _P, _SZ, _P]),
     "im_argmax_workspace_bytes": (_SZ, [_I64, _I64]),
     "im_verify_greedy": (_INT, [_P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _SZ, _P]),

@@ -193,7 +193,6 @@ extern "C" int im_rmsnorm_residual(const uint16_t* y, const uint16_t* weight, ui
   IM_REQUIRE(M >= 0 && H >= 1 && H <= (1 << 20), IM_INVALID, "im_rmsnorm_residual: bad sizes");
   if (M == 0) return IM_OK;
   IM_REQUIRE(y && h, IM_INVALID, "im_rmsnorm_residual: null pointer");
-  IM_REQUIRE(!out_sq || M <= 32, IM_INVALID, "im_rmsnorm_residual: row sums of squares cover at most 32 rows");
   return launch("rmsnorm_residual_kernel", rmsnorm_residual_kernel, dim3((unsigned)M), dim3(LN_THREADS), 0,
                 reinterpret_cast<cudaStream_t>(stream), y, weight, h, (int)H, eps, gemma_style, out_sq);
 }
@@ -230,7 +229,6 @@ extern "C" int im_embed_w4g64(const int32_t* tokens, int64_t tokens_stride, cons
              "im_embed_w4g64: bad sizes");
   if (M == 0) return IM_OK;
   IM_REQUIRE(tokens && wq && scales && biases && out, IM_INVALID, "im_embed_w4g64: null pointer");
-  IM_REQUIRE(!out_sq || M <= 32, IM_INVALID, "im_embed_w4g64: row sums of squares cover at most 32 rows");
   return launch("embed_kernel", embed_kernel, dim3((unsigned)M), dim3(128), 0, reinterpret_cast<cudaStream_t>(stream),
                 tokens, (int)tokens_stride, wq, scales, biases, (int)H, (int)V, mult, out, out_sq);
 }

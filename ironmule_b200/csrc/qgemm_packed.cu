@@ -24,7 +24,8 @@ constexpr int Q4_WARPS = 4;
 constexpr int Q4_THREADS = Q4_WARPS * 32;
 constexpr int Q4_UNIT = 1152;
 constexpr int Q4_RMAX = 16;               // groups per CTA range (shared-memory budget: 16 KB per 8 rows)
-constexpr size_t Q4_COUNTER_BYTES = 65536;
+constexpr size_t Q4_COUNTER_BYTES = 524288;  // split-K arrival counters: one per (32-row chunk, tile)
+constexpr int Q4_MAX_ROWS = 320;             // rows per call: up to 10 chunks of 32
 constexpr int Q4_DEPTH = 3;               // units in flight per warp
 static int g_q4_split_override = 0;       // sweep hook (0 = automatic)
 static int g_q4_target_ctas = 148 * 4;    // split policy: aim for this many CTAs
@@ -102,13 +103,13 @@ struct Q4Args {
   const uint16_t* x;        // [M, K] activations (raw residual when norm_w != NULL)
   uint16_t* y;
   const uint16_t* res;
-  const float* norm_sq;     // [norm_parts][32] sums of squares of x rows (RMSNorm prologue) or NULL
+  const float* norm_sq;     // [norm_parts][sq_ld] sums of squares of x rows (RMSNorm prologue) or NULL
   const uint16_t* norm_w;   // [K]
-  float* out_sq;            // [tiles][32] sums of squares of the written rows (residual epilogue) or NULL
+  float* out_sq;            // [tiles][sq_ld] sums of squares of the written rows (residual epilogue) or NULL
   float* partial;
   unsigned* counters;
   float eps;
-  int M, N, K, tiles, splits, norm_parts, gemma_norm;
+  int M, N, K, tiles, splits, norm_parts, gemma_norm, sq_ld;
 };
 
 // Dynamic shared memory: xf [rmax][NT][32 lanes][2 x 16 B] activation fragments, sx [rmax][NT*8] group sums,
@@ -117,10 +118,24 @@ __host__ __device__ constexpr size_t q4_smem_bytes(int nt) {
   return (size_t)Q4_RMAX * nt * 32 * 32 + (size_t)Q4_RMAX * nt * 8 * 4 + 32 * 4;
 }
 
+// grid (CTA columns of 4 tiles, K splits, 32-row chunks). A chunk is computed exactly as a call of its rows alone
+// would be: the same plan, its own split-K counters and partials.
 template <int NT, int EPI>
 __global__ void __launch_bounds__(Q4_THREADS)
 qgemm_packed_kernel(Q4Args a) {
   extern __shared__ __align__(16) unsigned char q4_raw[];
+  if (gridDim.z > 1) {  // this CTA's 32-row chunk
+    const int m0 = blockIdx.z * 32;
+    const int nout = (EPI == IM_EPI_SWIGLU || EPI == IM_EPI_GEGLU) ? a.N >> 1 : a.N;
+    a.x += (size_t)m0 * a.K;
+    a.y += (size_t)m0 * nout;
+    if (a.res) a.res += (size_t)m0 * a.N;
+    if (a.norm_sq) a.norm_sq += m0;
+    if (a.out_sq) a.out_sq += m0;
+    a.counters += (size_t)blockIdx.z * a.tiles;
+    a.partial += (size_t)blockIdx.z * a.tiles * a.splits * (2 * 4 * 4 * 32);
+    a.M = min(32, a.M - m0);
+  }
   uint4 (*xf)[NT][32][2] = reinterpret_cast<uint4 (*)[NT][32][2]>(q4_raw);
   float (*sxs)[NT * 8] = reinterpret_cast<float (*)[NT * 8]>(q4_raw + (size_t)Q4_RMAX * NT * 32 * 32);
   float* inv_s = reinterpret_cast<float*>(q4_raw + (size_t)Q4_RMAX * NT * 32 * 32 + (size_t)Q4_RMAX * NT * 8 * 4);
@@ -160,7 +175,7 @@ qgemm_packed_kernel(Q4Args a) {
     for (int m = threadIdx.x; m < NT * 8; m += Q4_THREADS) {
       float s = 0.f;
       if (m < a.M)
-        for (int p = 0; p < a.norm_parts; p++) s += a.norm_sq[p * 32 + m];
+        for (int p = 0; p < a.norm_parts; p++) s += a.norm_sq[(size_t)p * a.sq_ld + m];
       inv_s[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(s, (float)a.K) + a.eps));
     }
     __syncthreads();
@@ -387,14 +402,14 @@ qgemm_packed_kernel(Q4Args a) {
           v += __shfl_xor_sync(0xffffffffu, v, 8);
           v += __shfl_xor_sync(0xffffffffu, v, 16);
           const int m = nt * 8 + 2 * t + e;
-          if (g == 0 && m < 32) a.out_sq[(size_t)tile * 32 + m] = m < a.M ? v : 0.f;
+          if (g == 0 && m < a.M) a.out_sq[(size_t)tile * a.sq_ld + m] = v;
         }
     }
   }
 }
 
 struct Q4Plan {
-  int tiles, ctas_x, splits, nt;
+  int tiles, ctas_x, splits, nt, chunks;
   size_t workspace;
 };
 
@@ -402,7 +417,7 @@ static Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
   Q4Plan p;
   p.tiles = (int)((N + 31) / 32);
   p.ctas_x = (p.tiles + Q4_WARPS - 1) / Q4_WARPS;
-  p.nt = (int)((M + 7) / 8);
+  p.nt = (int)((M > 32 ? 32 : M) + 7) / 8;
   const int G = (int)(K / 64);
   const int rmax = Q4_RMAX;
   const int need = (G + rmax - 1) / rmax;                // shared-memory budget
@@ -413,7 +428,8 @@ static Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
   if (s < need) s = need;
   if (g_q4_split_override > 0) s = g_q4_split_override < need ? need : (g_q4_split_override > G ? G : g_q4_split_override);
   p.splits = s;
-  p.workspace = s > 1 ? Q4_COUNTER_BYTES + (size_t)p.tiles * s * 2 * 4 * 4 * 32 * sizeof(float) : 0;
+  p.chunks = (int)((M + 31) / 32);
+  p.workspace = s > 1 ? Q4_COUNTER_BYTES + (size_t)p.chunks * p.tiles * s * 2 * 4 * 4 * 32 * sizeof(float) : 0;
   return p;
 }
 
@@ -425,7 +441,7 @@ static int q4_launch(const Q4Plan& p, const Q4Args& a, cudaStream_t st) {
     cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     configured = true;
   }
-  dim3 grid(p.ctas_x, p.splits);
+  dim3 grid(p.ctas_x, p.splits, p.chunks);
   return launch("qgemm_packed_kernel", qgemm_packed_kernel<NT, EPI>, grid, dim3(Q4_THREADS), smem, st, a);
 }
 
@@ -471,17 +487,18 @@ extern "C" int im_qgemm_pack_w4g64(const uint32_t* w, const uint16_t* scales, co
 }
 
 extern "C" size_t im_qgemm_packed_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  if (M < 1 || M > 32 || N < 1 || K < 64 || K % 64) return 0;
+  if (M < 1 || M > Q4_MAX_ROWS || N < 1 || K < 64 || K % 64) return 0;
   const Q4Plan p = q4_plan(M, N, K);
-  return p.tiles <= (int)(Q4_COUNTER_BYTES / 4) ? p.workspace : 0;
+  return (size_t)p.chunks * p.tiles <= Q4_COUNTER_BYTES / 4 ? p.workspace : 0;
 }
 
 extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* y, const uint16_t* residual,
                                int64_t M, int64_t N, int64_t K, int epilogue, const float* norm_sq,
                                int64_t norm_parts, const uint16_t* norm_weight, float eps, int gemma_norm,
-                               float* out_sq, void* workspace, size_t workspace_bytes, void* stream) {
+                               float* out_sq, int64_t sq_ld, void* workspace, size_t workspace_bytes,
+                               void* stream) {
   clear_error();
-  IM_REQUIRE(M >= 0 && M <= 32 && N >= 1 && K >= 64 && K % 64 == 0 && N <= (1 << 30) && K <= (1 << 24),
+  IM_REQUIRE(M >= 0 && M <= Q4_MAX_ROWS && N >= 1 && K >= 64 && K % 64 == 0 && N <= (1 << 30) && K <= (1 << 24),
              IM_INVALID, "im_qgemm_packed: bad sizes M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
   if (M == 0) return IM_OK;
   IM_REQUIRE(packed && x && y, IM_INVALID, "im_qgemm_packed: null pointer");
@@ -493,8 +510,11 @@ extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* 
   IM_REQUIRE(!glu || !out_sq, IM_INVALID, "im_qgemm_packed: sums of squares come from store/residual epilogues");
   IM_REQUIRE(!norm_weight || (norm_sq && norm_parts >= 1 && aligned(norm_weight, 2)), IM_INVALID,
              "im_qgemm_packed: the RMSNorm prologue needs norm_sq partials and a weight");
+  const int64_t ld = sq_ld > 0 ? sq_ld : (M + 31) / 32 * 32;
+  IM_REQUIRE(ld >= M, IM_INVALID, "im_qgemm_packed: sq_ld %lld below M", (long long)ld);
   const Q4Plan p = q4_plan(M, N, K);
-  IM_REQUIRE(p.tiles <= (int)(Q4_COUNTER_BYTES / 4), IM_UNSUPPORTED, "im_qgemm_packed: N too large for split-K");
+  IM_REQUIRE((size_t)p.chunks * p.tiles <= Q4_COUNTER_BYTES / 4, IM_UNSUPPORTED,
+             "im_qgemm_packed: N too large for split-K at %lld rows", (long long)M);
   if (p.splits > 1)
     IM_REQUIRE(workspace && aligned(workspace, 256) && workspace_bytes >= p.workspace, IM_INVALID,
                "im_qgemm_packed: workspace of %zu bytes (256-aligned) needed, %zu given", p.workspace,
@@ -517,6 +537,7 @@ extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* 
   a.splits = p.splits;
   a.norm_parts = (int)norm_parts;
   a.gemma_norm = gemma_norm;
+  a.sq_ld = (int)ld;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   switch (epilogue) {
     case IM_EPI_STORE: return q4_dispatch<IM_EPI_STORE>(p, a, st);

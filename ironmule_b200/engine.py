@@ -34,7 +34,8 @@ import torch
 from . import kernels
 
 PAGE = 16
-MAX_QGEMM_ROWS = 32
+MAX_QGEMM_ROWS = 320   # rows of one forward (the packed qGEMM takes them in chunks of 32)
+MAX_SEQ_ROWS = 32      # rows of one sequence in one forward (the fused attention's limit): prefill chunks
 
 
 @dataclass(frozen=True)
@@ -271,9 +272,10 @@ class QuantModel:
         # row sums of squares of h for the fused RMSNorms: one part from the embedding, one per 32-row tile
         # of the hidden dimension from the residual epilogues
         self.h_tiles = -(-c.hidden // 32)
-        self.sq_embed = torch.zeros((32,), dtype=torch.float32, device=dev)
-        self.sq_attn = torch.zeros((self.h_tiles, 32), dtype=torch.float32, device=dev)
-        self.sq_mlp = torch.zeros((self.h_tiles, 32), dtype=torch.float32, device=dev)
+        self.sq_ld = -(-min(r, MAX_QGEMM_ROWS) // 32) * 32  # row stride of the sums-of-squares buffers
+        self.sq_embed = torch.zeros((self.sq_ld,), dtype=torch.float32, device=dev)
+        self.sq_attn = torch.zeros((self.h_tiles, self.sq_ld), dtype=torch.float32, device=dev)
+        self.sq_mlp = torch.zeros((self.h_tiles, self.sq_ld), dtype=torch.float32, device=dev)
         self.qkv = torch.zeros((r, c.qkv_rows), dtype=bf, device=dev)
         self.attn = torch.zeros((r, c.heads * c.head_dim), dtype=bf, device=dev)  # [M, Hq, D] packed
         self.act = torch.zeros((r, c.inter), dtype=bf, device=dev)
@@ -290,7 +292,7 @@ class QuantModel:
         self.ws_gemm = kernels.workspace(max(q_need, head_need), dev)
         a_need = max(kernels.attention_workspace_bytes(self.max_seqs, rows, c.heads, c.kv_heads, c.head_dim,
                                                        self.max_ctx, self.keys_per_split)
-                     for rows in (1, 8, r))
+                     for rows in (1, 8, min(r, MAX_SEQ_ROWS)))
         self.ws_attn = kernels.workspace(a_need, dev)
         self.ws_argmax = kernels.workspace(kernels.argmax_workspace_bytes(self.max_logit_rows, c.vocab), dev)
 
@@ -316,7 +318,7 @@ class QuantModel:
         sq, parts = self.sq_embed, 1
         for li, layer in enumerate(self.layers):
             kernels.qgemm_packed(h, layer.qkv.p, out=self.qkv, rows=m, norm_sq=sq, norm_parts=parts,
-                                 norm_weight=layer.in_norm, eps=c.eps, gemma_norm=gemma, ws=ws)
+                                 norm_weight=layer.in_norm, eps=c.eps, gemma_norm=gemma, sq_ld=self.sq_ld, ws=ws)
             glob = c.is_global(li)
             kernels.attention_qkv(self.qkv, layer.q_norm, layer.k_norm, self.inv_freq if glob else self.inv_freq_local,
                                   meta.pos, self.k_cache[li], self.v_cache[li], self.page_table, meta.seq_rows,
@@ -326,46 +328,46 @@ class QuantModel:
                                   keys_per_split=self.keys_per_split, window=0 if glob else c.sliding_window,
                                   out=self.attn, rows=m, ws=self.ws_attn, seq_slot=meta.seq_slot)
             if self.tp > 1:  # partial sums of the row-sharded o and down, all-reduced before the residual add
-                kernels.qgemm_packed(self.attn, layer.o.p, out=self.y, rows=m, ws=ws)
+                kernels.qgemm_packed(self.attn, layer.o.p, out=self.y, rows=m, sq_ld=self.sq_ld, ws=ws)
                 self._all_reduce(self.y[:m])
                 kernels.rmsnorm_residual(self.y, layer.post_attn_norm, h, c.eps, gemma=gemma, rows=m,
                                          out_sq=self.sq_attn)
                 kernels.qgemm_packed(h, layer.gate_up.p, epilogue="geglu" if gemma else "swiglu", out=self.act,
                                      rows=m, norm_sq=self.sq_attn, norm_parts=1, norm_weight=layer.post_norm,
-                                     eps=c.eps, gemma_norm=gemma, ws=ws)
-                kernels.qgemm_packed(self.act, layer.down.p, out=self.y, rows=m, ws=ws)
+                                     eps=c.eps, gemma_norm=gemma, sq_ld=self.sq_ld, ws=ws)
+                kernels.qgemm_packed(self.act, layer.down.p, out=self.y, rows=m, sq_ld=self.sq_ld, ws=ws)
                 self._all_reduce(self.y[:m])
                 kernels.rmsnorm_residual(self.y, layer.post_ff_norm, h, c.eps, gemma=gemma, rows=m, out_sq=self.sq_mlp)
                 sq, parts = self.sq_mlp, 1
                 continue
             if gemma:  # Gemma-3: output norms before each residual add; one sum-of-squares part per row
-                kernels.qgemm_packed(self.attn, layer.o.p, out=self.y, rows=m, ws=ws)
+                kernels.qgemm_packed(self.attn, layer.o.p, out=self.y, rows=m, sq_ld=self.sq_ld, ws=ws)
                 kernels.rmsnorm_residual(self.y, layer.post_attn_norm, h, c.eps, gemma=True, rows=m,
                                          out_sq=self.sq_attn)
                 kernels.qgemm_packed(h, layer.gate_up.p, epilogue="geglu", out=self.act, rows=m, norm_sq=self.sq_attn,
-                                     norm_parts=1, norm_weight=layer.post_norm, eps=c.eps, gemma_norm=True, ws=ws)
-                kernels.qgemm_packed(self.act, layer.down.p, out=self.y, rows=m, ws=ws)
+                                     norm_parts=1, norm_weight=layer.post_norm, eps=c.eps, gemma_norm=True, sq_ld=self.sq_ld, ws=ws)
+                kernels.qgemm_packed(self.act, layer.down.p, out=self.y, rows=m, sq_ld=self.sq_ld, ws=ws)
                 kernels.rmsnorm_residual(self.y, layer.post_ff_norm, h, c.eps, gemma=True, rows=m,
                                          out_sq=self.sq_mlp)
                 sq, parts = self.sq_mlp, 1
                 continue
             kernels.qgemm_packed(self.attn, layer.o.p, epilogue="residual", residual=h, out=h, rows=m,
-                                 out_sq=self.sq_attn, ws=ws)
+                                 out_sq=self.sq_attn, sq_ld=self.sq_ld, ws=ws)
             kernels.qgemm_packed(h, layer.gate_up.p, epilogue="swiglu", out=self.act, rows=m,
                                  norm_sq=self.sq_attn, norm_parts=self.h_tiles, norm_weight=layer.post_norm,
-                                 eps=c.eps, gemma_norm=gemma, ws=ws)
+                                 eps=c.eps, gemma_norm=gemma, sq_ld=self.sq_ld, ws=ws)
             kernels.qgemm_packed(self.act, layer.down.p, epilogue="residual", residual=h, out=h, rows=m,
-                                 out_sq=self.sq_mlp, ws=ws)
+                                 out_sq=self.sq_mlp, sq_ld=self.sq_ld, ws=ws)
             sq, parts = self.sq_mlp, self.h_tiles
         if not logit_rows:
             return None
         if self.tp == 1:
             kernels.qgemm_packed(h, self.head.p, out=self.logits, rows=logit_rows, norm_sq=sq, norm_parts=parts,
-                                 norm_weight=self.final_norm, eps=c.eps, gemma_norm=gemma, ws=ws)
+                                 norm_weight=self.final_norm, eps=c.eps, gemma_norm=gemma, sq_ld=self.sq_ld, ws=ws)
             return self.logits[:logit_rows]
         lr, vl = logit_rows, c.vocab // self.tp
         kernels.qgemm_packed(h, self.head.p, out=self.logits_local, rows=lr, norm_sq=sq, norm_parts=parts,
-                             norm_weight=self.final_norm, eps=c.eps, gemma_norm=gemma, ws=ws)
+                             norm_weight=self.final_norm, eps=c.eps, gemma_norm=gemma, sq_ld=self.sq_ld, ws=ws)
         import torch.distributed as dist
         gathered = self.logits_gather[:self.tp * lr * vl]
         dist.all_gather_into_tensor(gathered, self.logits_local[:lr], group=self.group)
@@ -390,7 +392,7 @@ class QuantModel:
     def prefill(self, tokens: torch.Tensor, seq: int = 0, start: int = 0) -> None:
         """Write the KV of `tokens` (int32 on the device) at slots start.. of sequence slot `seq`."""
         total = tokens.numel()
-        step = min(self.max_rows, MAX_QGEMM_ROWS)
+        step = min(self.max_rows, MAX_SEQ_ROWS)
         for off in range(0, total, step):
             part = tokens[off:off + step].contiguous()
             meta = self._meta(part, list(range(start + off, start + off + part.numel())), seq)

@@ -444,7 +444,7 @@ def qgemm_packed_workspace_bytes(m: int, n: int, k: int) -> int:
 def qgemm_packed(x: torch.Tensor, p: Packed, *, epilogue: str = "store", residual: torch.Tensor | None = None,
                  out: torch.Tensor | None = None, rows: int | None = None, norm_sq: torch.Tensor | None = None,
                  norm_parts: int = 0, norm_weight: torch.Tensor | None = None, eps: float = 1e-6,
-                 gemma_norm: bool = False, out_sq: torch.Tensor | None = None,
+                 gemma_norm: bool = False, out_sq: torch.Tensor | None = None, sq_ld: int = 0,
                  ws: torch.Tensor | None = None) -> torch.Tensor:
     """y = x . W^T over packed weights, with an optional fused RMSNorm prologue (norm_sq/norm_weight) and
     per-tile sums of squares of the output (out_sq)."""
@@ -461,5 +461,5 @@ def qgemm_packed(x: torch.Tensor, p: Packed, *, epilogue: str = "store", residua
     ws_ptr, ws_bytes = _scratch(ws, device, qgemm_packed_workspace_bytes(m, p.n, p.k), "qgemm_packed")
     _lib.call("im_qgemm_packed", p.data.data_ptr(), x.data_ptr(), out.data_ptr(), _ptr_or_none(residual), m, p.n, p.k,
               epi, _ptr_or_none(norm_sq), norm_parts, _ptr_or_none(norm_weight), float(eps), int(gemma_norm),
-              _ptr_or_none(out_sq), ws_ptr, ws_bytes, _stream(device))
+              _ptr_or_none(out_sq), sq_ld, ws_ptr, ws_bytes, _stream(device))
     return out

@@ -322,6 +322,26 @@ def test_identical_draft_has_every_draft_accepted(cuda):
     assert dec.generated(0, prompt.numel()) == engine.greedy_decode(target, prompt, 25)
 
 
+def test_batched_speculation_beyond_32_verify_rows(cuda):
+    """7 sequences x (k + 1) = 35 verify rows: the qGEMMs take two 32-row chunks; every sequence still gets
+    exactly its own greedy tokens."""
+    b = 7
+    target = tiny("tiny-target", seed=1, sigma=0.08, max_seqs=b, max_rows=40, max_logit_rows=40)
+    draft = tiny("tiny-draft", seed=2, sigma=0.08, max_seqs=b, max_rows=16, max_logit_rows=16)
+    gen = torch.Generator().manual_seed(12)
+    prompts = [torch.randint(0, 1000, (n,), generator=gen).to(torch.int32).to(cuda) for n in (5, 9, 30, 17, 3, 22, 11)]
+    dec = engine.SpecDecoder(target, draft, k=4, batch=b)
+    dec.start(prompts, max_new=16)
+    dec.round()
+    dec.capture()
+    while not dec.done():
+        dec.run_rounds(3)
+    solo = tiny("tiny-target", seed=1, sigma=0.08)
+    for i, p in enumerate(prompts):
+        solo_dec = engine.greedy_decode(solo, p, 16)
+        assert dec.generated(i, p.numel()) == solo_dec, i
+
+
 def test_batched_speculation(cuda):
     target = tiny("tiny-target", seed=1, sigma=0.08, max_seqs=3)
     draft = tiny("tiny-draft", seed=2, sigma=0.08, max_seqs=3)

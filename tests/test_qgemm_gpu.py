@@ -273,6 +273,43 @@ def test_packed_fused_rmsnorm_and_sums_of_squares(cuda):
     assert mx <= MAX_REL and mean <= MEAN_REL, (mx, mean)
 
 
+@pytest.mark.parametrize("m", [33, 70, 160])
+def test_packed_many_rows_match_oracle(cuda, m):
+    """More than 32 rows go in chunks of 32, each exactly as a call of those rows alone."""
+    wq, s, b, x, p, x_t = packed_case(cuda, 2048, 1536, m, 40 + m)
+    got = torch_to_bf16_bits(kernels.qgemm_packed(x_t, p))
+    mx, mean = rel_errors(got, qmv.qmv(wq, s, b, x, vpt=8))
+    assert mx <= MAX_REL and mean <= MEAN_REL, (mx, mean)
+    for r0 in range(0, m, 32):
+        alone = torch_to_bf16_bits(kernels.qgemm_packed(x_t[r0:r0 + 32].contiguous(), p))
+        assert np.array_equal(alone, got[r0:r0 + 32]), r0
+    one = torch_to_bf16_bits(kernels.qgemm_packed(x_t[m - 1:].contiguous(), p))
+    assert np.array_equal(one[0], got[m - 1])
+
+
+def test_packed_many_rows_fused_norm_and_sums_of_squares(cuda):
+    """A 70-row residual GEMM's sums of squares (row stride 96) feed a 70-row normalised GEMM: equal to the
+    same two calls made 32 rows at a time."""
+    rng = np.random.default_rng(8)
+    m, h, ld = 70, 1024, 96
+    wq, s, b, x, p_o, x_t = packed_case(cuda, h, 512, m, 94)
+    res = torch.randn(m, h, device=cuda).to(torch.bfloat16)
+    sq = torch.zeros((p_o.tiles, ld), dtype=torch.float32, device=cuda)
+    h_new = kernels.qgemm_packed(x_t, p_o, epilogue="residual", residual=res, out_sq=sq, sq_ld=ld)
+    want_sq = (bf16.to_f32(torch_to_bf16_bits(h_new)).astype(np.float64) ** 2).sum(axis=1)
+    assert np.allclose(sq.sum(0).cpu().numpy()[:m], want_sq, rtol=1e-5)
+    _, _, _, _, p2, _ = packed_case(cuda, 768, h, m, 95)
+    nw = torch.from_numpy(bf16.from_f32(rng.normal(1, 0.1, h).astype(np.float32)).view(np.int16)).view(torch.bfloat16)
+    nw = nw.to(cuda)
+    big = kernels.qgemm_packed(h_new, p2, norm_sq=sq, norm_parts=p_o.tiles, norm_weight=nw, sq_ld=ld)
+    for r0 in range(0, m, 32):
+        n = min(32, m - r0)
+        sq_c = sq[:, r0:r0 + n].contiguous()
+        part = kernels.qgemm_packed(h_new[r0:r0 + n].contiguous(), p2, norm_sq=sq_c, norm_parts=p_o.tiles,
+                                    norm_weight=nw, sq_ld=n)
+        assert torch.equal(part.view(torch.int16), big[r0:r0 + n].view(torch.int16)), r0
+
+
 @pytest.mark.parametrize("epi", ["swiglu", "geglu"])
 def test_packed_gated_epilogues(cuda, epi):
     from oracle import model as om
