@@ -13,15 +13,15 @@ streams the full 3.6 GB of weights, far more than the 126 MB L2, so no flush is 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload spec_decode|verify_step|stochastic|tree|tp]
 
---workload stochastic: BASELINE config 3's round -- Qwen3-4B + 0.6B, temperature 0.7, top-p 0.95, k = 4,
-rejection sampling with residual resampling on Philox -- over 6 concurrent sequences with prompt lengths drawn
-uniformly from [128, 2048] (seed 0): 6 x 5 = 30 verify rows, the most one qGEMM call takes (the configuration's
-32 sequences need 160 rows). --workload tree: config 4's tree verification on Gemma-3-12B shapes (48 layers,
-hidden 3840, 16/8 heads, head_dim 256, GeGLU 15360, vocab 262144) with a Gemma-3-1B-shaped draft, a 4 x 2 x 2
-draft tree verified as root + 28 nodes = 29 rows, one sequence, a 1024-token prompt. --workload tp (under
-torchrun, N ranks): config 5a -- Gemma-3-27B shapes tensor-parallel over the N GPUs (NCCL all-reduce after o and
-down, all-gathered vocabulary-sharded head) with a replicated Gemma-3-1B-shaped draft, greedy, k = 4, 6
-sequences with 512-token prompts; one job over all ranks, so `value` is that job's tokens/s (strong scaling).
+--workload stochastic: BASELINE config 3's round -- Qwen3-4B + 0.6B, temperature 0.7, top-p 0.95, k = 4, rejection
+sampling with residual resampling on Philox -- over 32 concurrent sequences with prompt lengths drawn uniformly
+from [128, 2048] (seed 0): 32 x 5 = 160 verify rows per qGEMM call. --workload tree: config 4's tree verification
+on Gemma-3-12B shapes (48 layers, hidden 3840, 16/8 heads, head_dim 256, GeGLU 15360, vocab 262144) with a
+Gemma-3-1B-shaped draft, a 4 x 2 x 2 draft tree verified as root + 28 nodes = 29 rows per sequence, 8 sequences,
+1024-token prompts. --workload tp (under torchrun, N ranks): config 5a -- Gemma-3-27B shapes tensor-parallel over
+the N GPUs (NCCL all-reduce after o and down, all-gathered vocabulary-sharded head) with a replicated
+Gemma-3-1B-shaped draft, greedy, k = 4, 64 sequences with 512-token prompts; one job over all ranks, so `value` is
+that job's tokens/s (strong scaling).
 
 --impl reference times the CPU implementation of the same round (the oracle port in oracle/spec.py: the
 reference's greedy round with projections dequantised and dotted in float32 by OpenMP C code) on the box's host
@@ -451,44 +451,46 @@ def run_rounds_workload(args, world: int, rank: int, local: int, kind: str) -> N
         import torch.distributed as dist
         tp_group = dist.group.WORLD
     if kind == "tp":
-        b, ctx = 6, 512 + 512
+        b, ctx = 64, 512 + 256
         gen = torch.Generator().manual_seed(0)  # the same sequences on every rank: one tensor-parallel job
-        target = QuantModel(PRESETS["gemma3-27b"], device, seed=0, max_ctx=ctx, max_seqs=b, max_rows=32,
-                            max_logit_rows=32, tp=world, rank=rank, group=tp_group)
-        draft = QuantModel(PRESETS["gemma3-1b"], device, seed=1, max_ctx=ctx, max_seqs=b, max_rows=16,
-                           max_logit_rows=16)
+        target = QuantModel(PRESETS["gemma3-27b"], device, seed=0, max_ctx=ctx, max_seqs=b, max_rows=b * (K_DRAFTS + 1),
+                            max_logit_rows=b * (K_DRAFTS + 1), tp=world, rank=rank, group=tp_group)
+        draft = QuantModel(PRESETS["gemma3-1b"], device, seed=1, max_ctx=ctx, max_seqs=b, max_rows=2 * b,
+                           max_logit_rows=2 * b)
         dec = SpecDecoder(target, draft, k=K_DRAFTS, batch=b)
         prompts = [torch.randint(0, target.cfg.vocab, (512,), generator=gen, dtype=torch.int32) for _ in range(b)]
         round_bytes = K_DRAFTS * draft.cfg.weight_bytes() + target.cfg.weight_bytes() // world
         workload = (f"BASELINE config 5a: Gemma-3-27B shapes (4-bit) tensor-parallel over {world} GPU(s), NCCL "
                     "all-reduce after o and down, vocabulary-sharded head all-gathered; replicated Gemma-3-1B-shaped "
-                    "draft; greedy, k 4, 6 sequences (30 verify rows; the configuration's batch 64 needs 320 rows "
-                    "per qGEMM call), 512-token prompts")
-        metric = "accepted tokens/s (spec decode, Gemma-3-27B tensor-parallel + 1B draft, k=4, 6 sequences)"
+                    "draft; greedy, k 4, 64 sequences (320 verify rows per qGEMM call), 512-token prompts")
+        metric = "accepted tokens/s (spec decode, Gemma-3-27B tensor-parallel + 1B draft, k=4, 64 sequences)"
     elif kind == "stochastic":
-        b, ctx = 6, 2048 + 256
+        b, ctx = 32, 2048 + 256
         lens = torch.randint(128, 2049, (b,), generator=gen).tolist()
-        target = QuantModel(PRESETS["qwen3-4b"], device, seed=0, max_ctx=ctx, max_seqs=b, max_rows=32,
-                            max_logit_rows=32)
-        draft = QuantModel(PRESETS["qwen3-0.6b"], device, seed=1, max_ctx=ctx, max_seqs=b, max_rows=16,
-                           max_logit_rows=16)
+        target = QuantModel(PRESETS["qwen3-4b"], device, seed=0, max_ctx=ctx, max_seqs=b, max_rows=b * (K_DRAFTS + 1),
+                            max_logit_rows=b * (K_DRAFTS + 1))
+        draft = QuantModel(PRESETS["qwen3-0.6b"], device, seed=1, max_ctx=ctx, max_seqs=b, max_rows=2 * b,
+                           max_logit_rows=2 * b)
         dec = SpecDecoder(target, draft, k=K_DRAFTS, batch=b, sampling=Sampling(0.7, 0.95, 0))
         prompts = [torch.randint(0, target.cfg.vocab, (n,), generator=gen, dtype=torch.int32) for n in lens]
         round_bytes = K_DRAFTS * draft.cfg.weight_bytes() + target.cfg.weight_bytes()
         workload = ("BASELINE config 3: stochastic speculative decoding (T 0.7, top-p 0.95, k 4, rejection sampling "
-                    "with residual resample on Philox), Qwen3-4B + Qwen3-0.6B 4-bit, 6 sequences (30 verify rows; "
-                    "the configuration's 32 need 160 rows per qGEMM call), prompts U[128, 2048]")
-        metric = "accepted tokens/s (stochastic spec decode, Qwen3-4B + 0.6B, k=4, 6 sequences)"
+                    "with residual resample on Philox), Qwen3-4B + Qwen3-0.6B 4-bit, 32 concurrent sequences (160 "
+                    "verify rows per qGEMM call), paged KV with 16-token pages, prompts U[128, 2048]")
+        metric = "accepted tokens/s (stochastic spec decode, Qwen3-4B + 0.6B, k=4, 32 sequences)"
     else:
-        ctx = 1024 + 128 + 64
-        target = QuantModel(PRESETS["gemma3-12b"], device, seed=0, max_ctx=ctx, max_rows=32, max_logit_rows=32)
-        draft = QuantModel(PRESETS["gemma3-1b"], device, seed=1, max_ctx=ctx, max_rows=32, max_logit_rows=32)
-        dec = TreeDecoder(target, draft, branch=(4, 2, 2))
-        prompts = [torch.randint(0, target.cfg.vocab, (1024,), generator=gen, dtype=torch.int32)]
+        b, ctx = 8, 1024 + 128 + 64
+        target = QuantModel(PRESETS["gemma3-12b"], device, seed=0, max_ctx=ctx, max_seqs=b, max_rows=29 * b,
+                            max_logit_rows=29 * b)
+        draft = QuantModel(PRESETS["gemma3-1b"], device, seed=1, max_ctx=ctx, max_seqs=b, max_rows=8 * b,
+                           max_logit_rows=8 * b)
+        dec = TreeDecoder(target, draft, branch=(4, 2, 2), batch=b)
+        prompts = [torch.randint(0, target.cfg.vocab, (1024,), generator=gen, dtype=torch.int32) for _ in range(b)]
         round_bytes = 3 * draft.cfg.weight_bytes() + target.cfg.weight_bytes()
         workload = ("BASELINE config 4: greedy tree verification, Gemma-3-12B shapes (4-bit) with a Gemma-3-1B-shaped "
-                    "draft, 4 x 2 x 2 draft tree verified as root + 28 nodes (29 rows), 1 sequence, 1024-token prompt")
-        metric = "accepted tokens/s (tree spec decode, Gemma-3-12B + 1B draft, 4x2x2 tree, 1 sequence)"
+                    "draft, 4 x 2 x 2 draft tree verified as root + 28 nodes (29 rows) per sequence, 8 sequences "
+                    "(232 verify rows per qGEMM call), 1024-token prompts")
+        metric = "accepted tokens/s (tree spec decode, Gemma-3-12B + 1B draft, 4x2x2 tree, 8 sequences)"
     room = max(8, ctx - max(p.numel() for p in prompts) - dec.reserve - 8)
     dec.start([p.to(device) for p in prompts], max_new=room)
     dec.round()
@@ -504,7 +506,9 @@ def run_rounds_workload(args, world: int, rank: int, local: int, kind: str) -> N
     clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    torch.cuda.nvtx.range_push("timed_rounds")
     dec.run_rounds(args.steps)
+    torch.cuda.nvtx.range_pop()
     e1.record(stream)
     torch.cuda.synchronize()
     barrier(world)

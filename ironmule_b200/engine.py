@@ -619,68 +619,99 @@ class SpecDecoder:
 
 
 class TreeDecoder(SpecDecoder):
-    """Greedy tree speculation of one sequence, the round on the device.
+    """Greedy tree speculation of `batch` sequences, the round on the device.
 
     The draft tree has a static shape: `branch[L]` children per node at depth L + 1 (default 4 x 2 x 2: 4 + 8 +
     16 = 28 nodes). A round: prepare the rows (im_tree_prepare); draft pass 0 re-feeds the last two committed
-    tokens and its top-branch[0] tokens become depth-1 nodes; each further draft pass runs one level's nodes
-    (tree-masked attention: a node sees the committed prefix and its own ancestors) and its rows' top-k become
-    the next level; one verify forward of the target over the root and every node (1 + 28 = 29 rows); the
-    target's argmax per row and the walk down the tree (im_tree_accept) keep the longest agreeing path plus the
-    target's own token; the accepted nodes' K/V move to the committed slots in both models (im_tree_compact);
-    commit. Every kernel is row-invariant and a node sees exactly its path, so the tokens equal plain greedy
-    decoding's. BASELINE's "16-node ... M=16" cannot describe a 4 x 2 x 2 tree; this build verifies the whole
-    tree (29 rows per sequence, within the 32 rows of one qGEMM call), so one sequence per decoder.
+    tokens of every sequence and its top-branch[0] tokens become depth-1 nodes; each further draft pass runs one
+    level's nodes of every sequence (tree-masked attention: a node sees its sequence's committed prefix and its
+    own ancestors) and its rows' top-k become the next level; one verify forward of the target over every
+    sequence's root and nodes (1 + 28 = 29 rows per sequence); the target's argmax per row and the walk down each
+    tree (im_tree_accept) keep the longest agreeing path plus the target's own token; the accepted nodes' K/V move
+    to the committed slots in both models (im_tree_compact); commit. A level's rows are gathered from the
+    per-sequence tree rows and the top-k children scattered back with fixed index maps. Every kernel is
+    row-invariant and a node sees exactly its path, so the tokens equal plain greedy decoding's. BASELINE's
+    "16-node ... M=16" cannot describe a 4 x 2 x 2 tree; this build verifies the whole tree (29 rows per sequence).
     """
 
-    def __init__(self, target: QuantModel, draft: QuantModel, *, branch: tuple[int, ...] = (4, 2, 2)):
+    def __init__(self, target: QuantModel, draft: QuantModel, *, branch: tuple[int, ...] = (4, 2, 2),
+                 batch: int = 1):
         levels = len(branch)
         counts = [math.prod(branch[:i + 1]) for i in range(levels)]
         nodes = sum(counts)
         rows = 1 + nodes
-        if rows > min(target.max_rows, MAX_QGEMM_ROWS, target.max_logit_rows):
-            raise ValueError(f"a {rows}-row tree exceeds the target's per-forward limit")
-        if max(counts[:-1] + [2]) > min(draft.max_rows, draft.max_logit_rows):
+        if rows > MAX_SEQ_ROWS:
+            raise ValueError(f"a {rows}-row tree exceeds the {MAX_SEQ_ROWS} rows of one sequence per forward")
+        if batch * rows > min(target.max_rows, MAX_QGEMM_ROWS, target.max_logit_rows):
+            raise ValueError(f"{batch} trees of {rows} rows exceed the target's per-forward limit")
+        if batch * max(counts[:-1] + [2]) > min(draft.max_rows, draft.max_logit_rows):
             raise ValueError("a tree level exceeds the draft model's per-forward limit")
-        super().__init__(target, draft, k=levels, batch=1)
+        super().__init__(target, draft, k=levels, batch=batch)
         self.branch, self.counts, self.nodes, self.rows = tuple(branch), counts, nodes, rows
         self.first = [sum(counts[:i]) for i in range(levels)]
         self.reserve = nodes
         dev, i32 = self.device, dict(dtype=torch.int32, device=self.device)
-        self.t_tok = torch.zeros((rows,), **i32)
-        self.t_pos = torch.zeros((rows,), **i32)
-        self.t_slot = torch.zeros((rows,), **i32)
-        self.t_mask = torch.zeros((rows,), dtype=torch.int64, device=dev)
-        self.t_base = torch.zeros((1,), **i32)
-        self.t_argmax = torch.zeros((rows,), **i32)
-        self.acc_node = torch.zeros((levels,), **i32)
-        self.seq_t = torch.zeros((rows,), **i32)
-        self.rows_t = torch.tensor([0, rows], **i32)
-        self.rows_l = [torch.tensor([0, c], **i32) for c in counts]
-        self.ws_topk = kernels.workspace(kernels.topk_workspace_bytes(max(counts), target.cfg.vocab, max(branch)), dev)
+        b = batch
+        self.t_tok = torch.zeros((b * rows,), **i32)
+        self.t_pos = torch.zeros((b * rows,), **i32)
+        self.t_slot = torch.zeros((b * rows,), **i32)
+        self.t_mask = torch.zeros((b * rows,), dtype=torch.int64, device=dev)
+        self.t_base = torch.zeros((b,), **i32)
+        self.t_argmax = torch.zeros((b * rows,), **i32)
+        self.acc_node = torch.zeros((b * levels,), **i32)
+        self.seq_t = torch.arange(b, **i32).repeat_interleave(rows)
+        self.rows_t = torch.arange(0, b * rows + 1, rows, **i32)
+        ar = torch.arange(b, dtype=torch.int64, device=dev)
+        # children of level-L parents (L = -1: the roots) -> their tree rows, parent-major
+        self.child_idx = []
+        for lv in range(levels):
+            parents = 1 if lv == 0 else counts[lv - 1]
+            i = torch.arange(parents * branch[lv], dtype=torch.int64, device=dev)
+            self.child_idx.append((ar[:, None] * rows + 1 + self.first[lv] + i[None, :]).reshape(-1))
+        # the draft pass over level lv - 1's nodes: gather maps, per-level row buffers and sequence groups
+        self.level = []
+        for lv in range(1, levels):
+            cnt = counts[lv - 1]
+            idx = (ar[:, None] * rows + 1 + self.first[lv - 1] + torch.arange(cnt, device=dev)[None, :]).reshape(-1)
+            bufs = dict(tok=torch.zeros((b * cnt,), **i32), pos=torch.zeros((b * cnt,), **i32),
+                        slot=torch.zeros((b * cnt,), **i32),
+                        mask=torch.zeros((b * cnt,), dtype=torch.int64, device=dev),
+                        seq=torch.arange(b, **i32).repeat_interleave(cnt),
+                        seq_rows=torch.arange(0, b * cnt + 1, cnt, **i32), idx=idx, cnt=cnt)
+            self.level.append(bufs)
+        self.children = torch.zeros((b * max(counts) + b * branch[0],), **i32)
+        self.ws_topk = kernels.workspace(
+            kernels.topk_workspace_bytes(b * max(counts + [1]), target.cfg.vocab, max(branch)), dev)
 
     def round(self) -> None:
-        t, d, br = self.target, self.draft, self.branch
-        cap = self.cap
+        t, d, br, b = self.target, self.draft, self.branch, self.batch
+        cap, v = self.cap, d.cfg.vocab
         kernels.tree_prepare(self.hist, self.n, br, cap, self.d0_tok, self.d0_pos, self.t_tok, self.t_pos, self.t_slot,
                              self.t_mask, self.t_base)
-        meta = RowMeta(self.d0_tok, 1, self.d0_pos, self.seq_d0, self.rows_d0, 2, 2)
-        logits = d.forward(meta, max_kv_len=cap, logit_rows=2)
-        kernels.topk_rows(logits[1:], br[0], rows=1, out=self.t_tok[1:], ws=self.ws_topk)
+        meta = RowMeta(self.d0_tok, 1, self.d0_pos, self.seq_d0, self.rows_d0, 2 * b, 2)
+        logits = d.forward(meta, max_kv_len=cap, logit_rows=2 * b)
+        kids = self.children[:b * br[0]]
+        kernels.topk_rows(logits[1:], br[0], rows=b, ld=2 * v, out=kids, ws=self.ws_topk)
+        self.t_tok.index_copy_(0, self.child_idx[0], kids)
         for lv in range(1, len(br)):
-            s0, cnt = 1 + self.first[lv - 1], self.counts[lv - 1]
-            meta = RowMeta(self.t_tok[s0:], 1, self.t_pos[s0:], self.seq_t, self.rows_l[lv - 1], cnt, cnt,
-                           slot=self.t_slot[s0:], tree_mask=self.t_mask[s0:], tree_base=self.t_base)
-            logits = d.forward(meta, max_kv_len=cap, logit_rows=cnt)
-            kernels.topk_rows(logits, br[lv], rows=cnt, out=self.t_tok[1 + self.first[lv]:], ws=self.ws_topk)
-        meta = RowMeta(self.t_tok, 1, self.t_pos, self.seq_t, self.rows_t, self.rows, self.rows, slot=self.t_slot,
+            L = self.level[lv - 1]
+            for key, src in (("tok", self.t_tok), ("pos", self.t_pos), ("slot", self.t_slot), ("mask", self.t_mask)):
+                torch.index_select(src, 0, L["idx"], out=L[key])
+            n = b * L["cnt"]
+            meta = RowMeta(L["tok"], 1, L["pos"], L["seq"], L["seq_rows"], n, L["cnt"], slot=L["slot"],
+                           tree_mask=L["mask"], tree_base=self.t_base)
+            logits = d.forward(meta, max_kv_len=cap, logit_rows=n)
+            kids = self.children[:n * br[lv]]
+            kernels.topk_rows(logits, br[lv], rows=n, out=kids, ws=self.ws_topk)
+            self.t_tok.index_copy_(0, self.child_idx[lv], kids)
+        meta = RowMeta(self.t_tok, 1, self.t_pos, self.seq_t, self.rows_t, b * self.rows, self.rows, slot=self.t_slot,
                        tree_mask=self.t_mask, tree_base=self.t_base)
-        logits = t.forward(meta, max_kv_len=cap, logit_rows=self.rows)
-        kernels.argmax_rows(logits, out=self.t_argmax, ws=t.ws_argmax, rows=self.rows)
-        kernels.tree_accept(self.t_argmax, self.t_tok, 1, br, self.out_tokens, self.out_count, self.acc_node)
-        kernels.tree_compact(t.k_cache, t.v_cache, t.page_table, self.t_base, self.acc_node, len(br), len(br), 1)
-        kernels.tree_compact(d.k_cache, d.v_cache, d.page_table, self.t_base, self.acc_node, len(br), len(br) - 1, 1)
-        kernels.spec_commit(self.hist, self.n, self.target_len, 1, len(br), self.out_tokens, self.out_count,
+        logits = t.forward(meta, max_kv_len=cap, logit_rows=b * self.rows)
+        kernels.argmax_rows(logits, out=self.t_argmax, ws=t.ws_argmax, rows=b * self.rows)
+        kernels.tree_accept(self.t_argmax, self.t_tok, b, br, self.out_tokens, self.out_count, self.acc_node)
+        kernels.tree_compact(t.k_cache, t.v_cache, t.page_table, self.t_base, self.acc_node, len(br), len(br), b)
+        kernels.tree_compact(d.k_cache, d.v_cache, d.page_table, self.t_base, self.acc_node, len(br), len(br) - 1, b)
+        kernels.spec_commit(self.hist, self.n, self.target_len, b, len(br), self.out_tokens, self.out_count,
                             self.stats)
 
     def launches_per_round(self) -> int:

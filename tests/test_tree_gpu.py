@@ -95,3 +95,26 @@ def test_identical_draft_accepts_full_depth(cuda):
     assert st.rounds == 5 and st.accepted == 15 and st.tokens == 20
     solo = tiny("tiny-target", 1)
     assert dec.generated(0, prompt.numel()) == engine.greedy_decode(solo, prompt, 20)
+
+
+@pytest.mark.parametrize("branch", [(4, 2, 2), (2, 3)])
+def test_batched_trees_change_no_answer(cuda, branch):
+    """Several sequences of different lengths in one tree round: each level's rows gathered across the
+    sequences, the verify forward over every sequence's tree; each sequence still returns its own greedy
+    tokens."""
+    b = 3
+    target = engine.QuantModel(engine.PRESETS["tiny-target"], "cuda", seed=1, sigma=0.08, max_ctx=256, max_seqs=b,
+                               max_rows=32 * b, max_logit_rows=32 * b)
+    draft = engine.QuantModel(engine.PRESETS["tiny-draft"], "cuda", seed=2, sigma=0.08, max_ctx=256, max_seqs=b,
+                              max_rows=32 * b, max_logit_rows=32 * b)
+    gen = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 1000, (n,), generator=gen).to(torch.int32).to(cuda) for n in (21, 9, 40)]
+    dec = engine.TreeDecoder(target, draft, branch=branch, batch=b)
+    dec.start(prompts, max_new=30)
+    dec.round()
+    dec.capture()
+    while not dec.done():
+        dec.run_rounds(2)
+    for s, p in enumerate(prompts):
+        solo = tiny("tiny-target", 1)
+        assert dec.generated(s, p.numel()) == engine.greedy_decode(solo, p, 30), s
