@@ -123,8 +123,10 @@ int im_qgemm_tma_status(const void* workspace, uint32_t* status);
  * im_qgemm_pack_w4g64 converts MLX-layout w/scales/biases [N, K] into `packed` (16-byte aligned,
  * im_qgemm_packed_bytes(N, K) bytes): rows padded to 32-row tiles, one contiguous 1152-byte unit per
  * (tile, 64-group) holding that tile's codes in lane order and its 32 scales/biases.
- * im_qgemm_packed computes the same product and epilogues as im_qgemm_w4g64_ex from it for M <= 320 rows (in
- * chunks of 32, each computed exactly as a call of those rows alone), and can fuse the RMSNorm that precedes a
+ * im_qgemm_packed computes the same product and epilogues as im_qgemm_w4g64_ex from it for M <= 320 rows (every
+ * row exactly as a call of at most 32 rows computes it: up to 32 rows on the warp MMA, more on the tcgen05
+ * tensor cores with the same k-steps and fp32 order, activations staged as 64-row tiles in the workspace),
+ * and can fuse the RMSNorm that precedes a
  * projection: with norm_weight != NULL, x is the raw residual stream and each row is normalised on the way in
  * (x * 1/sqrt(sum(x^2)/K + eps) * w', w' = w or 1 + w when gemma_norm), its sum of squares taken from
  * norm_sq[p * sq_ld + m] summed over p < norm_parts (per-tile partial sums). With out_sq != NULL, a
@@ -141,6 +143,9 @@ size_t im_qgemm_packed_workspace_bytes(int64_t M, int64_t N, int64_t K);
 /* Tuning hook of the K-split policy: a forced split (0 = automatic), the CTA count the automatic policy aims
  * for, and its largest split. Process-wide; changes workspace sizes, so set it before sizing workspaces. */
 int im_qgemm_packed_tune(int split_override, int target_ctas, int max_split);
+/* The error word of a workspace last used by a call of more than 32 rows (the tensor-core kernel): 0 when
+ * every bounded wait of that kernel completed, 1 when one ran out. Synchronous (reads device memory). */
+int im_qgemm_packed_status(const void* workspace);
 int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* y, const uint16_t* residual, int64_t M, int64_t N,
                     int64_t K, int epilogue, const float* norm_sq, int64_t norm_parts, const uint16_t* norm_weight,
                     float eps, int gemma_norm, float* out_sq, int64_t sq_ld, void* workspace, size_t workspace_bytes,
@@ -246,6 +251,9 @@ int im_attention_paged(const uint16_t* q, const uint16_t* k_cache, const uint16_
                        float scale, uint16_t* out, void* workspace, size_t workspace_bytes, void* stream);
 size_t im_attention_workspace_bytes(int64_t B, int64_t max_rows_per_seq, int64_t Hq, int64_t Hkv, int64_t D,
                                     int64_t max_kv_len, int64_t keys_per_split);
+/* Tuning hook of the attention launch: the waves of resident CTAs it aims for when it gives a (sequence,
+ * kv head) group several CTAs. Process-wide; scheduling only -- every result is the same at any value. */
+int im_attention_tune(int waves);
 /*
  * The same attention starting from the packed projection rows qkv [M, (Hq + 2 Hkv) D] (q heads, k heads,
  * v heads): q and the new keys get RMSNorm (q_norm / k_norm; w or 1 + w when gemma_style) and RoPE at

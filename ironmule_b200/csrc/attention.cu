@@ -18,10 +18,12 @@
 // (row, kv head) writes them to the cache. Keys that no row of this launch writes are staged with cp.async
 // before the kernel waits for the previous kernel, so their loads overlap it.
 //
-// Work split: grid (key splits, kv heads, sequences x query blocks). A CTA owns up to NQ query vectors
-// (rows x the kv head's query heads) and one split of `kpc` keys at fixed absolute positions, walked in
-// 64-key blocks staged in shared memory with an online softmax. CTAs publish (acc, max, sum) partials; the
-// last CTA of a (sequence, kv head, query block) merges the splits in split order. A row's result depends
+// Work split: grid (CTAs per group, kv heads, sequences x query blocks). A CTA owns up to NQ query vectors
+// (rows x the kv head's query heads) and walks splits of `kpc` keys at fixed absolute positions (split x, x +
+// gridDim.x, ...), each in 64-key blocks staged in shared memory with an online softmax started afresh per
+// split. Every split publishes its (acc, max, sum) partial; the last CTA of a (sequence, kv head, query block)
+// to finish merges the splits in split order. The host picks the CTAs per group from the occupancy and the
+// number of groups (one CTA per split for a single sequence, several splits per CTA for large batches). A row's result depends
 // only on its own query, its mask and the KV -- not on how many rows or sequences share the launch.
 #include <math.h>
 
@@ -153,7 +155,9 @@ attn_kernel(AttnArgs a) {
   }
   // Before the wait (fused mode) only data that the previous kernel (the qkv projection) does not write is
   // read: the row metadata, the page table and the keys of slots no row of this launch writes.
-  const int split = blockIdx.x, kvh = blockIdx.y;
+  // The CTA walks splits blockIdx.x, blockIdx.x + gridDim.x, ... of its (sequence, kv head, query block); each
+  // split is computed and published exactly as if it had a CTA of its own.
+  const int kvh = blockIdx.y;
   const int b = blockIdx.z / a.qblocks, qb = blockIdx.z % a.qblocks;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = a.Hq / a.Hkv;
@@ -161,12 +165,12 @@ attn_kernel(AttnArgs a) {
   const int prow = a.seq_slot ? a.seq_slot[b] : b;
   const int q0 = qb * NQ;
   const int nq = max(0, min(NQ, nr * G - q0));
+  const int stride_x = gridDim.x;
 
   const int tbase = a.tree_mask ? a.tree_base[b] : 0;
-  const int k_begin = split * a.kpc;
   // Row metadata with every load in flight at once: warp 0 reads the rows' slots (kv length = one past the
-  // largest; the rows whose slot falls in this split are this launch's new keys there), the other threads the
-  // query vectors' limits and masks.
+  // largest; the rows whose slot falls in one of this CTA's splits are this launch's new keys there), the
+  // other threads the query vectors' limits and masks.
   if (warp == 0) {
     int mx = -1, n = 0;
     for (int r0l = 0; r0l < nr; r0l += 32) {
@@ -177,7 +181,7 @@ attn_kernel(AttnArgs a) {
       for (int o = 16; o > 0; o >>= 1) m2 = max(m2, __shfl_xor_sync(0xffffffffu, m2, o));
       mx = max(mx, m2);
       if constexpr (FUSED) {
-        const bool isnew = slot >= k_begin && slot < k_begin + a.kpc;
+        const bool isnew = slot >= 0 && (slot / a.kpc) % stride_x == (int)blockIdx.x;
         const unsigned ball = __ballot_sync(0xffffffffu, isnew);
         const int idx = n + __popc(ball & ((1u << lane) - 1u));
         if (isnew && idx < AT_MAXNEW) {
@@ -209,8 +213,9 @@ attn_kernel(AttnArgs a) {
   }
   __syncthreads();
   const int kv_len = sm.kv_len;
-  const int k_end = min(kv_len, k_begin + a.kpc);
-  const bool active = nq > 0 && k_begin < k_end;
+  const bool any = nq > 0 && (int)blockIdx.x * a.kpc < kv_len;  // this CTA has at least one non-empty split
+  int k_begin = blockIdx.x * a.kpc;
+  int k_end = min(kv_len, k_begin + a.kpc);
 
   // stage keys [kb0, kb0 + 64): K as bf16 pairs and V; slots written by this launch come from nk/nv later
   auto stage_old = [&](int kb0) {
@@ -256,12 +261,12 @@ attn_kernel(AttnArgs a) {
     }
   };
 
-  if (active) stage_old(k_begin);
+  if (any) stage_old(k_begin);
 
   if constexpr (FUSED) {
     pdl_wait();
     pdl_trigger();
-    if (active) {
+    if (any) {
       const int stride = (a.Hq + 2 * a.Hkv) * D;
       // this CTA's query vectors: RMSNorm + RoPE, rounded to bf16 as the unfused path stores them; a warp
       // loads all of its vectors before computing any
@@ -291,7 +296,7 @@ attn_kernel(AttnArgs a) {
           }
         }
       }
-      // the new rows' keys and values of this split (the first query block's CTA also writes them out)
+      // the new rows' keys and values of this CTA's splits (the first query block's CTA also writes them out)
       for (int n = warp; n < sm.nnew; n += AT_THREADS / 32) {
         const int row = sm.new_row[n], slot = sm.new_slot[n];
         const uint16_t* src = a.qkv + (size_t)row * stride + (a.Hq + kvh) * D;
@@ -339,155 +344,176 @@ attn_kernel(AttnArgs a) {
 #pragma unroll
       for (int e = 0; e < 4; e++) o_acc[mt][nt][e] = 0.f;
   const int g = lane >> 2, t = lane & 3;
+  const size_t group = ((size_t)b * a.Hkv + kvh) * a.qblocks + qb;
 
-  for (int kb0 = k_begin; kb0 < k_end && active; kb0 += AT_KB) {
-    if (kb0 != k_begin) {
-      __syncthreads();  // the previous block's K/V and probabilities are consumed
-      stage_old(kb0);
-      fill_new();
-    }
-    cp_async_wait_all();
-    __syncthreads();
-    // scores
-    {
-      float sacc[MT][2][4];
+  for (int split = blockIdx.x; any && split * a.kpc < kv_len; split += stride_x) {
+    if (split != (int)blockIdx.x) {
+      // the previous split's probabilities, K/V and statistics are consumed and published
+      __syncthreads();
+      k_begin = split * a.kpc;
+      k_end = min(kv_len, k_begin + a.kpc);
+      for (int i = tid; i < NQ; i += AT_THREADS) {
+        sm.m[i] = -INFINITY;
+        sm.l[i] = 0.f;
+      }
+      for (int i = tid; i < Smem::QM; i += AT_THREADS) sm.alpha[i] = 0.f;
 #pragma unroll
       for (int mt = 0; mt < MT; mt++)
 #pragma unroll
-        for (int nt = 0; nt < 2; nt++)
+        for (int nt = 0; nt < NTO; nt++)
 #pragma unroll
-          for (int e = 0; e < 4; e++) sacc[mt][nt][e] = 0.f;
-      const int n0 = warp * 16;
+          for (int e = 0; e < 4; e++) o_acc[mt][nt][e] = 0.f;
+      stage_old(k_begin);
+      fill_new();
+    }
+    for (int kb0 = k_begin; kb0 < k_end; kb0 += AT_KB) {
+      if (kb0 != k_begin) {
+        __syncthreads();  // the previous block's K/V and probabilities are consumed
+        stage_old(kb0);
+        fill_new();
+      }
+      cp_async_wait_all();
+      __syncthreads();
+      // scores
+      {
+        float sacc[MT][2][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+          for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) sacc[mt][nt][e] = 0.f;
+        const int n0 = warp * 16;
 #pragma unroll 4
-      for (int kk = 0; kk < D / 16; kk++) {
-        uint32_t bk[2][2];
+        for (int kk = 0; kk < D / 16; kk++) {
+          uint32_t bk[2][2];
 #pragma unroll
-        for (int nt = 0; nt < 2; nt++) {
-          bk[nt][0] = sm.ks[n0 + nt * 8 + g][kk * 8 + t];
-          bk[nt][1] = sm.ks[n0 + nt * 8 + g][kk * 8 + 4 + t];
+          for (int nt = 0; nt < 2; nt++) {
+            bk[nt][0] = sm.ks[n0 + nt * 8 + g][kk * 8 + t];
+            bk[nt][1] = sm.ks[n0 + nt * 8 + g][kk * 8 + 4 + t];
+          }
+#pragma unroll
+          for (int mt = 0; mt < MT; mt++) {
+            const uint32_t* q0r = reinterpret_cast<const uint32_t*>(&sm.qs[mt * 16 + g][kk * 16 + 2 * t]);
+            const uint32_t* q8r = reinterpret_cast<const uint32_t*>(&sm.qs[mt * 16 + g + 8][kk * 16 + 2 * t]);
+            const uint32_t a0 = q0r[0], a1 = q8r[0], a2 = q0r[4], a3 = q8r[4];
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++) mma_bf16(sacc[mt][nt], a0, a1, a2, a3, bk[nt][0], bk[nt][1]);
+          }
+        }
+        // scale and mask into sm.s
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+          for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              const int qi = mt * 16 + g + (e >> 1) * 8;
+              const int j = n0 + nt * 8 + 2 * t + (e & 1);
+              if (qi < nq) {
+                const int slot = kb0 + j;
+                const int lim = sm.row_slot[qi];
+                bool vis = slot < k_end && slot <= lim;
+                if (a.window > 0) vis = vis && slot > lim - a.window;
+                if (a.tree_mask && slot >= tbase) {
+                  const int node = slot - tbase;
+                  vis = vis && node < 64 && ((sm.tmask[qi] >> node) & 1ull);
+                }
+                sm.s[qi][j] = vis ? sacc[mt][nt][e] * a.scale : -INFINITY;
+              }
+            }
+      }
+      __syncthreads();
+      // online softmax per query vector: warp w takes w, w+4, ...; p goes out as bf16 high + low parts
+      for (int qi = warp; qi < nq; qi += AT_THREADS / 32) {
+        const float s0 = sm.s[qi][lane], s1 = sm.s[qi][lane + 32];
+        float bm = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+        const float mo = sm.m[qi];
+        const float mn = fmaxf(mo, bm);
+        const float p0 = mn == -INFINITY ? 0.f : expf(s0 - mn);
+        const float p1 = mn == -INFINITY ? 0.f : expf(s1 - mn);
+        const float ps = warp_sum(p0 + p1);
+        const uint16_t h0 = to_bf(p0), h1 = to_bf(p1);
+        sm.ph[qi][lane] = h0;
+        sm.ph[qi][lane + 32] = h1;
+        sm.pl[qi][lane] = to_bf(p0 - bf(h0));
+        sm.pl[qi][lane + 32] = to_bf(p1 - bf(h1));
+        if (lane == 0) {
+          const float al = mo == -INFINITY ? 0.f : expf(mo - mn);
+          sm.alpha[qi] = al;
+          sm.l[qi] = sm.l[qi] * al + ps;
+          sm.m[qi] = mn;
+        }
+      }
+      __syncthreads();
+      // O = alpha O + P V
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++) {
+        const float al0 = sm.alpha[mt * 16 + g], al8 = sm.alpha[mt * 16 + g + 8];
+#pragma unroll
+        for (int nt = 0; nt < NTO; nt++) {
+          o_acc[mt][nt][0] *= al0;
+          o_acc[mt][nt][1] *= al0;
+          o_acc[mt][nt][2] *= al8;
+          o_acc[mt][nt][3] *= al8;
+        }
+      }
+#pragma unroll
+      for (int kk = 0; kk < AT_KB / 16; kk++) {
+        uint32_t bv[NTO][2];
+#pragma unroll
+        for (int nt = 0; nt < NTO; nt += 2) {
+          const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int d0 = warp * DW + nt * 8 + (lane >> 4) * 8;
+          ldsm_x4_trans(bv[nt][0], bv[nt][1], bv[nt + 1][0], bv[nt + 1][1], &sm.vs[key][d0]);
         }
 #pragma unroll
         for (int mt = 0; mt < MT; mt++) {
-          const uint32_t* q0r = reinterpret_cast<const uint32_t*>(&sm.qs[mt * 16 + g][kk * 16 + 2 * t]);
-          const uint32_t* q8r = reinterpret_cast<const uint32_t*>(&sm.qs[mt * 16 + g + 8][kk * 16 + 2 * t]);
-          const uint32_t a0 = q0r[0], a1 = q8r[0], a2 = q0r[4], a3 = q8r[4];
+          const int r0w = mt * 16 + g;
+          const uint32_t h0 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w][kk * 16 + 2 * t]);
+          const uint32_t h1 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w + 8][kk * 16 + 2 * t]);
+          const uint32_t h2 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w][kk * 16 + 2 * t + 8]);
+          const uint32_t h3 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w + 8][kk * 16 + 2 * t + 8]);
+          const uint32_t l0 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w][kk * 16 + 2 * t]);
+          const uint32_t l1 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w + 8][kk * 16 + 2 * t]);
+          const uint32_t l2 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w][kk * 16 + 2 * t + 8]);
+          const uint32_t l3 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w + 8][kk * 16 + 2 * t + 8]);
 #pragma unroll
-          for (int nt = 0; nt < 2; nt++) mma_bf16(sacc[mt][nt], a0, a1, a2, a3, bk[nt][0], bk[nt][1]);
+          for (int nt = 0; nt < NTO; nt++) {
+            mma_bf16(o_acc[mt][nt], h0, h1, h2, h3, bv[nt][0], bv[nt][1]);
+            mma_bf16(o_acc[mt][nt], l0, l1, l2, l3, bv[nt][0], bv[nt][1]);
+          }
         }
       }
-      // scale and mask into sm.s
+    }
+
+    // publish this split's partial (empty splits publish nothing: the merge stops at the last non-empty one)
+    {
+      float* mine = a.part + (group * a.nsplit + split) * (size_t)NQ * (D + AT_PAD);
 #pragma unroll
       for (int mt = 0; mt < MT; mt++)
 #pragma unroll
-        for (int nt = 0; nt < 2; nt++)
+        for (int nt = 0; nt < NTO; nt++)
 #pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const int qi = mt * 16 + g + (e >> 1) * 8;
-            const int j = n0 + nt * 8 + 2 * t + (e & 1);
+          for (int h = 0; h < 2; h++) {
+            const int qi = mt * 16 + g + h * 8;
             if (qi < nq) {
-              const int slot = kb0 + j;
-              const int lim = sm.row_slot[qi];
-              bool vis = slot < k_end && slot <= lim;
-              if (a.window > 0) vis = vis && slot > lim - a.window;
-              if (a.tree_mask && slot >= tbase) {
-                const int node = slot - tbase;
-                vis = vis && node < 64 && ((sm.tmask[qi] >> node) & 1ull);
-              }
-              sm.s[qi][j] = vis ? sacc[mt][nt][e] * a.scale : -INFINITY;
+              const int d = warp * DW + nt * 8 + 2 * t;
+              __stcg(reinterpret_cast<float2*>(mine + (size_t)qi * (D + AT_PAD) + d),
+                     make_float2(o_acc[mt][nt][2 * h], o_acc[mt][nt][2 * h + 1]));
             }
           }
-    }
-    __syncthreads();
-    // online softmax per query vector: warp w takes w, w+4, ...; p goes out as bf16 high + low parts
-    for (int qi = warp; qi < nq; qi += AT_THREADS / 32) {
-      const float s0 = sm.s[qi][lane], s1 = sm.s[qi][lane + 32];
-      float bm = fmaxf(s0, s1);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
-      const float mo = sm.m[qi];
-      const float mn = fmaxf(mo, bm);
-      const float p0 = mn == -INFINITY ? 0.f : expf(s0 - mn);
-      const float p1 = mn == -INFINITY ? 0.f : expf(s1 - mn);
-      const float ps = warp_sum(p0 + p1);
-      const uint16_t h0 = to_bf(p0), h1 = to_bf(p1);
-      sm.ph[qi][lane] = h0;
-      sm.ph[qi][lane + 32] = h1;
-      sm.pl[qi][lane] = to_bf(p0 - bf(h0));
-      sm.pl[qi][lane + 32] = to_bf(p1 - bf(h1));
-      if (lane == 0) {
-        const float al = mo == -INFINITY ? 0.f : expf(mo - mn);
-        sm.alpha[qi] = al;
-        sm.l[qi] = sm.l[qi] * al + ps;
-        sm.m[qi] = mn;
+      for (int i = tid; i < nq; i += AT_THREADS) {
+        __stcg(mine + (size_t)i * (D + AT_PAD) + D, sm.m[i]);
+        __stcg(mine + (size_t)i * (D + AT_PAD) + D + 1, sm.l[i]);
       }
-    }
-    __syncthreads();
-    // O = alpha O + P V
-#pragma unroll
-    for (int mt = 0; mt < MT; mt++) {
-      const float al0 = sm.alpha[mt * 16 + g], al8 = sm.alpha[mt * 16 + g + 8];
-#pragma unroll
-      for (int nt = 0; nt < NTO; nt++) {
-        o_acc[mt][nt][0] *= al0;
-        o_acc[mt][nt][1] *= al0;
-        o_acc[mt][nt][2] *= al8;
-        o_acc[mt][nt][3] *= al8;
-      }
-    }
-#pragma unroll
-    for (int kk = 0; kk < AT_KB / 16; kk++) {
-      uint32_t bv[NTO][2];
-#pragma unroll
-      for (int nt = 0; nt < NTO; nt += 2) {
-        const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int d0 = warp * DW + nt * 8 + (lane >> 4) * 8;
-        ldsm_x4_trans(bv[nt][0], bv[nt][1], bv[nt + 1][0], bv[nt + 1][1], &sm.vs[key][d0]);
-      }
-#pragma unroll
-      for (int mt = 0; mt < MT; mt++) {
-        const int r0w = mt * 16 + g;
-        const uint32_t h0 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w][kk * 16 + 2 * t]);
-        const uint32_t h1 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w + 8][kk * 16 + 2 * t]);
-        const uint32_t h2 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w][kk * 16 + 2 * t + 8]);
-        const uint32_t h3 = *reinterpret_cast<const uint32_t*>(&sm.ph[r0w + 8][kk * 16 + 2 * t + 8]);
-        const uint32_t l0 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w][kk * 16 + 2 * t]);
-        const uint32_t l1 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w + 8][kk * 16 + 2 * t]);
-        const uint32_t l2 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w][kk * 16 + 2 * t + 8]);
-        const uint32_t l3 = *reinterpret_cast<const uint32_t*>(&sm.pl[r0w + 8][kk * 16 + 2 * t + 8]);
-#pragma unroll
-        for (int nt = 0; nt < NTO; nt++) {
-          mma_bf16(o_acc[mt][nt], h0, h1, h2, h3, bv[nt][0], bv[nt][1]);
-          mma_bf16(o_acc[mt][nt], l0, l1, l2, l3, bv[nt][0], bv[nt][1]);
-        }
-      }
-    }
-  }
-
-  // publish this split's partial (empty splits publish nothing: the merge stops at the last non-empty one)
-  const size_t group = ((size_t)b * a.Hkv + kvh) * a.qblocks + qb;
-  float* mine = a.part + (group * a.nsplit + split) * (size_t)NQ * (D + AT_PAD);
-  if (active) {
-#pragma unroll
-    for (int mt = 0; mt < MT; mt++)
-#pragma unroll
-      for (int nt = 0; nt < NTO; nt++)
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-          const int qi = mt * 16 + g + h * 8;
-          if (qi < nq) {
-            const int d = warp * DW + nt * 8 + 2 * t;
-            __stcg(reinterpret_cast<float2*>(mine + (size_t)qi * (D + AT_PAD) + d),
-                   make_float2(o_acc[mt][nt][2 * h], o_acc[mt][nt][2 * h + 1]));
-          }
-        }
-    for (int i = tid; i < nq; i += AT_THREADS) {
-      __stcg(mine + (size_t)i * (D + AT_PAD) + D, sm.m[i]);
-      __stcg(mine + (size_t)i * (D + AT_PAD) + D + 1, sm.l[i]);
     }
   }
   __threadfence();
   __syncthreads();
-  if (tid == 0) sm.last = atomicAdd(a.counters + group, 1u) == (unsigned)(a.nsplit - 1);
+  if (tid == 0) sm.last = atomicAdd(a.counters + group, 1u) == (unsigned)(stride_x - 1);
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
@@ -585,20 +611,36 @@ attn_kernel(AttnArgs a) {
   if (tid == 0) a.counters[group] = 0u;
 }
 
+// CTAs per (sequence, kv head, query block): enough for `g_attn_waves` waves of resident CTAs over the whole
+// GPU, at most one per split. Only the scheduling changes with it: every split is computed and merged the same
+// way whichever CTA walks it.
+static int g_attn_waves = 2;
+
 template <int D, int NQ, bool FUSED>
 static int launch_attn(const AttnArgs& args, int B, cudaStream_t st) {
   const size_t smem = sizeof(AttnSmem<D, NQ, FUSED>);
   static bool configured = false;  // per instantiation
+  static int resident = 1, sms = 148;
   if (!configured) {
     cudaError_t e =
         cudaFuncSetAttribute(attn_kernel<D, NQ, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int dev = 0;
+    if (e == cudaSuccess) e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, attn_kernel<D, NQ, FUSED>, AT_THREADS, smem);
     if (e != cudaSuccess) {
-      set_error("attention: cannot reserve %zu bytes of shared memory: %s", smem, cudaGetErrorString(e));
+      set_error("attention: cannot configure the kernel for %zu bytes of shared memory: %s", smem,
+                cudaGetErrorString(e));
       return IM_CUDA_ERROR;
     }
+    resident = resident < 1 ? 1 : resident;
     configured = true;
   }
-  dim3 grid(args.nsplit, args.Hkv, B * args.qblocks);
+  const long long groups = (long long)B * args.Hkv * args.qblocks;
+  const long long want = ((long long)sms * resident * g_attn_waves + groups - 1) / groups;
+  const int per_group = (int)(want < 1 ? 1 : (want > args.nsplit ? args.nsplit : want));
+  dim3 grid(per_group, args.Hkv, B * args.qblocks);
   return launch("attn_kernel", attn_kernel<D, NQ, FUSED>, grid, dim3(AT_THREADS), smem, st, args);
 }
 
@@ -635,6 +677,12 @@ extern "C" size_t im_attention_workspace_bytes(int64_t B, int64_t max_rows_per_s
   const int64_t groups = B * Hkv * qblocks;
   if (groups > AT_MAX_GROUPS) return 0;
   return AT_COUNTER_BYTES + (size_t)groups * nsplit * nq * (D + AT_PAD) * sizeof(float);
+}
+
+extern "C" int im_attention_tune(int waves) {
+  IM_REQUIRE(waves >= 1 && waves <= 64, IM_INVALID, "im_attention_tune: waves %d", waves);
+  g_attn_waves = waves;
+  return IM_OK;
 }
 
 namespace im {

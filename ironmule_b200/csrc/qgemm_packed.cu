@@ -16,16 +16,13 @@
 // GEMM (or the embedding) wrote, summed in tile order. A residual epilogue can write those sums for the next GEMM.
 // Partition (tiles x K splits) depends on (N, K) only; rows are independent: a row's bits do not depend on M.
 #include "common.cuh"
+#include "qgemm_packed.cuh"
 #include "../../include/imspec.h"
 
 namespace im {
 
 constexpr int Q4_WARPS = 4;
 constexpr int Q4_THREADS = Q4_WARPS * 32;
-constexpr int Q4_UNIT = 1152;
-constexpr int Q4_RMAX = 16;               // groups per CTA range (shared-memory budget: 16 KB per 8 rows)
-constexpr size_t Q4_COUNTER_BYTES = 524288;  // split-K arrival counters: one per (32-row chunk, tile)
-constexpr int Q4_MAX_ROWS = 320;             // rows per call: up to 10 chunks of 32
 constexpr int Q4_DEPTH = 3;               // units in flight per warp
 static int g_q4_split_override = 0;       // sweep hook (0 = automatic)
 static int g_q4_target_ctas = 148 * 4;    // split policy: aim for this many CTAs
@@ -98,20 +95,6 @@ __global__ void q4_pack_kernel(const uint32_t* __restrict__ w, const uint16_t* _
 }
 
 // ---- the GEMM -------------------------------------------------------------------------------------------
-struct Q4Args {
-  const unsigned char* wp;  // packed units
-  const uint16_t* x;        // [M, K] activations (raw residual when norm_w != NULL)
-  uint16_t* y;
-  const uint16_t* res;
-  const float* norm_sq;     // [norm_parts][sq_ld] sums of squares of x rows (RMSNorm prologue) or NULL
-  const uint16_t* norm_w;   // [K]
-  float* out_sq;            // [tiles][sq_ld] sums of squares of the written rows (residual epilogue) or NULL
-  float* partial;
-  unsigned* counters;
-  float eps;
-  int M, N, K, tiles, splits, norm_parts, gemma_norm, sq_ld;
-};
-
 // Dynamic shared memory: xf [rmax][NT][32 lanes][2 x 16 B] activation fragments, sx [rmax][NT*8] group sums,
 // inv [32] RMSNorm factors.
 __host__ __device__ constexpr size_t q4_smem_bytes(int nt) {
@@ -408,12 +391,7 @@ qgemm_packed_kernel(Q4Args a) {
   }
 }
 
-struct Q4Plan {
-  int tiles, ctas_x, splits, nt, chunks;
-  size_t workspace;
-};
-
-static Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
+Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
   Q4Plan p;
   p.tiles = (int)((N + 31) / 32);
   p.ctas_x = (p.tiles + Q4_WARPS - 1) / Q4_WARPS;
@@ -429,7 +407,10 @@ static Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
   if (g_q4_split_override > 0) s = g_q4_split_override < need ? need : (g_q4_split_override > G ? G : g_q4_split_override);
   p.splits = s;
   p.chunks = (int)((M + 31) / 32);
-  p.workspace = s > 1 ? Q4_COUNTER_BYTES + (size_t)p.chunks * p.tiles * s * 2 * 4 * 4 * 32 * sizeof(float) : 0;
+  if (M > 32)  // the tensor-core path always needs its activation tiles
+    p.workspace = Q4_COUNTER_BYTES + qtc_workspace_bytes(p, M, K);
+  else
+    p.workspace = s > 1 ? Q4_COUNTER_BYTES + (size_t)p.chunks * p.tiles * s * 2 * 4 * 4 * 32 * sizeof(float) : 0;
   return p;
 }
 
@@ -489,7 +470,20 @@ extern "C" int im_qgemm_pack_w4g64(const uint32_t* w, const uint16_t* scales, co
 extern "C" size_t im_qgemm_packed_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   if (M < 1 || M > Q4_MAX_ROWS || N < 1 || K < 64 || K % 64) return 0;
   const Q4Plan p = q4_plan(M, N, K);
-  return (size_t)p.chunks * p.tiles <= Q4_COUNTER_BYTES / 4 ? p.workspace : 0;
+  return (size_t)((p.chunks + 1) / 2 * 2) * p.tiles < Q4_COUNTER_BYTES / 4 ? p.workspace : 0;
+}
+
+extern "C" int im_qgemm_packed_status(const void* workspace) {
+  clear_error();
+  IM_REQUIRE(workspace, IM_INVALID, "im_qgemm_packed_status: null workspace");
+  unsigned word = 0;
+  const cudaError_t e = cudaMemcpy(&word, reinterpret_cast<const char*>(workspace) + Q4_COUNTER_BYTES - 4, 4,
+                                   cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    set_error("im_qgemm_packed_status: %s", cudaGetErrorString(e));
+    return IM_CUDA_ERROR;
+  }
+  return (int)word;
 }
 
 extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* y, const uint16_t* residual,
@@ -513,9 +507,11 @@ extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* 
   const int64_t ld = sq_ld > 0 ? sq_ld : (M + 31) / 32 * 32;
   IM_REQUIRE(ld >= M, IM_INVALID, "im_qgemm_packed: sq_ld %lld below M", (long long)ld);
   const Q4Plan p = q4_plan(M, N, K);
-  IM_REQUIRE((size_t)p.chunks * p.tiles <= Q4_COUNTER_BYTES / 4, IM_UNSUPPORTED,
+  // counters: one per (32-row chunk, tile) below 33 rows, per (64-row chunk, tile, column half) above; the
+  // last word of the counter region is the tensor-core kernel's error word
+  IM_REQUIRE((size_t)((p.chunks + 1) / 2 * 2) * p.tiles < Q4_COUNTER_BYTES / 4, IM_UNSUPPORTED,
              "im_qgemm_packed: N too large for split-K at %lld rows", (long long)M);
-  if (p.splits > 1)
+  if (p.splits > 1 || M > 32)
     IM_REQUIRE(workspace && aligned(workspace, 256) && workspace_bytes >= p.workspace, IM_INVALID,
                "im_qgemm_packed: workspace of %zu bytes (256-aligned) needed, %zu given", p.workspace,
                workspace_bytes);
@@ -539,6 +535,7 @@ extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* 
   a.gemma_norm = gemma_norm;
   a.sq_ld = (int)ld;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (M > 32) return qtc_launch(p, a, epilogue, workspace, st);
   switch (epilogue) {
     case IM_EPI_STORE: return q4_dispatch<IM_EPI_STORE>(p, a, st);
     case IM_EPI_RESIDUAL: return q4_dispatch<IM_EPI_RESIDUAL>(p, a, st);

@@ -1,0 +1,45 @@
+// Shared by the two kernels behind im_qgemm_packed: the warp-MMA kernel for up to 32 activation rows
+// (qgemm_packed.cu) and the tensor-core kernel for more (qgemm_tc.cu). Both use the same packed units, the same
+// K-split plan and the same arithmetic, so a row's bits do not depend on which kernel computed it.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+
+#include <cuda_runtime.h>
+
+namespace im {
+
+constexpr int Q4_UNIT = 1152;                // packed bytes per (32-row tile, 64-wide group)
+constexpr int Q4_RMAX = 16;                  // groups per CTA K range (the split plan never exceeds it)
+constexpr size_t Q4_COUNTER_BYTES = 524288;  // split-K arrival counters; the last word is the error word
+constexpr int Q4_MAX_ROWS = 320;             // activation rows per call
+
+struct Q4Args {
+  const unsigned char* wp;  // packed units
+  const uint16_t* x;        // [M, K] activations (raw residual when norm_w != NULL)
+  uint16_t* y;
+  const uint16_t* res;
+  const float* norm_sq;     // [norm_parts][sq_ld] sums of squares of x rows (RMSNorm prologue) or NULL
+  const uint16_t* norm_w;   // [K]
+  float* out_sq;            // [tiles][sq_ld] sums of squares of the written rows (residual epilogue) or NULL
+  float* partial;
+  unsigned* counters;
+  float eps;
+  int M, N, K, tiles, splits, norm_parts, gemma_norm, sq_ld;
+};
+
+struct Q4Plan {
+  int tiles, ctas_x, splits, nt, chunks;
+  size_t workspace;
+};
+
+// The K-split plan: depends on (N, K) only, never on M.
+Q4Plan q4_plan(int64_t M, int64_t N, int64_t K);
+
+// Tensor-core path (M > 32): workspace bytes past the counters for M rows, and the launch (prologue kernel +
+// GEMM kernel) on `workspace` laid out as [counters][partials][activation tiles].
+size_t qtc_workspace_bytes(const Q4Plan& p, int64_t M, int64_t K);
+int qtc_launch(const Q4Plan& p, const Q4Args& a, int epilogue, void* workspace, cudaStream_t st);
+
+}  // namespace im

@@ -10,8 +10,9 @@
 //
 // Distributions: p = softmax(logits / T) restricted to the top-p set {v : l_v >= l*} where l* is the largest
 // logit whose set holds at least top_p of the mass (ties at the boundary are all kept), renormalised. The
-// boundary is found exactly over the 65536 bf16 keys with two 256-bin mass histograms; the normaliser of the
-// kept set is a fixed-order block reduction.
+// boundary is found over the 65536 bf16 keys with two 256-bin mass histograms (integer sums of the weights in
+// units of 2^-26, independent of the order of the additions); the normaliser of the kept set is a fixed-order
+// block reduction.
 //
 // Philox stream: key = (seed low, seed high), counter = (offset low, offset high, stream, draw), uniform =
 // (word0 >> 8) * 2^-24. Acceptance uses stream = sequence, draw 2i (test of draft i), 2i+1 (resample after
@@ -89,12 +90,27 @@ __device__ __forceinline__ float block_max_1024(float v, float* sh) {
   return t;
 }
 
+// Mass histograms of the top-p boundary search hold integer sums of the per-token weights exp((l - m) / T)
+// (at most 1) rounded to multiples of 2^-26, so a bin's mass does not depend on the order of the additions and
+// the boundary is the same on every run. A warp first adds the weights of its lanes that share a bin
+// (match + reduce), then one lane per distinct bin adds that to the shared histogram.
+constexpr float DIST_Q = 67108864.0f;  // 2^26
+
+__device__ __forceinline__ void hist_add(unsigned long long* hist, uint32_t bin, uint32_t q, bool valid) {
+  const uint32_t key = valid ? bin : 0xffffffffu;  // lanes without a weight form a group of their own
+  const unsigned grp = __match_any_sync(0xffffffffu, key);
+  const uint32_t sum = __reduce_add_sync(grp, q);  // <= 32 * 2^26
+  if (valid && (int)(threadIdx.x & 31) == __ffs(grp) - 1) atomicAdd(&hist[bin], (unsigned long long)sum);
+}
+
 // One CTA per row: max, top-p boundary key, kept-set normaliser.
 __global__ void __launch_bounds__(SM_THREADS)
 row_dist_kernel(const uint16_t* __restrict__ logits, int V, long long ld, float temperature, float top_p,
                 RowDist* __restrict__ out) {
   __shared__ float sh[32];
-  __shared__ float hist[256];
+  __shared__ unsigned long long hist[256];
+  __shared__ unsigned long long above_sh;
+  __shared__ double goal_sh;
   __shared__ uint32_t sel;
   pdl_wait();
   pdl_trigger();
@@ -108,53 +124,57 @@ row_dist_kernel(const uint16_t* __restrict__ logits, int V, long long ld, float 
   const float m = block_max_1024(mx, sh);
   uint32_t thr = 0;
   if (top_p < 1.0f) {
-    // level 1: mass per top key byte
-    for (int i = threadIdx.x; i < 256; i += SM_THREADS) hist[i] = 0.f;
+    // level 1: mass per top key byte (every lane takes part in every step: the warp-wide match needs it)
+    for (int i = threadIdx.x; i < 256; i += SM_THREADS) hist[i] = 0ull;
     __syncthreads();
-    float tot = 0.f;
-    for (int v = threadIdx.x; v < V; v += SM_THREADS) {
-      const uint16_t h = lp[v];
+    for (int base = 0; base < V; base += SM_THREADS) {
+      const int v = base + threadIdx.x;
+      const uint16_t h = v < V ? lp[v] : (uint16_t)0x7fffu;  // past the end: a NaN, no weight
       const uint32_t key = bf_key(h);
-      if (!key) continue;
-      const float w = expf((bf(h) - m) * inv_t);
-      tot += w;
-      atomicAdd(&hist[key >> 8], w);
+      const uint32_t q = key ? __float2uint_rn(expf((bf(h) - m) * inv_t) * DIST_Q) : 0u;
+      hist_add(hist, key >> 8, q, key != 0u);
     }
-    const float total = block_sum_1024(tot, sh);
+    __syncthreads();
     if (threadIdx.x == 0) {
-      const float goal = top_p * total;
-      float cum = 0.f;
+      unsigned long long total = 0ull;
+      for (int i = 0; i < 256; i++) total += hist[i];
+      const double goal = (double)top_p * (double)total;
+      unsigned long long cum = 0ull;
       uint32_t b = 0;
       for (int i = 255; i >= 0; i--) {
         cum += hist[i];
-        if (cum >= goal) {
+        if ((double)cum >= goal) {
           b = (uint32_t)i;
           break;
         }
       }
-      sel = (b << 16) | 0u;
-      hist[0] = cum - hist[b];  // mass strictly above the chosen bin (read after the barrier below)
+      sel = b;
+      above_sh = cum - hist[b];  // mass strictly above the chosen bin
+      goal_sh = goal;
     }
     __syncthreads();
-    const uint32_t b1 = sel >> 16;
-    const float above = hist[0];
+    const uint32_t b1 = sel;
+    const unsigned long long above = above_sh;
+    const double goal = goal_sh;
     __syncthreads();
     // level 2: mass per low key byte inside bin b1
-    for (int i = threadIdx.x; i < 256; i += SM_THREADS) hist[i] = 0.f;
+    for (int i = threadIdx.x; i < 256; i += SM_THREADS) hist[i] = 0ull;
     __syncthreads();
-    for (int v = threadIdx.x; v < V; v += SM_THREADS) {
-      const uint16_t h = lp[v];
+    for (int base = 0; base < V; base += SM_THREADS) {
+      const int v = base + threadIdx.x;
+      const uint16_t h = v < V ? lp[v] : (uint16_t)0x7fffu;
       const uint32_t key = bf_key(h);
-      if (key && (key >> 8) == b1) atomicAdd(&hist[key & 0xffu], expf((bf(h) - m) * inv_t));
+      const bool in = key != 0u && (key >> 8) == b1;
+      const uint32_t q = in ? __float2uint_rn(expf((bf(h) - m) * inv_t) * DIST_Q) : 0u;
+      hist_add(hist, key & 0xffu, q, in);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-      const float goal = top_p * total;
-      float cum = above;
+      unsigned long long cum = above;
       uint32_t lo = 0;
       for (int i = 255; i >= 0; i--) {
         cum += hist[i];
-        if (cum >= goal) {
+        if ((double)cum >= goal) {
           lo = (uint32_t)i;
           break;
         }

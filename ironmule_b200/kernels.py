@@ -262,6 +262,11 @@ def attention_workspace_bytes(b: int, rows: int, hq: int, hkv: int, d: int, max_
     return int(_lib.load().im_attention_workspace_bytes(b, rows, hq, hkv, d, max_kv_len, kpc))
 
 
+def attention_tune(waves: int) -> None:
+    """Waves of resident CTAs the attention launch aims for (scheduling only; results do not change)."""
+    _lib.call("im_attention_tune", int(waves))
+
+
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, page_table: torch.Tensor,
               seq_rows: torch.Tensor, row_slot: torch.Tensor, *, max_rows_per_seq: int, max_kv_len: int,
               scale: float, keys_per_split: int = 64, window: int = 0, tree_mask: torch.Tensor | None = None,
@@ -439,6 +444,17 @@ def set_launch_overlap(on: bool) -> bool:
 
 def qgemm_packed_workspace_bytes(m: int, n: int, k: int) -> int:
     return int(_lib.load().im_qgemm_packed_workspace_bytes(m, n, k))
+
+
+def qgemm_packed_status(ws: torch.Tensor) -> int:
+    """The error word of a workspace last used by a call of more than 32 rows (0: every wait completed)."""
+    ptr, _ = _ws(ws, 1 << 16)
+    return int(_lib.load().im_qgemm_packed_status(ptr))
+
+
+def qgemm_packed_tune(split_override: int = 0, target_ctas: int = 592, max_split: int = 64) -> None:
+    """The K-split policy (process-wide; changes workspace sizes)."""
+    _lib.call("im_qgemm_packed_tune", split_override, target_ctas, max_split)
 
 
 def qgemm_packed(x: torch.Tensor, p: Packed, *, epilogue: str = "store", residual: torch.Tensor | None = None,

@@ -196,6 +196,47 @@ def test_fused_attention_equals_rope_then_attention(cuda, d, hq, hkv, rows, wind
     assert torch.equal(vc_a.view(torch.int16), vc_b.view(torch.int16))
 
 
+@pytest.mark.parametrize("d,hq,hkv,rows,tree", [(128, 32, 8, 5, False), (256, 16, 8, 7, True),
+                                                 (128, 16, 8, 1, False)])
+def test_attention_ctas_per_group_change_no_bits(cuda, d, hq, hkv, rows, tree):
+    """32 sequences: with few waves a CTA walks several splits; with many, each split has its own CTA. Outputs
+    and the K/V written are the same bits either way, fused and unfused."""
+    rng = np.random.default_rng(d + rows)
+    b, max_pages = 32, 40
+    lens = rng.integers(rows + 1, max_pages * 16 - 8, b).tolist()
+    table = rng.permutation(b * max_pages).reshape(b, max_pages).astype(np.int32)
+    shape = (b * max_pages, hkv, 16, d)
+    kc0, vc0 = rand_bits(rng, shape), rand_bits(rng, shape)
+    m = b * rows
+    qkv = rand_bits(rng, (m, (hq + 2 * hkv) * d))
+    qn, kn = rand_bits(rng, (d,), 0.5), rand_bits(rng, (d,), 0.5)
+    inv_freq = torch.from_numpy((1e6 ** (-2.0 * np.arange(d // 2) / d)).astype(np.float32)).to(cuda)
+    slots = np.concatenate([np.arange(n - rows, n) for n in lens]).astype(np.int32)
+    masks = tb = None
+    if tree:
+        masks = torch.tensor([(1 << (i + 1)) - 1 for i in range(rows)] * b, dtype=torch.int64, device=cuda)
+        tb = torch.tensor([n - rows for n in lens], dtype=torch.int32, device=cuda)
+    seq_rows = torch.arange(0, m + 1, rows, dtype=torch.int32, device=cuda)
+    tbl, sl = torch.from_numpy(table).to(cuda), torch.from_numpy(slots).to(cuda)
+    qkv_t, qn_t, kn_t = bf16_bits_to_torch(qkv, cuda), bf16_bits_to_torch(qn, cuda), bf16_bits_to_torch(kn, cuda)
+    kw = dict(max_rows_per_seq=rows, max_kv_len=max_pages * 16, scale=d ** -0.5, tree_mask=masks, tree_base=tb)
+    q = bf16_bits_to_torch(rand_bits(rng, (m, hq, d)), cuda)
+    outs = []
+    try:
+        for waves in (1, 64):
+            kernels.attention_tune(waves)
+            kc, vc = bf16_bits_to_torch(kc0, cuda), bf16_bits_to_torch(vc0, cuda)
+            got = kernels.attention_qkv(qkv_t, qn_t, kn_t, inv_freq, sl, kc, vc, tbl, seq_rows, sl, hq=hq, hkv=hkv,
+                                        d=d, eps=1e-6, **kw)
+            plain = kernels.attention(q, kc, vc, tbl, seq_rows, sl, **kw)
+            torch.cuda.synchronize()
+            outs.append([t.view(torch.int16).clone() for t in (got, plain, kc, vc)])
+    finally:
+        kernels.attention_tune(2)
+    for x, y in zip(*outs):
+        assert torch.equal(x, y)
+
+
 def tiny(name="tiny-target", seed=0, **kw):
     return engine.QuantModel(engine.PRESETS[name], "cuda", seed=seed, max_ctx=256, **kw)
 

@@ -321,3 +321,61 @@ def test_packed_gated_epilogues(cuda, epi):
     want = (om.silu_mul if epi == "swiglu" else om.gelu_mul)(g[:, :, 0, :].reshape(5, -1), g[:, :, 1, :].reshape(5, -1))
     diff = np.abs(bf16.to_f32(got) - bf16.to_f32(want))
     assert np.all(diff <= 2 * (np.abs(bf16.to_f32(want)) * 2.0 ** -7 + 1e-30))
+
+
+@pytest.mark.parametrize("n,k,m", [(2048, 1536, 64), (2048, 1536, 65), (40, 512, 100), (6144, 2560, 160),
+                                   (2560, 9728, 320), (19456, 2560, 128), (1000, 4096, 33)])
+def test_tensor_core_rows_equal_32_row_calls(cuda, n, k, m):
+    """More than 32 rows run on the tcgen05 kernel: every row gets the bits a call of at most 32 rows gives it
+    (dead tiles, partial tiles and a ragged last chunk included), and every bounded wait completes."""
+    wq, s, b, x, p, x_t = packed_case(cuda, n, k, m, 7 * m + n)
+    ws = kernels.workspace(kernels.qgemm_packed_workspace_bytes(m, n, k), cuda)
+    got = torch_to_bf16_bits(kernels.qgemm_packed(x_t, p, ws=ws))
+    assert kernels.qgemm_packed_status(ws) == 0
+    for r0 in range(0, m, 32):
+        alone = torch_to_bf16_bits(kernels.qgemm_packed(x_t[r0:r0 + 32].contiguous(), p))
+        assert np.array_equal(alone, got[r0:r0 + 32]), r0
+    if n * k * m <= 2048 * 1536 * 100:
+        mx, mean = rel_errors(got, qmv.qmv(wq, s, b, x, vpt=8))
+        assert mx <= MAX_REL and mean <= MEAN_REL, (mx, mean)
+
+
+@pytest.mark.parametrize("splits", [1, 3, 16])
+def test_tensor_core_forced_splits(cuda, splits):
+    """Any K split: the tcgen05 kernel's split-K partials and merge equal the warp-MMA kernel's."""
+    wq, s, b, x, p, x_t = packed_case(cuda, 1536, 3072, 96, 50 + splits)
+    kernels.qgemm_packed_tune(split_override=splits)
+    try:
+        got = torch_to_bf16_bits(kernels.qgemm_packed(x_t, p))
+        for r0 in range(0, 96, 32):
+            alone = torch_to_bf16_bits(kernels.qgemm_packed(x_t[r0:r0 + 32].contiguous(), p))
+            assert np.array_equal(alone, got[r0:r0 + 32]), r0
+    finally:
+        kernels.qgemm_packed_tune()
+
+
+@pytest.mark.parametrize("epi", ["residual", "swiglu", "geglu"])
+def test_tensor_core_epilogues_equal_32_row_calls(cuda, epi):
+    """Residual (with sums of squares), SwiGLU and GeGLU epilogues over 150 rows, with the fused RMSNorm
+    prologue: the same bits as 32-row calls."""
+    rng = np.random.default_rng(17)
+    m, n, k, ld = 150, 2048, 1024, 160
+    wq, s, b, x, p, x_t = packed_case(cuda, n, k, m, 61)
+    tiles_in = 8
+    sq_in = torch.from_numpy(rng.uniform(50, 200, (tiles_in, ld)).astype(np.float32)).to(cuda)
+    nw = torch.from_numpy(bf16.from_f32(rng.normal(1, 0.1, k).astype(np.float32)).view(np.int16)).view(torch.bfloat16)
+    nw = nw.to(cuda)
+    kw = dict(norm_sq=sq_in, norm_parts=tiles_in, norm_weight=nw, sq_ld=ld)
+    res = torch.randn(m, n, device=cuda).to(torch.bfloat16) if epi == "residual" else None
+    sq = torch.zeros((p.tiles, ld), dtype=torch.float32, device=cuda) if epi == "residual" else None
+    big = kernels.qgemm_packed(x_t, p, epilogue=epi, residual=res, out_sq=sq, **kw)
+    for r0 in range(0, m, 32):
+        nr = min(32, m - r0)
+        sq_c = torch.zeros((p.tiles, nr), dtype=torch.float32, device=cuda) if sq is not None else None
+        part = kernels.qgemm_packed(x_t[r0:r0 + nr].contiguous(), p, epilogue=epi,
+                                    residual=None if res is None else res[r0:r0 + nr].contiguous(), out_sq=sq_c,
+                                    norm_sq=sq_in[:, r0:r0 + nr].contiguous(), norm_parts=tiles_in, norm_weight=nw,
+                                    sq_ld=nr)
+        assert torch.equal(part.view(torch.int16), big[r0:r0 + nr].view(torch.int16)), r0
+        if sq is not None:
+            assert torch.equal(sq_c.view(torch.int32), sq[:, r0:r0 + nr].view(torch.int32)), r0
