@@ -57,6 +57,8 @@ def parse():
                     default="spec_decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--qgemm-path", type=int, choices=[0, 1, 2], default=0,
+                    help="packed qGEMM kernel: 0 automatic, 1 warp MMA only, 2 tcgen05 tensor cores only (same bits)")
     return ap.parse_args()
 
 
@@ -546,6 +548,9 @@ def main() -> int:
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), rank)
         return 0
     world, rank, local = dist_setup(args)
+    if args.qgemm_path:
+        from ironmule_b200 import kernels
+        kernels.qgemm_packed_path(args.qgemm_path)
     try:
         if args.workload == "verify_step":
             run_verify_step(args, world, rank, local)

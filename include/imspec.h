@@ -124,8 +124,8 @@ int im_qgemm_tma_status(const void* workspace, uint32_t* status);
  * im_qgemm_packed_bytes(N, K) bytes): rows padded to 32-row tiles, one contiguous 1152-byte unit per
  * (tile, 64-group) holding that tile's codes in lane order and its 32 scales/biases.
  * im_qgemm_packed computes the same product and epilogues as im_qgemm_w4g64_ex from it for M <= 320 rows (every
- * row exactly as a call of at most 32 rows computes it: up to 32 rows on the warp MMA, more on the tcgen05
- * tensor cores with the same k-steps and fp32 order, activations staged as 64-row tiles in the workspace),
+ * row exactly as a call of at most 32 rows computes it, on the warp MMA in 32-row chunks or on the tcgen05
+ * tensor cores with the same k-steps and fp32 order, activations staged as tiles in the workspace),
  * and can fuse the RMSNorm that precedes a
  * projection: with norm_weight != NULL, x is the raw residual stream and each row is normalised on the way in
  * (x * 1/sqrt(sum(x^2)/K + eps) * w', w' = w or 1 + w when gemma_norm), its sum of squares taken from
@@ -143,6 +143,10 @@ size_t im_qgemm_packed_workspace_bytes(int64_t M, int64_t N, int64_t K);
 /* Tuning hook of the K-split policy: a forced split (0 = automatic), the CTA count the automatic policy aims
  * for, and its largest split. Process-wide; changes workspace sizes, so set it before sizing workspaces. */
 int im_qgemm_packed_tune(int split_override, int target_ctas, int max_split);
+/* Kernel choice: 0 (default) = automatic (tcgen05 tensor cores from 192 rows when the K split is at most 16, the
+ * warp MMA otherwise), 1 = warp MMA always, 2 = tensor cores always. Process-wide; every choice gives the same
+ * bits; changes workspace sizes, so set it before sizing workspaces. */
+int im_qgemm_packed_path(int path);
 /* The error word of a workspace last used by a call of more than 32 rows (the tensor-core kernel): 0 when
  * every bounded wait of that kernel completed, 1 when one ran out. Synchronous (reads device memory). */
 int im_qgemm_packed_status(const void* workspace);

@@ -27,6 +27,16 @@ constexpr int Q4_DEPTH = 3;               // units in flight per warp
 static int g_q4_split_override = 0;       // sweep hook (0 = automatic)
 static int g_q4_target_ctas = 148 * 4;    // split policy: aim for this many CTAs
 static int g_q4_max_split = 64;
+static int g_q4_path = 0;                 // 0: automatic, 1: warp MMA always, 2: tensor cores always
+
+// The tensor-core kernel wins where an item streams many groups for many rows. Measured on B200 whole rounds:
+// Gemma-3-12B tree verification at 232 rows 71.2 ms (automatic) vs 75.1 ms (warp MMA only); Qwen3-4B at 160 rows
+// 49.3 ms vs 42.0 ms; Gemma-3-27B at 320 rows even. So: from 192 rows with at most 16 K splits.
+static bool q4_tensor_cores(int64_t M, int splits) {
+  if (g_q4_path == 2) return true;
+  if (g_q4_path == 1) return false;
+  return M >= 192 && splits <= 16;
+}
 constexpr uint32_t Q4_128 = 0x43004300u;
 
 __device__ __forceinline__ void q4_mma(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
@@ -407,7 +417,7 @@ Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
   if (g_q4_split_override > 0) s = g_q4_split_override < need ? need : (g_q4_split_override > G ? G : g_q4_split_override);
   p.splits = s;
   p.chunks = (int)((M + 31) / 32);
-  if (M > 32)  // the tensor-core path always needs its activation tiles
+  if (q4_tensor_cores(M, s))  // the tensor-core path always needs the counter region (its error word)
     p.workspace = Q4_COUNTER_BYTES + qtc_workspace_bytes(p, M, K);
   else
     p.workspace = s > 1 ? Q4_COUNTER_BYTES + (size_t)p.chunks * p.tiles * s * 2 * 4 * 4 * 32 * sizeof(float) : 0;
@@ -445,6 +455,12 @@ extern "C" int im_qgemm_packed_tune(int split_override, int target_ctas, int max
   g_q4_split_override = split_override;
   g_q4_target_ctas = target_ctas;
   g_q4_max_split = max_split;
+  return IM_OK;
+}
+
+extern "C" int im_qgemm_packed_path(int path) {
+  IM_REQUIRE(path >= 0 && path <= 2, IM_INVALID, "im_qgemm_packed_path: 0, 1 or 2");
+  g_q4_path = path;
   return IM_OK;
 }
 
@@ -511,7 +527,8 @@ extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* 
   // last word of the counter region is the tensor-core kernel's error word
   IM_REQUIRE((size_t)((p.chunks + 1) / 2 * 2) * p.tiles < Q4_COUNTER_BYTES / 4, IM_UNSUPPORTED,
              "im_qgemm_packed: N too large for split-K at %lld rows", (long long)M);
-  if (p.splits > 1 || M > 32)
+  const bool tc = q4_tensor_cores(M, p.splits);
+  if (p.splits > 1 || tc)
     IM_REQUIRE(workspace && aligned(workspace, 256) && workspace_bytes >= p.workspace, IM_INVALID,
                "im_qgemm_packed: workspace of %zu bytes (256-aligned) needed, %zu given", p.workspace,
                workspace_bytes);
@@ -535,7 +552,7 @@ extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* 
   a.gemma_norm = gemma_norm;
   a.sq_ld = (int)ld;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (M > 32) return qtc_launch(p, a, epilogue, workspace, st);
+  if (tc) return qtc_launch(p, a, epilogue, workspace, st);
   switch (epilogue) {
     case IM_EPI_STORE: return q4_dispatch<IM_EPI_STORE>(p, a, st);
     case IM_EPI_RESIDUAL: return q4_dispatch<IM_EPI_RESIDUAL>(p, a, st);

@@ -452,6 +452,12 @@ def qgemm_packed_status(ws: torch.Tensor) -> int:
     return int(_lib.load().im_qgemm_packed_status(ptr))
 
 
+def qgemm_packed_path(path: int) -> None:
+    """0: automatic (default); 1: warp MMA always; 2: tcgen05 tensor cores always. Every choice gives the same
+    bits."""
+    _lib.call("im_qgemm_packed_path", int(path))
+
+
 def qgemm_packed_tune(split_override: int = 0, target_ctas: int = 592, max_split: int = 64) -> None:
     """The K-split policy (process-wide; changes workspace sizes)."""
     _lib.call("im_qgemm_packed_tune", split_override, target_ctas, max_split)

@@ -326,12 +326,16 @@ def test_packed_gated_epilogues(cuda, epi):
 @pytest.mark.parametrize("n,k,m", [(2048, 1536, 64), (2048, 1536, 65), (40, 512, 100), (6144, 2560, 160),
                                    (2560, 9728, 320), (19456, 2560, 128), (1000, 4096, 33)])
 def test_tensor_core_rows_equal_32_row_calls(cuda, n, k, m):
-    """More than 32 rows run on the tcgen05 kernel: every row gets the bits a call of at most 32 rows gives it
+    """More than 32 rows on the tcgen05 kernel: every row gets the bits a call of at most 32 rows gives it
     (dead tiles, partial tiles and a ragged last chunk included), and every bounded wait completes."""
     wq, s, b, x, p, x_t = packed_case(cuda, n, k, m, 7 * m + n)
-    ws = kernels.workspace(kernels.qgemm_packed_workspace_bytes(m, n, k), cuda)
-    got = torch_to_bf16_bits(kernels.qgemm_packed(x_t, p, ws=ws))
-    assert kernels.qgemm_packed_status(ws) == 0
+    kernels.qgemm_packed_path(2)
+    try:
+        ws = kernels.workspace(kernels.qgemm_packed_workspace_bytes(m, n, k), cuda)
+        got = torch_to_bf16_bits(kernels.qgemm_packed(x_t, p, ws=ws))
+        assert kernels.qgemm_packed_status(ws) == 0
+    finally:
+        kernels.qgemm_packed_path(0)
     for r0 in range(0, m, 32):
         alone = torch_to_bf16_bits(kernels.qgemm_packed(x_t[r0:r0 + 32].contiguous(), p))
         assert np.array_equal(alone, got[r0:r0 + 32]), r0
@@ -345,6 +349,7 @@ def test_tensor_core_forced_splits(cuda, splits):
     """Any K split: the tcgen05 kernel's split-K partials and merge equal the warp-MMA kernel's."""
     wq, s, b, x, p, x_t = packed_case(cuda, 1536, 3072, 96, 50 + splits)
     kernels.qgemm_packed_tune(split_override=splits)
+    kernels.qgemm_packed_path(2)
     try:
         got = torch_to_bf16_bits(kernels.qgemm_packed(x_t, p))
         for r0 in range(0, 96, 32):
@@ -352,6 +357,7 @@ def test_tensor_core_forced_splits(cuda, splits):
             assert np.array_equal(alone, got[r0:r0 + 32]), r0
     finally:
         kernels.qgemm_packed_tune()
+        kernels.qgemm_packed_path(0)
 
 
 @pytest.mark.parametrize("epi", ["residual", "swiglu", "geglu"])
@@ -368,7 +374,11 @@ def test_tensor_core_epilogues_equal_32_row_calls(cuda, epi):
     kw = dict(norm_sq=sq_in, norm_parts=tiles_in, norm_weight=nw, sq_ld=ld)
     res = torch.randn(m, n, device=cuda).to(torch.bfloat16) if epi == "residual" else None
     sq = torch.zeros((p.tiles, ld), dtype=torch.float32, device=cuda) if epi == "residual" else None
-    big = kernels.qgemm_packed(x_t, p, epilogue=epi, residual=res, out_sq=sq, **kw)
+    kernels.qgemm_packed_path(2)
+    try:
+        big = kernels.qgemm_packed(x_t, p, epilogue=epi, residual=res, out_sq=sq, **kw)
+    finally:
+        kernels.qgemm_packed_path(0)
     for r0 in range(0, m, 32):
         nr = min(32, m - r0)
         sq_c = torch.zeros((p.tiles, nr), dtype=torch.float32, device=cuda) if sq is not None else None
@@ -379,3 +389,35 @@ def test_tensor_core_epilogues_equal_32_row_calls(cuda, epi):
         assert torch.equal(part.view(torch.int16), big[r0:r0 + nr].view(torch.int16)), r0
         if sq is not None:
             assert torch.equal(sq_c.view(torch.int32), sq[:, r0:r0 + nr].view(torch.int32)), r0
+
+
+@pytest.mark.parametrize("m", [1, 2, 5, 13, 32])
+def test_tensor_core_path_for_few_rows_gives_the_same_bits(cuda, m):
+    """With the tensor-core kernel chosen for every M, calls of up to 32 rows (store, residual + sums of
+    squares with the fused RMSNorm, SwiGLU) return exactly the warp-MMA kernel's bits."""
+    rng = np.random.default_rng(m)
+    n, k, ld = 2048, 2560, 32
+    wq, s, b, x, p, x_t = packed_case(cuda, n, k, m, 300 + m)
+    sq_in = torch.from_numpy(rng.uniform(50, 200, (4, ld)).astype(np.float32)).to(cuda)
+    nw = torch.from_numpy(bf16.from_f32(rng.normal(1, 0.1, k).astype(np.float32)).view(np.int16)).view(torch.bfloat16)
+    nw = nw.to(cuda)
+    res = torch.randn(m, n, device=cuda).to(torch.bfloat16)
+    outs = []
+    for path in (0, 2):
+        kernels.qgemm_packed_path(path)
+        try:
+            ws = kernels.workspace(kernels.qgemm_packed_workspace_bytes(m, n, k), cuda)
+            sq = torch.zeros((p.tiles, ld), dtype=torch.float32, device=cuda)
+            plain = kernels.qgemm_packed(x_t, p, ws=ws)
+            resid = kernels.qgemm_packed(x_t, p, epilogue="residual", residual=res, out_sq=sq, sq_ld=ld,
+                                         norm_sq=sq_in, norm_parts=4, norm_weight=nw, ws=ws)
+            glu = kernels.qgemm_packed(x_t, p, epilogue="swiglu", ws=ws)
+            torch.cuda.synchronize()
+            if path == 2:
+                assert kernels.qgemm_packed_status(ws) == 0
+            outs.append([plain.view(torch.int16).clone(), resid.view(torch.int16).clone(),
+                         glu.view(torch.int16).clone(), sq[:, :m].view(torch.int32).clone()])
+        finally:
+            kernels.qgemm_packed_path(0)
+    for a, c in zip(*outs):
+        assert torch.equal(a, c)
