@@ -53,21 +53,29 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["spec_decode", "verify_step", "stochastic", "tree", "tp"],
+    ap.add_argument("--workload", choices=["spec_decode", "verify_step", "stochastic", "tree", "tp", "attention"],
                     default="spec_decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="verify_step: activation rows of the qGEMM (default 5); attention: rows per sequence (5)")
+    ap.add_argument("--attn-case", choices=["config3-verify", "config3-draft", "config2-draft"],
+                    default="config3-verify",
+                    help="attention: config 3's verify (32 sequences, Qwen3-4B heads, 5 rows) or draft pass "
+                         "(Qwen3-0.6B heads, 1 row), or config 2's draft pass (1 sequence, 520 keys)")
     ap.add_argument("--qgemm-path", type=int, choices=[0, 1, 2], default=0,
                     help="packed qGEMM kernel: 0 automatic, 1 warp MMA only, 2 tcgen05 tensor cores only (same bits)")
     return ap.parse_args()
 
 
 def peaks() -> dict:
+    """HBM GB/s and dense bf16 TFLOP/s (burst) measured on this pool, else the recorded fallback figures."""
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         d = json.loads(path.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d.get("bf16_tflops", 1590.0)),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 class Clocks:
@@ -398,13 +406,14 @@ def run_verify_step(args, world: int, rank: int, local: int) -> None:
     gen = torch.Generator(device=device).manual_seed(0)
     copies = [kernels.Packed(*kernels.quantize((torch.randn((15360, 3840), generator=gen, device=device) * 0.02)
                                                .to(torch.bfloat16))) for _ in range(8)]
-    x = torch.randn((5, 3840), generator=gen, device=device).to(torch.bfloat16)
-    y = torch.empty((5, 15360), dtype=torch.bfloat16, device=device)
+    m = args.rows or 5
+    x = torch.randn((m, 3840), generator=gen, device=device).to(torch.bfloat16)
+    y = torch.empty((m, 15360), dtype=torch.bfloat16, device=device)
     reps = -(-151936 // 15360)
     noise = (torch.randn((5, reps * 15360), generator=gen, device=device) * 1e-3).to(torch.bfloat16)
     logits = torch.empty((5, 151936), dtype=torch.bfloat16, device=device)
     drafts = torch.randint(0, 151936, (1, 4), generator=gen, device=device, dtype=torch.int32)
-    ws = kernels.workspace(kernels.qgemm_packed_workspace_bytes(5, 15360, 3840), device)
+    ws = kernels.workspace(kernels.qgemm_packed_workspace_bytes(m, 15360, 3840), device)
     tokens = torch.empty((1, 5), dtype=torch.int32, device=device)
     count = torch.empty((1,), dtype=torch.int32, device=device)
     stream = torch.cuda.current_stream(device)
@@ -426,12 +435,88 @@ def run_verify_step(args, world: int, rank: int, local: int) -> None:
     e1.record(stream)
     torch.cuda.synchronize()
     sec = e0.elapsed_time(e1) / 1000 / (5 * 64)
-    algo = 15360 * 3840 * 9 // 16 + 5 * 3840 * 2 + 5 * 15360 * 2
+    algo = 15360 * 3840 * 9 // 16 + m * 3840 * 2 + m * 15360 * 2
     achieved = algo / sec / 1e9
-    line = {"metric": "qGEMM HBM GB/s (verify step, K=3840, N=15360, M=5)", "value": round(achieved, 1),
+    tflops = 2.0 * 15360 * 3840 * m / sec / 1e12
+    workload = "BASELINE config 1 qGEMM" if m == 5 else f"config 1 qGEMM shape at {m} rows"
+    line = {"metric": f"qGEMM HBM GB/s (verify step, K=3840, N=15360, M={m})", "value": round(achieved, 1),
             "unit": "GB/s", "n_gpus": world, "steps": 5 * 64, "warmup": 3, "ms_per_step": round(sec * 1e3, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16/4-bit",
-            "data": "synthetic", "config": {"workload": "BASELINE config 1 qGEMM", "rotating_weight_copies": 8},
+            "data": "synthetic", "config": {"workload": workload, "rotating_weight_copies": 8,
+                                            "qgemm_path": args.qgemm_path, "tflops": round(tflops, 2)},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None}}
+    if m > 32:  # many rows: the tensor pipe is the bound that matters
+        line["roofline"] = {"bound": "tensor", "achieved": round(tflops, 2), "peak": pk["bf16_tflops"],
+                            "unit": "TFLOP/s", "frac": round(tflops / pk["bf16_tflops"], 4), "traffic": None}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def run_attention(args, world: int, rank: int, local: int) -> None:
+    """One attention launch of a round, alone, through the fused entry point (q/k RMSNorm + RoPE + KV write +
+    attention), 16-token pages, 4 rotating KV layer caches. --attn-case config3-verify: 32 sequences with lengths
+    U[128, 2048] (seed 0), Qwen3-4B heads (32 q / 8 kv, head_dim 128), `--rows` (default 5) rows per sequence;
+    config3-draft: the same sequences, Qwen3-0.6B heads (16 / 8), 1 row; config2-draft: 1 sequence of 520 keys,
+    Qwen3-0.6B heads, 1 row. Bytes per launch: every visible key's K and V once (2 x 8 heads x 128 x 2 B per key)
+    plus the qkv rows in and the output rows out."""
+    import torch
+
+    from ironmule_b200 import kernels
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pk = peaks()
+    gen = torch.Generator(device=device).manual_seed(0)
+    case = args.attn_case
+    b = 1 if case == "config2-draft" else 32
+    hq, hkv, d = (32 if case == "config3-verify" else 16), 8, 128
+    rows = (args.rows or 5) if case == "config3-verify" else 1
+    lens = [520] if b == 1 else torch.randint(128, 2049, (b,), generator=torch.Generator().manual_seed(0)).tolist()
+    cap = 2048 + 64
+    pages = cap // 16
+    copies = 4
+    kc = [torch.randn((b * pages, hkv, 16, d), generator=gen, device=device).to(torch.bfloat16) for _ in range(copies)]
+    vc = [torch.randn((b * pages, hkv, 16, d), generator=gen, device=device).to(torch.bfloat16) for _ in range(copies)]
+    table = torch.arange(b * pages, dtype=torch.int32, device=device).reshape(b, pages)
+    m = b * rows
+    qkv = torch.randn((m, (hq + 2 * hkv) * d), generator=gen, device=device).to(torch.bfloat16)
+    qn = torch.ones(d, dtype=torch.bfloat16, device=device)
+    inv_freq = (1e6 ** (-2.0 * torch.arange(d // 2, device=device, dtype=torch.float32) / d)).contiguous()
+    slots = torch.tensor([n - rows + i for n in lens for i in range(rows)], dtype=torch.int32, device=device)
+    seq_rows = torch.arange(0, m + 1, rows, dtype=torch.int32, device=device)
+    out = torch.empty((m, hq * d), dtype=torch.bfloat16, device=device)
+    ws = kernels.workspace(kernels.attention_workspace_bytes(b, rows, hq, hkv, d, cap, 64), device)
+    stream = torch.cuda.current_stream(device)
+
+    def launches(n):
+        for i in range(n):
+            kernels.attention_qkv(qkv, qn, qn, inv_freq, slots, kc[i % copies], vc[i % copies], table, seq_rows, slots,
+                                  hq=hq, hkv=hkv, d=d, eps=1e-6, max_rows_per_seq=rows, max_kv_len=cap,
+                                  scale=d ** -0.5, out=out, ws=ws)
+
+    launches(max(args.warmup, 3))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        launches(32)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(1, args.steps // 32)
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1000 / (reps * 32)
+    algo = sum(lens) * 2 * hkv * d * 2 + m * (hq + 2 * hkv) * d * 2 + m * hq * d * 2
+    achieved = algo / sec / 1e9
+    line = {"metric": f"attention HBM GB/s ({case}: {b} sequences, {hq}/{hkv} heads, {rows} rows each)",
+            "value": round(achieved, 1), "unit": "GB/s", "n_gpus": world, "steps": reps * 32, "warmup": 3,
+            "ms_per_step": round(sec * 1e3, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{case} attention, fused q/k norm + RoPE + KV write",
+                       "kv_copies_rotating": copies, "bytes_per_launch": algo},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None}}
     if rank == 0:
@@ -554,6 +639,8 @@ def main() -> int:
     try:
         if args.workload == "verify_step":
             run_verify_step(args, world, rank, local)
+        elif args.workload == "attention":
+            run_attention(args, world, rank, local)
         elif args.workload in ("stochastic", "tree", "tp"):
             run_rounds_workload(args, world, rank, local, args.workload)
         else:
