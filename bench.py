@@ -63,6 +63,7 @@ def parse():
                     default="config3-verify",
                     help="attention: config 3's verify (32 sequences, Qwen3-4B heads, 5 rows) or draft pass "
                          "(Qwen3-0.6B heads, 1 row), or config 2's draft pass (1 sequence, 520 keys)")
+    ap.add_argument("--kpc", type=int, default=64, help="attention: keys per split (a multiple of 64)")
     ap.add_argument("--qgemm-path", type=int, choices=[0, 1, 2], default=0,
                     help="packed qGEMM kernel: 0 automatic, 1 warp MMA only, 2 tcgen05 tensor cores only (same bits)")
     return ap.parse_args()
@@ -486,14 +487,14 @@ def run_attention(args, world: int, rank: int, local: int) -> None:
     slots = torch.tensor([n - rows + i for n in lens for i in range(rows)], dtype=torch.int32, device=device)
     seq_rows = torch.arange(0, m + 1, rows, dtype=torch.int32, device=device)
     out = torch.empty((m, hq * d), dtype=torch.bfloat16, device=device)
-    ws = kernels.workspace(kernels.attention_workspace_bytes(b, rows, hq, hkv, d, cap, 64), device)
+    ws = kernels.workspace(kernels.attention_workspace_bytes(b, rows, hq, hkv, d, cap, args.kpc), device)
     stream = torch.cuda.current_stream(device)
 
     def launches(n):
         for i in range(n):
             kernels.attention_qkv(qkv, qn, qn, inv_freq, slots, kc[i % copies], vc[i % copies], table, seq_rows, slots,
                                   hq=hq, hkv=hkv, d=d, eps=1e-6, max_rows_per_seq=rows, max_kv_len=cap,
-                                  scale=d ** -0.5, out=out, ws=ws)
+                                  scale=d ** -0.5, keys_per_split=args.kpc, out=out, ws=ws)
 
     launches(max(args.warmup, 3))
     g = torch.cuda.CUDAGraph()
@@ -516,7 +517,7 @@ def run_attention(args, world: int, rank: int, local: int) -> None:
             "ms_per_step": round(sec * 1e3, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"{case} attention, fused q/k norm + RoPE + KV write",
-                       "kv_copies_rotating": copies, "bytes_per_launch": algo},
+                       "kv_copies_rotating": copies, "bytes_per_launch": algo, "keys_per_split": args.kpc},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None}}
     if rank == 0:

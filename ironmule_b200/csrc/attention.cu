@@ -25,6 +25,7 @@
 // to finish merges the splits in split order. The host picks the CTAs per group from the occupancy and the
 // number of groups (one CTA per split for a single sequence, several splits per CTA for large batches). A row's result depends
 // only on its own query, its mask and the KV -- not on how many rows or sequences share the launch.
+#include <climits>
 #include <math.h>
 
 #include "common.cuh"
@@ -214,6 +215,14 @@ attn_kernel(AttnArgs a) {
   __syncthreads();
   const int kv_len = sm.kv_len;
   const bool any = nq > 0 && (int)blockIdx.x * a.kpc < kv_len;  // this CTA has at least one non-empty split
+  // keys below min_vis are visible to every query vector of this CTA (no window; below the tree slots)
+  int min_vis = 0;
+  if (a.window <= 0 && nq > 0) {
+    int lo = INT_MAX;
+    for (int i = 0; i < nq; i++) lo = min(lo, sm.row_slot[i] + 1);
+    if (a.tree_mask) lo = min(lo, tbase);
+    min_vis = lo;
+  }
   int k_begin = blockIdx.x * a.kpc;
   int k_end = min(kv_len, k_begin + a.kpc);
 
@@ -401,7 +410,19 @@ attn_kernel(AttnArgs a) {
             for (int nt = 0; nt < 2; nt++) mma_bf16(sacc[mt][nt], a0, a1, a2, a3, bk[nt][0], bk[nt][1]);
           }
         }
-        // scale and mask into sm.s
+        // scale and mask into sm.s; a block that every row sees whole (below every row's limit and the tree, no
+      // window) skips the per-key tests
+      if (kb0 + AT_KB <= min_vis) {
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+          for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+              const int qi = mt * 16 + g + (e >> 1) * 8;
+              if (qi < nq) sm.s[qi][n0 + nt * 8 + 2 * t + (e & 1)] = sacc[mt][nt][e] * a.scale;
+            }
+      } else {
 #pragma unroll
         for (int mt = 0; mt < MT; mt++)
 #pragma unroll
@@ -422,6 +443,7 @@ attn_kernel(AttnArgs a) {
                 sm.s[qi][j] = vis ? sacc[mt][nt][e] * a.scale : -INFINITY;
               }
             }
+      }
       }
       __syncthreads();
       // online softmax per query vector: warp w takes w, w+4, ...; p goes out as bf16 high + low parts
