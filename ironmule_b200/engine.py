@@ -55,6 +55,7 @@ class ModelConfig:
     global_every: int = 0           # gemma3: layer i is global when (i + 1) % global_every == 0
     rope_local_theta: float = 10_000.0
     query_scale: float = 0.0        # attention scale; 0 -> head_dim ** -0.5
+    rope_scale: float = 1.0         # linear RoPE scaling of the global layers (positions / rope_scale)
 
     @property
     def qkv_rows(self) -> int:
@@ -185,7 +186,8 @@ class QuantModel:
 
     def __init__(self, cfg: ModelConfig, device: torch.device | str = "cuda", *, seed: int = 0,
                  sigma: float = 0.02, max_seqs: int = 1, max_ctx: int = 1024, max_rows: int = 32,
-                 max_logit_rows: int = 32, keys_per_split: int | None = None, tp: int = 1, rank: int = 0, group=None):
+                 max_logit_rows: int = 32, keys_per_split: int | None = None, tp: int = 1, rank: int = 0, group=None,
+                 weights: dict | None = None):
         self.cfg = cfg
         if tp > 1 and (cfg.heads % tp or cfg.kv_heads % tp or cfg.inter % (64 * tp) or (cfg.inter // tp) % 16
                        or cfg.vocab % tp or (cfg.heads * cfg.head_dim // tp) % 64):
@@ -201,8 +203,13 @@ class QuantModel:
         # 128 for one sequence (enough splits to spread it over the GPU), 256 for batches (fewer partials to merge;
         # measured on B200: config-3 verify attention 166 vs 205 us, config-2 draft pass 11.3 vs 16.3 us at 256)
         self.keys_per_split = keys_per_split or (128 if max_seqs == 1 else 256)
-        gen = torch.Generator(device=self.device).manual_seed(seed)
-        self._build_weights(gen, sigma)
+        if weights is None:
+            gen = torch.Generator(device=self.device).manual_seed(seed)
+            self._build_weights(gen, sigma)
+        else:  # a checkpoint's 4-bit tensors under MLX names (ironmule_b200.checkpoint)
+            from .checkpoint import assign_weights
+            assign_weights(self, weights)
+        self._build_rope()
         self._build_cache()
         self._build_buffers()
 
@@ -253,9 +260,11 @@ class QuantModel:
                 layer.post_attn_norm, layer.post_ff_norm = self._norm(gen, c.hidden), self._norm(gen, c.hidden)
             self.layers.append(layer)
         self.final_norm = self._norm(gen, c.hidden)
-        d = c.head_dim
+
+    def _build_rope(self) -> None:
+        c, d = self.cfg, self.cfg.head_dim
         idx = torch.arange(0, d // 2, dtype=torch.float64)
-        self.inv_freq = (c.rope_theta ** (-2.0 * idx / d)).to(torch.float32).to(self.device)
+        self.inv_freq = (c.rope_theta ** (-2.0 * idx / d) / c.rope_scale).to(torch.float32).to(self.device)
         self.inv_freq_local = (c.rope_local_theta ** (-2.0 * idx / d)).to(torch.float32).to(self.device)
 
     # ---- cache and buffers ------------------------------------------------------------------------------

@@ -8,6 +8,7 @@ from __future__ import annotations
 import datetime
 import os
 import socket
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -22,7 +23,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank(rank: int, world: int, port: int, failures) -> None:
+def _rank(rank: int, world: int, port: int, failures, tmp: str) -> None:
     import torch.distributed as dist
 
     from ironmule_b200 import engine
@@ -43,7 +44,13 @@ def _rank(rank: int, world: int, port: int, failures) -> None:
             err = np.abs(got - want).max()
             assert err <= 2e-2 * np.abs(want).max(), (name, err)
             assert np.mean(got.argmax(1) == want.argmax(1)) >= 0.9, name
-            del ref
+            # the tp = 1 model written as an MLX 4-bit snapshot and read back with tp = 2: the same shards
+            from ironmule_b200 import checkpoint
+            root = checkpoint.save_mlx_4bit(ref, Path(tmp) / f"{name}-{rank}")
+            loaded = checkpoint.load_mlx_4bit(root, dev, max_ctx=256, tp=world, rank=rank, group=dist.group.WORLD)
+            again = loaded.logits_for(prompt, 0).float().cpu().numpy()
+            assert np.array_equal(again, got), name
+            del ref, loaded
             # speculation on the tensor-parallel target == its own greedy decoding (draft replicated)
             fresh = engine.QuantModel(engine.PRESETS[name], dev, seed=4, sigma=0.08, max_ctx=256, tp=world, rank=rank,
                                       group=dist.group.WORLD)
@@ -68,11 +75,11 @@ def _rank(rank: int, world: int, port: int, failures) -> None:
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tensor_parallel_forward_and_speculation_on_two_gpus():
+def test_tensor_parallel_forward_and_speculation_on_two_gpus(tmp_path):
     ctx = torch.multiprocessing.get_context("spawn")
     failures = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, failures)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, failures, str(tmp_path))) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
