@@ -580,7 +580,12 @@ def run_rounds_workload(args, world: int, rank: int, local: int, kind: str) -> N
                     "(232 verify rows per qGEMM call), 1024-token prompts")
         metric = "accepted tokens/s (tree spec decode, Gemma-3-12B + 1B draft, 4x2x2 tree, 8 sequences)"
     room = max(8, ctx - max(p.numel() for p in prompts) - dec.reserve - 8)
-    dec.start([p.to(device) for p in prompts], max_new=room)
+    dev_prompts = [p.to(device) for p in prompts]
+    torch.cuda.synchronize()
+    t_prefill = time.perf_counter()
+    dec.start(dev_prompts, max_new=room)  # both models' prefill, sequences packed into many-row forwards
+    torch.cuda.synchronize()
+    prefill_ms = (time.perf_counter() - t_prefill) * 1000
     dec.round()
     torch.cuda.synchronize()
     dec.capture()
@@ -619,7 +624,9 @@ def run_rounds_workload(args, world: int, rank: int, local: int, kind: str) -> N
                 "config": {"workload": workload,
                            "parallelism": f"tp{world}" if kind == "tp" else f"replicas x{world}",
                            "accepted_per_round": round((after.accepted - before.accepted) / args.steps, 4),
-                           "round_weight_bytes": round_bytes},
+                           "round_weight_bytes": round_bytes,
+                           "prefill_ms": round(prefill_ms, 1),
+                           "prefill_tokens": sum(p.numel() - 1 for p in prompts)},
                 "roofline": {"bound": "hbm", "achieved": round(round_bytes / step_s / 1e9, 1), "peak": pk["hbm_gbs"],
                              "unit": "GB/s", "frac": round(round_bytes / step_s / 1e9 / pk["hbm_gbs"], 4),
                              "traffic": None, "kernel": "whole round (weights streamed per round / round time)"},

@@ -410,6 +410,40 @@ class QuantModel:
             meta = self._meta(part, list(range(start + off, start + off + part.numel())), seq)
             self.forward(meta, max_kv_len=self.max_ctx)
 
+    def prefill_many(self, prompts: list[tuple[int, torch.Tensor]]) -> None:
+        """Prefill several sequence slots together: each forward packs the next (up to 32-token) chunk of as many
+        sequences as fit in max_rows (up to 320 rows), so the projections run at many rows at once. A sequence's
+        chunks are the ones `prefill` would cut, and every kernel is row-invariant, so the KV written is the same
+        bits as prefilling the sequences one by one. `prompts`: (slot, int32 tokens on the device), slots from 0."""
+        dev = self.device
+        step = min(self.max_rows, MAX_SEQ_ROWS)
+        budget = min(self.max_rows, MAX_QGEMM_ROWS)
+        offs = [0] * len(prompts)
+        while True:
+            parts, pos, rows, slots = [], [], [0], []
+            for i, (slot, toks) in enumerate(prompts):
+                if offs[i] >= toks.numel():
+                    continue
+                n = min(step, toks.numel() - offs[i])
+                if rows[-1] + n > budget:
+                    break
+                parts.append(toks[offs[i]:offs[i] + n])
+                pos.extend(range(offs[i], offs[i] + n))
+                rows.append(rows[-1] + n)
+                slots.append(slot)
+                offs[i] += n
+            if not parts:
+                return
+            m = rows[-1]
+            meta = RowMeta(tokens=torch.cat(parts).to(torch.int32).contiguous(), token_stride=1,
+                           pos=torch.tensor(pos, dtype=torch.int32, device=dev),
+                           seq=torch.tensor([g for g in range(len(slots)) for _ in range(rows[g + 1] - rows[g])],
+                                            dtype=torch.int32, device=dev),
+                           seq_rows=torch.tensor(rows, dtype=torch.int32, device=dev), rows=m,
+                           max_rows_per_seq=max(rows[g + 1] - rows[g] for g in range(len(slots))),
+                           seq_slot=torch.tensor(slots, dtype=torch.int32, device=dev))
+            self.forward(meta, max_kv_len=self.max_ctx)
+
     def logits_for(self, tokens: torch.Tensor, start: int, seq: int = 0) -> torch.Tensor:
         """Feed `tokens` (one forward, rows at slots start..) and return every row's logits [M, V]."""
         m = tokens.numel()
@@ -564,8 +598,9 @@ class SpecDecoder:
             self.hist[b, :length] = p.to(torch.int32)
             self.n[b] = length
             self.target_len[b] = length + max_new
-            self.target.prefill(p[:-1].to(torch.int32), seq=b)
-            self.draft.prefill(p[:-1].to(torch.int32), seq=b)
+        body = [(b, p[:-1].to(torch.int32)) for b, p in enumerate(prompts)]
+        self.target.prefill_many(body)
+        self.draft.prefill_many(body)
         self.stats.zero_()
         if self.sampling is not None:
             self.offset.zero_()

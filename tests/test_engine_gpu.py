@@ -395,3 +395,24 @@ def test_batched_speculation(cuda):
     for b, p in enumerate(prompts):
         solo = tiny("tiny-target", seed=1, sigma=0.08)
         assert dec.generated(b, p.numel()) == engine.greedy_decode(solo, p, 20), b
+
+
+def test_batched_prefill_writes_the_same_kv(cuda):
+    """prefill_many packs several sequences' 32-token chunks into one forward (here 96 rows per forward): the
+    caches hold the same bits as prefilling the sequences one at a time."""
+    lens = (70, 33, 5, 100)
+    gen = torch.Generator().manual_seed(12)
+    prompts = [torch.randint(0, 1000, (n,), generator=gen).to(torch.int32).to(cuda) for n in lens]
+    one = tiny("tiny-target", seed=4, sigma=0.08, max_seqs=4, max_rows=96, max_logit_rows=8)
+    many = tiny("tiny-target", seed=4, sigma=0.08, max_seqs=4, max_rows=96, max_logit_rows=8)
+    for b, p in enumerate(prompts):
+        one.prefill(p, seq=b)
+    many.prefill_many(list(enumerate(prompts)))
+    torch.cuda.synchronize()
+    for b, n in enumerate(lens):
+        pages = one.page_table[b]
+        for cache in ("k_cache", "v_cache"):
+            def slots(model):  # [layers, pages, Hkv, 16, D] -> [layers, slot, Hkv, D]
+                t = getattr(model, cache)[:, pages].permute(0, 1, 3, 2, 4)
+                return t.reshape(model.cfg.layers, -1, model.cfg.kv_heads, model.cfg.head_dim)[:, :n]
+            assert torch.equal(slots(one).view(torch.int16), slots(many).view(torch.int16)), (b, cache)
