@@ -68,7 +68,8 @@ struct AttnArgs {
 
 template <int D, int NQ, bool FUSED>
 struct AttnSmem {
-  static constexpr int NEW = FUSED ? AT_MAXNEW : 1;
+  // new keys one CTA may hold: a query block of at most 8 vectors comes from at most 8 rows per sequence
+  static constexpr int NEW = FUSED ? (NQ <= 8 ? 8 : AT_MAXNEW) : 1;
   static constexpr int QM = NQ < 16 ? 16 : NQ;  // rows of the m16 MMA tiles (rows >= nq stay zero)
   // Row strides are padded by 16 bytes so the MMA fragment loads (and ldmatrix rows) hit distinct banks.
   uint16_t qs[QM][D + 8];         // bf16 queries
@@ -185,7 +186,7 @@ attn_kernel(AttnArgs a) {
         const bool isnew = slot >= 0 && (slot / a.kpc) % stride_x == (int)blockIdx.x;
         const unsigned ball = __ballot_sync(0xffffffffu, isnew);
         const int idx = n + __popc(ball & ((1u << lane) - 1u));
-        if (isnew && idx < AT_MAXNEW) {
+        if (isnew && idx < Smem::NEW) {
           sm.new_row[idx] = r0 + r;
           sm.new_slot[idx] = slot;
         }
@@ -194,7 +195,7 @@ attn_kernel(AttnArgs a) {
     }
     if (lane == 0) {
       sm.kv_len = mx + 1;
-      sm.nnew = min(n, AT_MAXNEW);
+      sm.nnew = min(n, Smem::NEW);
     }
   }
   for (int i = tid; i < Smem::QM * (D + 8) / 2; i += AT_THREADS) reinterpret_cast<uint32_t*>(&sm.qs[0][0])[i] = 0u;
