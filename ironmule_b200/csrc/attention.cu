@@ -32,7 +32,6 @@
 
 namespace im {
 
-constexpr int AT_THREADS = 128;
 constexpr int AT_KB = 64;       // keys per shared-memory block
 constexpr int AT_MAXNEW = 32;   // new (written by this launch) keys per split at most: rows per sequence <= 32
 constexpr int AT_MW = 64;       // splits whose merge weights are kept in shared memory
@@ -145,9 +144,10 @@ __device__ __forceinline__ void norm_rope_vals(const float (&v)[D / 32], const u
   }
 }
 
-template <int D, int NQ, bool FUSED>
-__global__ void __launch_bounds__(AT_THREADS)
+template <int D, int NQ, bool FUSED, int W>
+__global__ void __launch_bounds__(32 * W)
 attn_kernel(AttnArgs a) {
+  constexpr int TH = 32 * W;  // W warps
   extern __shared__ __align__(16) unsigned char smem_raw[];
   using Smem = AttnSmem<D, NQ, FUSED>;
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
@@ -198,13 +198,13 @@ attn_kernel(AttnArgs a) {
       sm.nnew = min(n, Smem::NEW);
     }
   }
-  for (int i = tid; i < Smem::QM * (D + 8) / 2; i += AT_THREADS) reinterpret_cast<uint32_t*>(&sm.qs[0][0])[i] = 0u;
-  for (int i = tid; i < Smem::QM * (AT_KB + 8) / 2; i += AT_THREADS) {
+  for (int i = tid; i < Smem::QM * (D + 8) / 2; i += TH) reinterpret_cast<uint32_t*>(&sm.qs[0][0])[i] = 0u;
+  for (int i = tid; i < Smem::QM * (AT_KB + 8) / 2; i += TH) {
     reinterpret_cast<uint32_t*>(&sm.ph[0][0])[i] = 0u;
     reinterpret_cast<uint32_t*>(&sm.pl[0][0])[i] = 0u;
   }
-  for (int i = tid; i < Smem::QM; i += AT_THREADS) sm.alpha[i] = 0.f;
-  for (int i = tid; i < NQ; i += AT_THREADS) {
+  for (int i = tid; i < Smem::QM; i += TH) sm.alpha[i] = 0.f;
+  for (int i = tid; i < NQ; i += TH) {
     sm.m[i] = -INFINITY;
     sm.l[i] = 0.f;
     if (i < nq) {
@@ -234,7 +234,7 @@ attn_kernel(AttnArgs a) {
       sm.page[tid] = slot < k_end ? a.page_table[(size_t)prow * a.max_pages + (slot >> 4)] : 0;
     }
     if constexpr (FUSED) {
-      for (int j = tid; j < AT_KB; j += AT_THREADS) {
+      for (int j = tid; j < AT_KB; j += TH) {
         int idx = -1;
         for (int n = 0; n < sm.nnew; n++)
           if (sm.new_slot[n] == kb0 + j) idx = n;
@@ -242,10 +242,10 @@ attn_kernel(AttnArgs a) {
       }
     }
     __syncthreads();
-    constexpr int PER = AT_KB * (D / 8) / AT_THREADS;
+    constexpr int PER = AT_KB * (D / 8) / TH;
 #pragma unroll
     for (int t = 0; t < PER; t++) {
-      const int i = tid + t * AT_THREADS;
+      const int i = tid + t * TH;
       const int j = i / (D / 8), c = i % (D / 8);
       const int slot = kb0 + j;
       bool skip = false;
@@ -260,7 +260,7 @@ attn_kernel(AttnArgs a) {
   };
   auto fill_new = [&]() {
     if constexpr (FUSED) {
-      for (int i = tid; i < AT_KB * (D / 8); i += AT_THREADS) {
+      for (int i = tid; i < AT_KB * (D / 8); i += TH) {
         const int j = i / (D / 8), c = i % (D / 8);
         const int idx = sm.newidx[j];
         if (idx >= 0) {
@@ -281,12 +281,12 @@ attn_kernel(AttnArgs a) {
       // this CTA's query vectors: RMSNorm + RoPE, rounded to bf16 as the unfused path stores them; a warp
       // loads all of its vectors before computing any
       {
-        constexpr int VPW = NQ / (AT_THREADS / 32);
+        constexpr int VPW = NQ / (TH / 32);
         float v[VPW][D / 32];
         int pos[VPW];
 #pragma unroll
         for (int t = 0; t < VPW; t++) {
-          const int qi = warp + t * (AT_THREADS / 32);
+          const int qi = warp + t * (TH / 32);
           if (qi < nq) {
             const int row = r0 + (q0 + qi) / G, head = kvh * G + (q0 + qi) % G;
             const uint16_t* src = a.qkv + (size_t)row * stride + head * D;
@@ -297,7 +297,7 @@ attn_kernel(AttnArgs a) {
         }
 #pragma unroll
         for (int t = 0; t < VPW; t++) {
-          const int qi = warp + t * (AT_THREADS / 32);
+          const int qi = warp + t * (TH / 32);
           if (qi < nq) {
             uint16_t o[D / 32];
             norm_rope_vals<D>(v[t], a.q_norm, a.gemma, a.eps, pos[t], a.inv_freq, o);
@@ -307,7 +307,7 @@ attn_kernel(AttnArgs a) {
         }
       }
       // the new rows' keys and values of this CTA's splits (the first query block's CTA also writes them out)
-      for (int n = warp; n < sm.nnew; n += AT_THREADS / 32) {
+      for (int n = warp; n < sm.nnew; n += TH / 32) {
         const int row = sm.new_row[n], slot = sm.new_slot[n];
         const uint16_t* src = a.qkv + (size_t)row * stride + (a.Hq + kvh) * D;
         uint16_t o[D / 32];
@@ -333,7 +333,7 @@ attn_kernel(AttnArgs a) {
       fill_new();
     }
   } else {
-    for (int i = tid; i < nq * D; i += AT_THREADS) {
+    for (int i = tid; i < nq * D; i += TH) {
       const int qi = i / D, d = i % D;
       const int row = r0 + (q0 + qi) / G, head = kvh * G + (q0 + qi) % G;
       sm.qs[qi][d] = a.q[((size_t)row * a.Hq + head) * D + d];
@@ -344,7 +344,9 @@ attn_kernel(AttnArgs a) {
   // keys 16w..16w+15 (two n8 tiles) for all query rows. Output O[q][d] = P V: warp w owns dims
   // [w D/4, (w+1) D/4); P enters as two bf16 operands (high and low parts), so it keeps ~16 bits.
   constexpr int MT = Smem::QM / 16;     // m16 tiles of query rows
-  constexpr int DW = D / 4;             // output dims per warp
+  constexpr int DW = D / W;             // output dims per warp
+  constexpr int KPW = AT_KB / W;        // keys per warp in the scores
+  constexpr int NTK = KPW / 8;          // n8 tiles of keys per warp
   constexpr int NTO = DW / 8;           // n8 tiles of output dims per warp
   float o_acc[MT][NTO][4];
 #pragma unroll
@@ -362,11 +364,11 @@ attn_kernel(AttnArgs a) {
       __syncthreads();
       k_begin = split * a.kpc;
       k_end = min(kv_len, k_begin + a.kpc);
-      for (int i = tid; i < NQ; i += AT_THREADS) {
+      for (int i = tid; i < NQ; i += TH) {
         sm.m[i] = -INFINITY;
         sm.l[i] = 0.f;
       }
-      for (int i = tid; i < Smem::QM; i += AT_THREADS) sm.alpha[i] = 0.f;
+      for (int i = tid; i < Smem::QM; i += TH) sm.alpha[i] = 0.f;
 #pragma unroll
       for (int mt = 0; mt < MT; mt++)
 #pragma unroll
@@ -386,19 +388,19 @@ attn_kernel(AttnArgs a) {
       __syncthreads();
       // scores
       {
-        float sacc[MT][2][4];
+        float sacc[MT][NTK][4];
 #pragma unroll
         for (int mt = 0; mt < MT; mt++)
 #pragma unroll
-          for (int nt = 0; nt < 2; nt++)
+          for (int nt = 0; nt < NTK; nt++)
 #pragma unroll
             for (int e = 0; e < 4; e++) sacc[mt][nt][e] = 0.f;
-        const int n0 = warp * 16;
+        const int n0 = warp * KPW;
 #pragma unroll 4
         for (int kk = 0; kk < D / 16; kk++) {
-          uint32_t bk[2][2];
+          uint32_t bk[NTK][2];
 #pragma unroll
-          for (int nt = 0; nt < 2; nt++) {
+          for (int nt = 0; nt < NTK; nt++) {
             bk[nt][0] = sm.ks[n0 + nt * 8 + g][kk * 8 + t];
             bk[nt][1] = sm.ks[n0 + nt * 8 + g][kk * 8 + 4 + t];
           }
@@ -408,7 +410,7 @@ attn_kernel(AttnArgs a) {
             const uint32_t* q8r = reinterpret_cast<const uint32_t*>(&sm.qs[mt * 16 + g + 8][kk * 16 + 2 * t]);
             const uint32_t a0 = q0r[0], a1 = q8r[0], a2 = q0r[4], a3 = q8r[4];
 #pragma unroll
-            for (int nt = 0; nt < 2; nt++) mma_bf16(sacc[mt][nt], a0, a1, a2, a3, bk[nt][0], bk[nt][1]);
+            for (int nt = 0; nt < NTK; nt++) mma_bf16(sacc[mt][nt], a0, a1, a2, a3, bk[nt][0], bk[nt][1]);
           }
         }
         // scale and mask into sm.s; a block that every row sees whole (below every row's limit and the tree, no
@@ -417,7 +419,7 @@ attn_kernel(AttnArgs a) {
 #pragma unroll
         for (int mt = 0; mt < MT; mt++)
 #pragma unroll
-          for (int nt = 0; nt < 2; nt++)
+          for (int nt = 0; nt < NTK; nt++)
 #pragma unroll
             for (int e = 0; e < 4; e++) {
               const int qi = mt * 16 + g + (e >> 1) * 8;
@@ -427,7 +429,7 @@ attn_kernel(AttnArgs a) {
 #pragma unroll
         for (int mt = 0; mt < MT; mt++)
 #pragma unroll
-          for (int nt = 0; nt < 2; nt++)
+          for (int nt = 0; nt < NTK; nt++)
 #pragma unroll
             for (int e = 0; e < 4; e++) {
               const int qi = mt * 16 + g + (e >> 1) * 8;
@@ -448,7 +450,7 @@ attn_kernel(AttnArgs a) {
       }
       __syncthreads();
       // online softmax per query vector: warp w takes w, w+4, ...; p goes out as bf16 high + low parts
-      for (int qi = warp; qi < nq; qi += AT_THREADS / 32) {
+      for (int qi = warp; qi < nq; qi += TH / 32) {
         const float s0 = sm.s[qi][lane], s1 = sm.s[qi][lane + 32];
         float bm = fmaxf(s0, s1);
 #pragma unroll
@@ -528,7 +530,7 @@ attn_kernel(AttnArgs a) {
                      make_float2(o_acc[mt][nt][2 * h], o_acc[mt][nt][2 * h + 1]));
             }
           }
-      for (int i = tid; i < nq; i += AT_THREADS) {
+      for (int i = tid; i < nq; i += TH) {
         __stcg(mine + (size_t)i * (D + AT_PAD) + D, sm.m[i]);
         __stcg(mine + (size_t)i * (D + AT_PAD) + D + 1, sm.l[i]);
       }
@@ -552,7 +554,7 @@ attn_kernel(AttnArgs a) {
   float* L = &sm.alpha[0];  // reuse: per-vector denominators
   if (used <= AT_MW) {
     // every (vector, split) max and sum loaded at once into shared memory (mw: maxima then weights, s: sums)
-    for (int job = tid; job < nq * used; job += AT_THREADS) {
+    for (int job = tid; job < nq * used; job += TH) {
       const int i = job / used, sp = job % used;
       const float* p = a.part + ((group * a.nsplit + sp) * NQ + i) * (D + AT_PAD);
       sm.mw[i][sp] = __ldcg(p + D);
@@ -560,7 +562,7 @@ attn_kernel(AttnArgs a) {
     }
     __syncthreads();
   }
-  for (int i = warp; i < nq; i += AT_THREADS / 32) {
+  for (int i = warp; i < nq; i += TH / 32) {
     auto m_of = [&](int sp) {
       return used <= AT_MW ? sm.mw[i][sp] : __ldcg(a.part + ((group * a.nsplit + sp) * NQ + i) * (D + AT_PAD) + D);
     };
@@ -595,7 +597,7 @@ attn_kernel(AttnArgs a) {
   }
   __syncthreads();
   constexpr int C4 = D / 4;
-  for (int job = tid; job < nq * C4; job += AT_THREADS) {
+  for (int job = tid; job < nq * C4; job += TH) {
     const int i = job / C4, d4 = (job % C4) * 4;
     const float mx = sm.m[i];
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -639,19 +641,19 @@ attn_kernel(AttnArgs a) {
 // way whichever CTA walks it.
 static int g_attn_waves = 2;
 
-template <int D, int NQ, bool FUSED>
+template <int D, int NQ, bool FUSED, int W>
 static int launch_attn(const AttnArgs& args, int B, cudaStream_t st) {
   const size_t smem = sizeof(AttnSmem<D, NQ, FUSED>);
   static bool configured = false;  // per instantiation
   static int resident = 1, sms = 148;
   if (!configured) {
     cudaError_t e =
-        cudaFuncSetAttribute(attn_kernel<D, NQ, FUSED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(attn_kernel<D, NQ, FUSED, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int dev = 0;
     if (e == cudaSuccess) e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, attn_kernel<D, NQ, FUSED>, AT_THREADS, smem);
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, attn_kernel<D, NQ, FUSED, W>, 32 * W, smem);
     if (e != cudaSuccess) {
       set_error("attention: cannot configure the kernel for %zu bytes of shared memory: %s", smem,
                 cudaGetErrorString(e));
@@ -664,13 +666,16 @@ static int launch_attn(const AttnArgs& args, int B, cudaStream_t st) {
   const long long want = ((long long)sms * resident * g_attn_waves + groups - 1) / groups;
   const int per_group = (int)(want < 1 ? 1 : (want > args.nsplit ? args.nsplit : want));
   dim3 grid(per_group, args.Hkv, B * args.qblocks);
-  return launch("attn_kernel", attn_kernel<D, NQ, FUSED>, grid, dim3(AT_THREADS), smem, st, args);
+  return launch("attn_kernel", attn_kernel<D, NQ, FUSED, W>, grid, dim3(32 * W), smem, st, args);
 }
 
 template <bool FUSED>
 static int dispatch_attn(const AttnArgs& args, int64_t D, int nq, int B, cudaStream_t st) {
-  if (D == 128) return nq == 8 ? launch_attn<128, 8, FUSED>(args, B, st) : launch_attn<128, 32, FUSED>(args, B, st);
-  return nq == 8 ? launch_attn<256, 8, FUSED>(args, B, st) : launch_attn<256, 32, FUSED>(args, B, st);
+  // 4 warps for query blocks of up to 8 vectors, 8 warps for blocks of 32 (more warps in flight where shared
+  // memory limits the CTAs per SM); every score and output element is computed the same way either way
+  if (D == 128)
+    return nq == 8 ? launch_attn<128, 8, FUSED, 4>(args, B, st) : launch_attn<128, 32, FUSED, 8>(args, B, st);
+  return nq == 8 ? launch_attn<256, 8, FUSED, 4>(args, B, st) : launch_attn<256, 32, FUSED, 8>(args, B, st);
 }
 
 static void attn_geometry(int64_t rows_per_seq, int64_t G, int* nq, int* qblocks) {
