@@ -671,10 +671,15 @@ static int launch_attn(const AttnArgs& args, int B, cudaStream_t st) {
 
 template <bool FUSED>
 static int dispatch_attn(const AttnArgs& args, int64_t D, int nq, int B, cudaStream_t st) {
-  // 4 warps for query blocks of up to 8 vectors, 8 warps for blocks of 32 (more warps in flight where shared
-  // memory limits the CTAs per SM); every score and output element is computed the same way either way
-  if (D == 128)
-    return nq == 8 ? launch_attn<128, 8, FUSED, 4>(args, B, st) : launch_attn<128, 32, FUSED, 8>(args, B, st);
+  // 8 warps for query blocks of 32 vectors (more warps in flight where shared memory limits the CTAs per SM) and
+  // for small blocks of head_dim 128 when the (sequence, kv head) groups are fewer than the SMs (one sequence:
+  // each split's chain is shorter); 4 warps for small blocks of large batches (more CTAs per SM). Every score and
+  // output element is computed the same way whatever the warp count.
+  if (D == 128) {
+    if (nq != 8) return launch_attn<128, 32, FUSED, 8>(args, B, st);
+    const long long groups = (long long)B * args.Hkv * args.qblocks;
+    return groups < 148 ? launch_attn<128, 8, FUSED, 8>(args, B, st) : launch_attn<128, 8, FUSED, 4>(args, B, st);
+  }
   return nq == 8 ? launch_attn<256, 8, FUSED, 4>(args, B, st) : launch_attn<256, 32, FUSED, 8>(args, B, st);
 }
 

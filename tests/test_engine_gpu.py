@@ -416,3 +416,26 @@ def test_batched_prefill_writes_the_same_kv(cuda):
                 t = getattr(model, cache)[:, pages].permute(0, 1, 3, 2, 4)
                 return t.reshape(model.cfg.layers, -1, model.cfg.kv_heads, model.cfg.head_dim)[:, :n]
             assert torch.equal(slots(one).view(torch.int16), slots(many).view(torch.int16)), (b, cache)
+
+
+@pytest.mark.parametrize("rows,hq", [(1, 16), (2, 16), (5, 32)])
+def test_attention_row_alone_equals_row_in_a_batch(cuda, rows, hq):
+    """20 sequences in one launch (160 kv-head groups: the large-batch warp layout and several splits per CTA)
+    against each sequence alone (8 groups: the one-sequence layout, one split per CTA): the same bits."""
+    rng = np.random.default_rng(rows * hq)
+    b, hkv, d, max_pages = 20, 8, 128, 40
+    lens = rng.integers(rows + 1, max_pages * 16 - 8, b).tolist()
+    table = rng.permutation(b * max_pages).reshape(b, max_pages).astype(np.int32)
+    shape = (b * max_pages, hkv, 16, d)
+    kc, vc = bf16_bits_to_torch(rand_bits(rng, shape), cuda), bf16_bits_to_torch(rand_bits(rng, shape), cuda)
+    q = bf16_bits_to_torch(rand_bits(rng, (b * rows, hq, d)), cuda)
+    slots = torch.tensor(np.concatenate([np.arange(n - rows, n) for n in lens]).astype(np.int32), device=cuda)
+    tbl = torch.from_numpy(table).to(cuda)
+    kw = dict(max_rows_per_seq=rows, max_kv_len=max_pages * 16, scale=d ** -0.5, keys_per_split=128)
+    seq_rows = torch.arange(0, b * rows + 1, rows, dtype=torch.int32, device=cuda)
+    together = kernels.attention(q, kc, vc, tbl, seq_rows, slots, **kw).clone()
+    one_rows = torch.tensor([0, rows], dtype=torch.int32, device=cuda)
+    for s in range(b):
+        alone = kernels.attention(q[s * rows:(s + 1) * rows].contiguous(), kc, vc, tbl[s:s + 1].contiguous(), one_rows,
+                                  slots[s * rows:(s + 1) * rows].contiguous(), **kw)
+        assert torch.equal(alone.view(torch.int16), together[s * rows:(s + 1) * rows].view(torch.int16)), s
