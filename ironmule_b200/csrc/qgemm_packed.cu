@@ -317,11 +317,12 @@ qgemm_packed_kernel(Q4Args a) {
       for (int nt = 0; nt < NT; nt++)
 #pragma unroll
         for (int e = 0; e < 4; e++) tot[tt][nt][e] = 0.f;
-    // loads of four splits at a time are issued together; the adds stay in split order
-    for (int s0 = 0; s0 < a.splits; s0 += 4) {
-      float buf[4][NV];
+    // loads of SB splits at a time (64 floats per lane) are issued together; the adds stay in split order
+    constexpr int SB = NV <= 8 ? 8 : (NV <= 16 ? 4 : 2);
+    for (int s0 = 0; s0 < a.splits; s0 += SB) {
+      float buf[SB][NV];
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
+      for (int j = 0; j < SB; j++) {
         if (s0 + j < a.splits) {
           const float* src = a.partial + ((size_t)tile * a.splits + s0 + j) * NV * 32;
 #pragma unroll
@@ -329,7 +330,7 @@ qgemm_packed_kernel(Q4Args a) {
         }
       }
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
+      for (int j = 0; j < SB; j++) {
         if (s0 + j < a.splits) {
 #pragma unroll
           for (int tt = 0; tt < 2; tt++)
