@@ -416,32 +416,22 @@ class QuantModel:
         chunks are the ones `prefill` would cut, and every kernel is row-invariant, so the KV written is the same
         bits as prefilling the sequences one by one. `prompts`: (slot, int32 tokens on the device), slots from 0."""
         dev = self.device
-        step = min(self.max_rows, MAX_SEQ_ROWS)
-        budget = min(self.max_rows, MAX_QGEMM_ROWS)
-        offs = [0] * len(prompts)
-        while True:
-            parts, pos, rows, slots = [], [], [0], []
-            for i, (slot, toks) in enumerate(prompts):
-                if offs[i] >= toks.numel():
-                    continue
-                n = min(step, toks.numel() - offs[i])
-                if rows[-1] + n > budget:
-                    break
-                parts.append(toks[offs[i]:offs[i] + n])
-                pos.extend(range(offs[i], offs[i] + n))
+        plan = prefill_plan([t.numel() for _, t in prompts], min(self.max_rows, MAX_SEQ_ROWS),
+                            min(self.max_rows, MAX_QGEMM_ROWS))
+        for forward in plan:
+            parts = [prompts[i][1][off:off + n] for i, off, n in forward]
+            rows = [0]
+            for _, _, n in forward:
                 rows.append(rows[-1] + n)
-                slots.append(slot)
-                offs[i] += n
-            if not parts:
-                return
-            m = rows[-1]
             meta = RowMeta(tokens=torch.cat(parts).to(torch.int32).contiguous(), token_stride=1,
-                           pos=torch.tensor(pos, dtype=torch.int32, device=dev),
-                           seq=torch.tensor([g for g in range(len(slots)) for _ in range(rows[g + 1] - rows[g])],
+                           pos=torch.tensor([p for _, off, n in forward for p in range(off, off + n)],
                                             dtype=torch.int32, device=dev),
-                           seq_rows=torch.tensor(rows, dtype=torch.int32, device=dev), rows=m,
-                           max_rows_per_seq=max(rows[g + 1] - rows[g] for g in range(len(slots))),
-                           seq_slot=torch.tensor(slots, dtype=torch.int32, device=dev))
+                           seq=torch.tensor([g for g, (_, _, n) in enumerate(forward) for _ in range(n)],
+                                            dtype=torch.int32, device=dev),
+                           seq_rows=torch.tensor(rows, dtype=torch.int32, device=dev), rows=rows[-1],
+                           max_rows_per_seq=max(n for _, _, n in forward),
+                           seq_slot=torch.tensor([prompts[i][0] for i, _, _ in forward], dtype=torch.int32,
+                                                 device=dev))
             self.forward(meta, max_kv_len=self.max_ctx)
 
     def logits_for(self, tokens: torch.Tensor, start: int, seq: int = 0) -> torch.Tensor:
@@ -449,6 +439,30 @@ class QuantModel:
         m = tokens.numel()
         meta = self._meta(tokens.contiguous(), list(range(start, start + m)), seq)
         return self.forward(meta, max_kv_len=self.max_ctx, logit_rows=m)
+
+
+def prefill_plan(lengths: list[int], step: int, budget: int) -> list[list[tuple[int, int, int]]]:
+    """The forwards of a packed prefill: each a list of (prompt index, offset, count). Every prompt advances by
+    chunks of `step` tokens (the chunks a one-by-one prefill cuts); a forward takes, in prompt order, the next
+    chunk of each unfinished prompt while the rows stay within `budget`."""
+    if step < 1 or budget < step:
+        raise ValueError("need 1 <= step <= budget")
+    offs = [0] * len(lengths)
+    plan = []
+    while True:
+        forward, rows = [], 0
+        for i, n in enumerate(lengths):
+            if offs[i] >= n:
+                continue
+            c = min(step, n - offs[i])
+            if rows + c > budget:
+                break
+            forward.append((i, offs[i], c))
+            offs[i] += c
+            rows += c
+        if not forward:
+            return plan
+        plan.append(forward)
 
 
 @dataclass

@@ -82,3 +82,28 @@ def test_gate_up_interleave_round_trip():
     gu = interleave_gate_up(g, u)
     g2, u2 = checkpoint._deinterleave(gu)
     assert torch.equal(g2, g) and torch.equal(u2, u)
+
+
+def test_shard_slices_of_quantised_tensors_equal_quantised_shards():
+    """The loader cuts tensor-parallel shards out of the quantised tensors (rows for q/k/v/gate/up/vocabulary,
+    64-aligned columns for o/down). Quantisation is per row and per 64-wide group, so a slice of the quantised
+    tensor equals the quantisation of the same slice of the dense matrix (oracle quantiser)."""
+    import numpy as np
+
+    from oracle import bf16, quant
+
+    rng = np.random.default_rng(0)
+    w = bf16.round_f32(rng.normal(0, 0.05, (96, 512)).astype(np.float32))
+    wq, s, b = quant.quantize(w)
+    as_torch = (torch.from_numpy(wq.view(np.int32)), torch.from_numpy(s.view(np.int16)),
+                torch.from_numpy(b.view(np.int16)))
+    for r0, r1 in ((0, 32), (32, 96)):
+        want = quant.quantize(w[r0:r1])
+        got = checkpoint._rows(as_torch, r0, r1)
+        for g, x in zip(got, want):
+            assert np.array_equal(g.numpy(), x.view(g.numpy().dtype))
+    for c0, c1 in ((0, 256), (256, 512), (128, 384)):
+        want = quant.quantize(np.ascontiguousarray(w[:, c0:c1]))
+        got = checkpoint._cols(as_torch, c0, c1)
+        for g, x in zip(got, want):
+            assert np.array_equal(g.contiguous().numpy(), x.view(g.numpy().dtype))
