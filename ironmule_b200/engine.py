@@ -32,8 +32,8 @@ from dataclasses import dataclass, field
 import torch
 
 from . import kernels
+from .kvpool import PAGE, PagePool  # PAGE: KV slots per cache page
 
-PAGE = 16
 MAX_QGEMM_ROWS = 320   # rows of one forward (the packed qGEMM takes them in chunks of 32)
 MAX_SEQ_ROWS = 32      # rows of one sequence in one forward (the fused attention's limit): prefill chunks
 
@@ -414,9 +414,11 @@ class QuantModel:
         """Prefill several sequence slots together: each forward packs the next (up to 32-token) chunk of as many
         sequences as fit in max_rows (up to 320 rows), so the projections run at many rows at once. A sequence's
         chunks are the ones `prefill` would cut, and every kernel is row-invariant, so the KV written is the same
-        bits as prefilling the sequences one by one. `prompts`: (slot, int32 tokens on the device), slots from 0."""
+        bits as prefilling the sequences one by one. `prompts`: (slot, int32 tokens on the device[, start]), the
+        tokens going to slots start.. of the slot (0 by default: the K/V of slots below start are already there)."""
         dev = self.device
-        plan = prefill_plan([t.numel() for _, t in prompts], min(self.max_rows, MAX_SEQ_ROWS),
+        starts = [p[2] if len(p) > 2 else 0 for p in prompts]
+        plan = prefill_plan([p[1].numel() for p in prompts], min(self.max_rows, MAX_SEQ_ROWS),
                             min(self.max_rows, MAX_QGEMM_ROWS))
         for forward in plan:
             parts = [prompts[i][1][off:off + n] for i, off, n in forward]
@@ -424,7 +426,7 @@ class QuantModel:
             for _, _, n in forward:
                 rows.append(rows[-1] + n)
             meta = RowMeta(tokens=torch.cat(parts).to(torch.int32).contiguous(), token_stride=1,
-                           pos=torch.tensor([p for _, off, n in forward for p in range(off, off + n)],
+                           pos=torch.tensor([starts[i] + p for i, off, n in forward for p in range(off, off + n)],
                                             dtype=torch.int32, device=dev),
                            seq=torch.tensor([g for g, (_, _, n) in enumerate(forward) for _ in range(n)],
                                             dtype=torch.int32, device=dev),
@@ -502,7 +504,7 @@ class SpecDecoder:
     """
 
     def __init__(self, target: QuantModel, draft: QuantModel, *, k: int = 4, batch: int = 1,
-                 sampling: Sampling | None = None):
+                 sampling: Sampling | None = None, prefix_cache: bool = False):
         if target.cfg.vocab != draft.cfg.vocab:
             raise ValueError("draft and target must share a vocabulary")
         if batch > min(target.max_seqs, draft.max_seqs):
@@ -547,6 +549,11 @@ class SpecDecoder:
             self.ws_accept = kernels.workspace(kernels.sampling_workspace_bytes(b * (2 * k + 1)), dev)
         self.graph: torch.cuda.CUDAGraph | None = None
         self.gpu_launches_per_round = 0
+        self.pool: PagePool | None = None
+        if prefix_cache:
+            # one page pool over both models' caches: a slot's row lists the same physical pages in each
+            pages = min(target.max_seqs * target.pages_per_seq, draft.max_seqs * draft.pages_per_seq)
+            self.pool = PagePool(pages, batch, min(target.pages_per_seq, draft.pages_per_seq), lead=2)
 
     # ---- one round, issued on the current stream --------------------------------------------------------
     def round(self) -> None:
@@ -605,19 +612,88 @@ class SpecDecoder:
         with all but the last prompt token."""
         if len(prompts) != self.batch:
             raise ValueError("one prompt per sequence slot")
-        for b, p in enumerate(prompts):
+        for p in prompts:
             length = p.numel()
             if length < 2 or length + max_new + self.reserve + 1 > self.cap:
                 raise ValueError("prompt too short or too long for the cache")
+        self.finish()  # with a page pool: the previous requests' pages go back to it (their K/V kept as a cache)
+        for b, p in enumerate(prompts):
+            length = p.numel()
             self.hist[b, :length] = p.to(torch.int32)
             self.n[b] = length
             self.target_len[b] = length + max_new
-        body = [(b, p[:-1].to(torch.int32)) for b, p in enumerate(prompts)]
-        self.target.prefill_many(body)
-        self.draft.prefill_many(body)
+        if self.pool is None:
+            body = [(b, p[:-1].to(torch.int32)) for b, p in enumerate(prompts)]
+            self.target.prefill_many(body)
+            self.draft.prefill_many(body)
+            self.prefill_tokens = sum(p.numel() - 1 for p in prompts)
+        else:
+            self._start_shared(prompts, max_new)
         self.stats.zero_()
         if self.sampling is not None:
             self.offset.zero_()
+
+    def _start_shared(self, prompts: list[torch.Tensor], max_new: int) -> None:
+        """`start` over the page pool: every slot's pages come from the pool, a prompt's longest full-page prefix
+        that an earlier request left in the caches (or that an earlier prompt of this batch writes) is linked into
+        its page-table rows instead of computed, and only the rest is prefilled (the reference's prompt-prefix
+        sharing, ironmule/ggml_engine.py:352-389 with :870-919). Prompts are prefilled in waves: a prompt that
+        would share more pages with an earlier prompt of the batch than the cache offers waits for the wave after
+        that prompt's, so every shared page is written before it is read. A slot's K/V are final, and its pages
+        are indexed, for the committed tokens but the last two (the first draft pass rewrites the K/V of the
+        second-to-last one)."""
+        pool = self.pool
+        ids = [p.tolist() for p in prompts]
+        limit = max_new + self.reserve + 1
+
+        def common(a: list[int], b: list[int]) -> int:
+            n = min(len(a), len(b))
+            i = 0
+            while i < n and a[i] == b[i]:
+                i += 1
+            return i
+
+        waiting = list(range(self.batch))
+        self.prefill_tokens = 0
+        while waiting:
+            wave, later = [], []
+            for b in waiting:
+                room = (len(ids[b]) - pool.lead) // PAGE
+                cached = min(len(pool.longest(ids[b])), room)
+                mine = max((min(common(ids[b], ids[a]), len(ids[a]) - 2) // PAGE for a in wave), default=0)
+                (later if min(mine, room) > cached else wave).append(b)
+            body = []
+            for b in wave:
+                placed = pool.place(ids[b], limit, slot=b)
+                if placed is None:
+                    raise RuntimeError("the page pool cannot hold the batch")
+                _, keep = placed
+                for model in (self.target, self.draft):
+                    row = pool.row(b, model.pages_per_seq)
+                    model.page_table[b].copy_(torch.tensor(row, dtype=torch.int32))
+                body.append((b, prompts[b][keep:-1].to(torch.int32), keep))
+                self.prefill_tokens += len(ids[b]) - 1 - keep
+            self.target.prefill_many(body)
+            self.draft.prefill_many(body)
+            for b in wave:
+                pool.commit(b, ids[b][:-2])
+            waiting = later
+
+    def _retire(self, b: int, keep: bool = True) -> None:
+        """Release slot b's pages to the pool, first indexing those that hold final K/V."""
+        n = int(self.n[b].item())
+        if keep and n > 2:
+            self.pool.commit(b, self.hist[b, :n - 2].tolist())
+        self.pool.release(b, keep=keep)
+
+    def finish(self, keep: bool = True) -> None:
+        """Release every slot's pages to the pool: the K/V of their committed tokens stay cached for later
+        requests (keep) or are dropped. `start` does this itself for slots still held."""
+        if self.pool is None:
+            return
+        for b in range(self.batch):
+            if self.pool.held(b):
+                self._retire(b, keep)
 
     def capture(self) -> None:
         """Record one round as a CUDA graph (after one eager round has loaded every kernel)."""
@@ -696,7 +772,7 @@ class TreeDecoder(SpecDecoder):
     """
 
     def __init__(self, target: QuantModel, draft: QuantModel, *, branch: tuple[int, ...] = (4, 2, 2),
-                 batch: int = 1):
+                 batch: int = 1, prefix_cache: bool = False):
         levels = len(branch)
         counts = [math.prod(branch[:i + 1]) for i in range(levels)]
         nodes = sum(counts)
@@ -707,7 +783,7 @@ class TreeDecoder(SpecDecoder):
             raise ValueError(f"{batch} trees of {rows} rows exceed the target's per-forward limit")
         if batch * max(counts[:-1] + [2]) > min(draft.max_rows, draft.max_logit_rows):
             raise ValueError("a tree level exceeds the draft model's per-forward limit")
-        super().__init__(target, draft, k=levels, batch=batch)
+        super().__init__(target, draft, k=levels, batch=batch, prefix_cache=prefix_cache)
         self.branch, self.counts, self.nodes, self.rows = tuple(branch), counts, nodes, rows
         self.first = [sum(counts[:i]) for i in range(levels)]
         self.reserve = nodes
