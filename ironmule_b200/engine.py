@@ -873,3 +873,183 @@ def greedy_decode(model: QuantModel, prompt: torch.Tensor, max_new: int, seq: in
         out.append(int(idx.item()))
         pos += 1
     return out
+
+
+# ---- the draft-model protocol of the reference's host speculation, on the device ------------------------------
+def decode_plan(wants: list[list[bool]], step: int, budget: int, logit_budget: int
+                ) -> list[tuple[list[tuple[int, int, int]], int]]:
+    """The forwards of one multi-sequence decode call: `wants[i]` says, per row of sequence i (rows in position
+    order), whether it needs logits. Each forward takes at most one chunk of up to `step` rows of each sequence
+    (a sequence's chunks in order), at most `budget` rows in all; the chunks that need logits come first so that the
+    logits cover a leading block of at most `logit_budget` rows. Returns [(chunks [(sequence, offset, count)],
+    logit rows)]."""
+    if step < 1 or budget < step or logit_budget < step:
+        raise ValueError("need 1 <= step <= budget and step <= logit_budget")
+    offs = [0] * len(wants)
+    plan = []
+    while True:
+        ready = []
+        for i, w in enumerate(wants):
+            if offs[i] < len(w):
+                n = min(step, len(w) - offs[i])
+                last = max((j for j in range(n) if w[offs[i] + j]), default=-1)
+                ready.append((i, offs[i], n, last))
+        if not ready:
+            return plan
+        chunks, rows, logit_rows = [], 0, 0
+        for i, off, n, last in [c for c in ready if c[3] >= 0] + [c for c in ready if c[3] < 0]:
+            if rows + n > budget or (last >= 0 and rows + last + 1 > logit_budget):
+                continue
+            if last >= 0:
+                logit_rows = rows + last + 1
+            chunks.append((i, off, n))
+            rows += n
+            offs[i] += n
+        plan.append((chunks, logit_rows))
+
+
+class DeviceDraftEngine:
+    """A draft model on the B200 behind the engine protocol the reference's `Drafter` drives
+    (ironmule/draft_model.py:159-288): `_decode_conf(rows)` takes llama.cpp-style rows (token, position, sequence,
+    wants logits) and returns, per row that wants logits, its top token and that token's probability (the
+    reference's host scan, ironmule/ggml_engine.py:669-683, here `kernels.argmax_rows(with_conf=True)`); `eog`,
+    `L.llama_memory_seq_rm(memory, seq, p0, p1)`, `memory` and `seqs` as the reference's engine has them.
+
+    The cache is indexed by position and a row reads only keys at or below its own position, so removing a
+    sequence's tail is bookkeeping: the next rows overwrite those slots. A removal that would leave a hole below
+    kept positions answers False, as llama.cpp does for removals its cache cannot make (the `Drafter` then
+    clears the sequence). Rows must continue each sequence from its first free position.
+    """
+
+    def __init__(self, model: QuantModel, eog_ids=()):
+        step = min(model.max_rows, MAX_SEQ_ROWS)
+        if model.max_logit_rows < step:
+            raise ValueError(f"the draft model needs max_logit_rows >= {step}")
+        self.model = model
+        self.seqs = model.max_seqs
+        self.memory = None
+        self.filled = [0] * model.max_seqs  # positions of each sequence whose K/V are written
+        self.eog_ids = frozenset(int(t) for t in eog_ids)
+        self.L = _SeqRm(self)
+        self.forwards = 0
+
+    def eog(self, token: int) -> bool:
+        return int(token) in self.eog_ids
+
+    def seq_rm(self, seq: int, p0: int, p1: int) -> bool:
+        if not 0 <= seq < self.seqs:
+            raise ValueError(f"sequence {seq} out of range")
+        start = 0 if p0 < 0 else p0
+        if 0 <= p1 < self.filled[seq] and start < p1:
+            return False
+        self.filled[seq] = min(self.filled[seq], start)
+        return True
+
+    def _decode_conf(self, rows) -> list[tuple[int, float]]:
+        if not rows:
+            return []
+        m = self.model
+        per: dict[int, list[int]] = {}
+        for i, (_, pos, seq, _) in enumerate(rows):
+            if not 0 <= seq < self.seqs:
+                raise ValueError(f"sequence {seq} out of range")
+            per.setdefault(seq, []).append(i)
+        seqs = list(per)
+        for seq in seqs:
+            first = self.filled[seq]
+            for j, i in enumerate(per[seq]):
+                if rows[i][1] != first + j:
+                    raise ValueError(f"sequence {seq}: row at position {rows[i][1]}, expected {first + j}")
+            if first + len(per[seq]) > m.max_ctx:
+                raise ValueError(f"sequence {seq} would exceed the model's {m.max_ctx} positions")
+        plan = decode_plan([[bool(rows[i][3]) for i in per[s]] for s in seqs], min(m.max_rows, MAX_SEQ_ROWS),
+                           min(m.max_rows, MAX_QGEMM_ROWS), m.max_logit_rows)
+        picks, where = [], {}
+        for chunks, logit_rows in plan:
+            order = [per[seqs[g]][off + j] for g, off, n in chunks for j in range(n)]
+            bounds = [0]
+            for _, _, n in chunks:
+                bounds.append(bounds[-1] + n)
+            host = ([int(rows[i][0]) for i in order] + [int(rows[i][1]) for i in order]
+                    + [g for g, (_, _, n) in enumerate(chunks) for _ in range(n)] + bounds
+                    + [seqs[g] for g, _, _ in chunks])
+            dev = torch.tensor(host, dtype=torch.int32).to(m.device)
+            r, c = len(order), len(chunks)
+            meta = RowMeta(tokens=dev[:r], token_stride=1, pos=dev[r:2 * r], seq=dev[2 * r:3 * r],
+                           seq_rows=dev[3 * r:3 * r + c + 1], rows=r, max_rows_per_seq=max(n for _, _, n in chunks),
+                           seq_slot=dev[3 * r + c + 1:])
+            logits = m.forward(meta, max_kv_len=m.max_ctx, logit_rows=logit_rows)
+            self.forwards += 1
+            if logit_rows:
+                idx, conf = kernels.argmax_rows(logits, with_conf=True, ws=m.ws_argmax)
+                for k, i in enumerate(order[:logit_rows]):
+                    if rows[i][3]:
+                        where[i] = (len(picks), k)
+                picks.append((idx, conf))
+            for g, off, n in chunks:
+                self.filled[seqs[g]] += n
+        if not picks:
+            return []
+        idx = torch.cat([p[0] for p in picks]).cpu().tolist()
+        conf = torch.cat([p[1] for p in picks]).cpu().tolist()
+        base = [0]
+        for p in picks:
+            base.append(base[-1] + p[0].numel())
+        out = []
+        for i, row in enumerate(rows):
+            if row[3]:
+                f, k = where[i]
+                out.append((int(idx[base[f] + k]), float(conf[base[f] + k])))
+        return out
+
+
+class _SeqRm:
+    """The `L` namespace of the engine protocol: llama.cpp's `llama_memory_seq_rm(memory, seq, p0, p1)`."""
+
+    def __init__(self, engine: DeviceDraftEngine):
+        self._e = engine
+
+    def llama_memory_seq_rm(self, memory, seq: int, p0: int, p1: int) -> bool:
+        return self._e.seq_rm(seq, p0, p1)
+
+
+def drafter_generate(target: QuantModel, drafter, prompt, max_new: int, *, max_drafts: int = 8, seq: int = 0,
+                     key: int = 0) -> tuple[list[int], dict]:
+    """Greedy speculative decoding of one request with the reference's host loop around a `Drafter`
+    (ironmule_b200.draft_model, over a `DeviceDraftEngine`): each step the drafter offers as many drafts as its
+    confidence-calibrated stop rule gives (0 .. max_drafts), the target verifies the last token and the drafts
+    in one forward at their positions, the leading drafts equal to the target's argmax are kept with the target's
+    own next token (`speculation.accept`), and the drafter learns from the outcome (`settle`, `end_step`) --
+    the per-request step of ironmule/ggml_engine.py:1155-1343 with one running request. Returns the generated
+    tokens (exactly max_new, equal to plain greedy decoding) and counts."""
+    import time
+
+    from .speculation import accept
+
+    prompt = [int(t) for t in prompt]
+    if len(prompt) < 2:
+        raise ValueError("a prompt of at least two tokens")
+    limit = min(target.max_logit_rows, target.max_rows, MAX_SEQ_ROWS) - 1  # the verify forward's rows, minus one
+    max_drafts = max(0, min(max_drafts, limit))
+    if len(prompt) + max_new + max_drafts + 1 > target.max_ctx:
+        raise ValueError("prompt and answer exceed the target's context")
+    dev = target.device
+    target.prefill(torch.tensor(prompt[:-1], dtype=torch.int32, device=dev), seq=seq)
+    context, out = list(prompt), []
+    steps = drafted = accepted = 0
+    while len(out) < max_new:
+        started = time.perf_counter()
+        room = min(max_drafts, max_new - len(out) - 1)
+        drafts = drafter.draft({key: (context, room)}, running=1).get(key, []) if room > 0 else []
+        feed = torch.tensor([context[-1]] + drafts, dtype=torch.int32, device=dev)
+        logits = target.logits_for(feed, len(context) - 1, seq=seq)
+        argmax, _ = kernels.argmax_rows(logits, ws=target.ws_argmax)
+        new = accept(drafts, argmax.cpu().tolist())
+        if drafts:
+            drafter.settle(key, len(drafts), len(new) - 1)
+        drafter.end_step(time.perf_counter() - started, 1, len(drafts), len(new))
+        steps, drafted, accepted = steps + 1, drafted + len(drafts), accepted + len(new) - 1
+        context += new
+        out += new
+    drafter.release(key)
+    return out[:max_new], {"steps": steps, "drafted": drafted, "accepted": accepted}
