@@ -36,6 +36,7 @@ from .kvpool import PAGE, PagePool  # PAGE: KV slots per cache page
 
 MAX_QGEMM_ROWS = 320   # rows of one forward (the packed qGEMM takes them in chunks of 32)
 MAX_SEQ_ROWS = 32      # rows of one sequence in one forward (the fused attention's limit): prefill chunks
+PARK_PAGES = 3         # pages an idle decoder slot writes (positions 0 .. 2 + MAX_SEQ_ROWS)
 
 
 @dataclass(frozen=True)
@@ -551,9 +552,22 @@ class SpecDecoder:
         self.gpu_launches_per_round = 0
         self.pool: PagePool | None = None
         if prefix_cache:
-            # one page pool over both models' caches: a slot's row lists the same physical pages in each
+            # one page pool over both models' caches (a slot's row lists the same physical pages in each), less
+            # PARK_PAGES private pages per slot at the top, where an idle slot's rounds write
             pages = min(target.max_seqs * target.pages_per_seq, draft.max_seqs * draft.pages_per_seq)
-            self.pool = PagePool(pages, batch, min(target.pages_per_seq, draft.pages_per_seq), lead=2)
+            self.park_base = pages - PARK_PAGES * batch
+            if self.park_base < 1:
+                raise ValueError("the caches are too small for a page pool")
+            self.pool = PagePool(self.park_base, batch, min(target.pages_per_seq, draft.pages_per_seq), lead=2)
+        # host view of the slots: running or idle (parked), the committed tokens reported so far, the end
+        self.running = [False] * batch
+        self.upto = [0] * batch
+        self.end = [0] * batch
+        self.reused = [0] * batch
+        self.prefill_tokens = 0
+        self._host_n = self._host_tok = None
+        for b in range(batch):
+            self._park(b)
 
     # ---- one round, issued on the current stream --------------------------------------------------------
     def round(self) -> None:
@@ -613,28 +627,75 @@ class SpecDecoder:
         if len(prompts) != self.batch:
             raise ValueError("one prompt per sequence slot")
         for p in prompts:
-            length = p.numel()
-            if length < 2 or length + max_new + self.reserve + 1 > self.cap:
-                raise ValueError("prompt too short or too long for the cache")
-        self.finish()  # with a page pool: the previous requests' pages go back to it (their K/V kept as a cache)
-        for b, p in enumerate(prompts):
-            length = p.numel()
-            self.hist[b, :length] = p.to(torch.int32)
-            self.n[b] = length
-            self.target_len[b] = length + max_new
-        if self.pool is None:
-            body = [(b, p[:-1].to(torch.int32)) for b, p in enumerate(prompts)]
-            self.target.prefill_many(body)
-            self.draft.prefill_many(body)
-            self.prefill_tokens = sum(p.numel() - 1 for p in prompts)
-        else:
-            self._start_shared(prompts, max_new)
+            self._check_prompt(p.numel(), max_new)
+        self.finish()  # the previous requests end (with a page pool their K/V stay cached)
+        self._admit([(b, p, max_new) for b, p in enumerate(prompts)])
         self.stats.zero_()
         if self.sampling is not None:
             self.offset.zero_()
 
-    def _start_shared(self, prompts: list[torch.Tensor], max_new: int) -> None:
-        """`start` over the page pool: every slot's pages come from the pool, a prompt's longest full-page prefix
+    def request_limit(self) -> int:
+        """The most prompt + answer tokens one request may have: the cache less the slots a round writes ahead."""
+        return self.cap - self.reserve - 1
+
+    def _check_prompt(self, length: int, max_new: int) -> None:
+        if length < 2 or max_new < 1 or length + max_new > self.request_limit():
+            raise ValueError("prompt too short or too long for the cache")
+
+    def start_slots(self, items: list[tuple[int, torch.Tensor, int]]) -> None:
+        """Start requests (slot, int32 prompt tensor on the device, max_new) in idle slots while the other slots
+        keep running: the continuous batching of the reference's step loop (ironmule/ggml_engine.py:1066-1160).
+        Between rounds only; a captured graph stays valid (the slot state lives in the same buffers)."""
+        seen = set()
+        for b, p, max_new in items:
+            if not 0 <= b < self.batch or self.running[b] or b in seen:
+                raise ValueError(f"slot {b} is not an idle slot")
+            seen.add(b)
+            self._check_prompt(p.numel(), max_new)
+        self._admit(items)
+
+    def stop_slot(self, b: int, keep: bool = True) -> None:
+        """End slot b's request between rounds. With a page pool its K/V stay cached (keep) and its pages go back
+        to the pool; the idle slot's rounds then write only its private parking pages."""
+        if not self.running[b]:
+            return
+        if self.pool is not None:
+            self._retire(b, keep)
+        self.running[b] = False
+        self._park(b)
+
+    def _park(self, b: int) -> None:
+        """An idle slot: two committed tokens and nothing to commit, so its rounds write positions 0 .. PARK_PAGES *
+        PAGE - 1 only (at most 2 + 31 tree nodes), which with a page pool map to the slot's own parking pages."""
+        self.hist[b, :2] = 0
+        self.n[b] = 2
+        self.target_len[b] = 2
+        if self.pool is not None:
+            park = [self.park_base + PARK_PAGES * b + i for i in range(PARK_PAGES)]
+            for model in (self.target, self.draft):
+                row = park + [park[-1]] * (model.pages_per_seq - PARK_PAGES)
+                model.page_table[b].copy_(torch.tensor(row, dtype=torch.int32))
+
+    def _admit(self, items: list[tuple[int, torch.Tensor, int]]) -> None:
+        for b, p, max_new in items:
+            length = p.numel()
+            self.hist[b, :length] = p.to(torch.int32)
+            self.n[b] = length
+            self.target_len[b] = length + max_new
+            self.running[b] = True
+            self.upto[b] = length
+            self.end[b] = length + max_new
+            self.reused[b] = 0
+        if self.pool is None:
+            body = [(b, p[:-1].to(torch.int32)) for b, p, _ in items]
+            self.target.prefill_many(body)
+            self.draft.prefill_many(body)
+            self.prefill_tokens = sum(p.numel() - 1 for _, p, _ in items)
+        else:
+            self._start_shared(items)
+
+    def _start_shared(self, items: list[tuple[int, torch.Tensor, int]]) -> None:
+        """Admission over the page pool: every slot's pages come from the pool, a prompt's longest full-page prefix
         that an earlier request left in the caches (or that an earlier prompt of this batch writes) is linked into
         its page-table rows instead of computed, and only the rest is prefilled (the reference's prompt-prefix
         sharing, ironmule/ggml_engine.py:352-389 with :870-919). Prompts are prefilled in waves: a prompt that
@@ -643,8 +704,9 @@ class SpecDecoder:
         are indexed, for the committed tokens but the last two (the first draft pass rewrites the K/V of the
         second-to-last one)."""
         pool = self.pool
-        ids = [p.tolist() for p in prompts]
-        limit = max_new + self.reserve + 1
+        prompts = {b: p for b, p, _ in items}
+        ids = {b: p.tolist() for b, p, _ in items}
+        limits = {b: max_new + self.reserve + 1 for b, _, max_new in items}
 
         def common(a: list[int], b: list[int]) -> int:
             n = min(len(a), len(b))
@@ -653,7 +715,7 @@ class SpecDecoder:
                 i += 1
             return i
 
-        waiting = list(range(self.batch))
+        waiting = [b for b, _, _ in items]
         self.prefill_tokens = 0
         while waiting:
             wave, later = [], []
@@ -664,10 +726,11 @@ class SpecDecoder:
                 (later if min(mine, room) > cached else wave).append(b)
             body = []
             for b in wave:
-                placed = pool.place(ids[b], limit, slot=b)
+                placed = pool.place(ids[b], limits[b], slot=b)
                 if placed is None:
                     raise RuntimeError("the page pool cannot hold the batch")
                 _, keep = placed
+                self.reused[b] = keep
                 for model in (self.target, self.draft):
                     row = pool.row(b, model.pages_per_seq)
                     model.page_table[b].copy_(torch.tensor(row, dtype=torch.int32))
@@ -687,13 +750,31 @@ class SpecDecoder:
         self.pool.release(b, keep=keep)
 
     def finish(self, keep: bool = True) -> None:
-        """Release every slot's pages to the pool: the K/V of their committed tokens stay cached for later
-        requests (keep) or are dropped. `start` does this itself for slots still held."""
-        if self.pool is None:
-            return
+        """End every running slot's request (`stop_slot`): with a page pool the K/V of their committed tokens stay
+        cached for later requests (keep) or are dropped. `start` does this itself."""
         for b in range(self.batch):
-            if self.pool.held(b):
-                self._retire(b, keep)
+            self.stop_slot(b, keep)
+
+    def step(self) -> dict[int, list[int]]:
+        """One round (the captured graph when there is one), then each running slot's newly committed tokens, read
+        back to the host with one synchronisation; a slot's tokens stop at its end (prompt + max_new)."""
+        if self._host_n is None:
+            self._host_n = torch.zeros(self.batch, dtype=torch.int32).pin_memory()
+            self._host_tok = torch.zeros((self.batch, self.k + 1), dtype=torch.int32).pin_memory()
+        self.run_rounds(1)
+        self._host_n.copy_(self.n, non_blocking=True)
+        self._host_tok.copy_(self.out_tokens, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        out = {}
+        for b in range(self.batch):
+            if not self.running[b]:
+                continue
+            n_b = min(int(self._host_n[b]), self.end[b])
+            new = n_b - self.upto[b]
+            if new > 0:
+                out[b] = self._host_tok[b, :new].tolist()
+                self.upto[b] = n_b
+        return out
 
     def capture(self) -> None:
         """Record one round as a CUDA graph (after one eager round has loaded every kernel)."""
@@ -716,30 +797,13 @@ class SpecDecoder:
         called, else eagerly."""
         pinned = [torch.as_tensor(p, dtype=torch.int32).pin_memory() for p in prompts]
         self.start([p.to(self.device, non_blocking=True) for p in pinned], max_new)
-        lens = [p.numel() for p in pinned]
-        done_upto = list(lens)
-        host_n = torch.zeros(self.batch, dtype=torch.int32).pin_memory()
-        host_tok = torch.zeros((self.batch, self.k + 1), dtype=torch.int32).pin_memory()
-        targets = [ln + max_new for ln in lens]
         out: list[list[int]] = [[] for _ in range(self.batch)]
-        stream = torch.cuda.current_stream(self.device)
         while True:
-            self.run_rounds(1)
-            host_n.copy_(self.n, non_blocking=True)
-            host_tok.copy_(self.out_tokens, non_blocking=True)
-            stream.synchronize()
-            finished = True
-            for b in range(self.batch):
-                n_b = min(int(host_n[b]), targets[b])
-                new = n_b - done_upto[b]
-                if new > 0:
-                    toks = host_tok[b, :new].tolist()
-                    out[b].extend(toks)
-                    if on_token is not None:
-                        on_token(b, toks)
-                    done_upto[b] = n_b
-                finished &= n_b >= targets[b]
-            if finished:
+            for b, toks in self.step().items():
+                out[b].extend(toks)
+                if on_token is not None:
+                    on_token(b, toks)
+            if all(self.upto[b] >= self.end[b] for b in range(self.batch)):
                 return out
 
     def done(self) -> bool:
