@@ -11,7 +11,7 @@ the data path), timed with CUDA events over K rounds replayed from one captured 
 streams the full 3.6 GB of weights, far more than the 126 MB L2, so no flush is needed.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload spec_decode|verify_step|stochastic|tree|tp]
+                    [--workload spec_decode|verify_step|stochastic|tree|tp|attention|kquant]
 
 --workload stochastic: BASELINE config 3's round -- Qwen3-4B + 0.6B, temperature 0.7, top-p 0.95, k = 4, rejection
 sampling with residual resampling on Philox -- over 32 concurrent sequences with prompt lengths drawn uniformly
@@ -53,7 +53,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["spec_decode", "verify_step", "stochastic", "tree", "tp", "attention"],
+    ap.add_argument("--workload", choices=["spec_decode", "verify_step", "stochastic", "tree", "tp", "attention",
+                                           "kquant"],
                     default="spec_decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -64,6 +65,7 @@ def parse():
                     help="attention: config 3's verify (32 sequences, Qwen3-4B heads, 5 rows) or draft pass "
                          "(Qwen3-0.6B heads, 1 row), or config 2's draft pass (1 sequence, 520 keys)")
     ap.add_argument("--kpc", type=int, default=64, help="attention: keys per split (a multiple of 64)")
+    ap.add_argument("--layers", type=int, default=0, help="kquant: layers of Q4_K matrices (default 36)")
     ap.add_argument("--qgemm-path", type=int, choices=[0, 1, 2], default=0,
                     help="packed qGEMM kernel: 0 automatic, 1 warp MMA only, 2 tcgen05 tensor cores only (same bits)")
     return ap.parse_args()
@@ -524,6 +526,91 @@ def run_attention(args, world: int, rank: int, local: int) -> None:
         print(json.dumps(line), flush=True)
 
 
+# Qwen3-4B's projections as a GGUF file stores them (q, k, v apart): (N rows, K inputs)
+KQ_SHAPES = ((4096, 2560), (1024, 2560), (1024, 2560), (2560, 4096), (9728, 2560), (9728, 2560), (2560, 9728))
+
+
+def run_kquant(args, world: int, rank: int, local: int) -> None:
+    """The ggml path's matmuls: every Q4_K projection of one Qwen3-4B token step (36 layers x 7, as the reference
+    measures its generated kernels, ironmule/kernel_gen.py:16) at `--rows` tokens (default 1) through im_kq_gemv,
+    captured as one CUDA graph; 2.04 GB of random Q4_K blocks (d, dmin ~ 2e-3), so no L2 flush is needed. Bytes per
+    step: the weights once plus the float32 activations in and outputs out. cpu_baseline: the oracle's C product
+    (one thread) over one layer's seven matrices."""
+    import numpy as np
+    import torch
+
+    from ironmule_b200 import kernels
+    from oracle import kquant as kq
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pk = peaks()
+    b = args.rows or 1
+    layers = args.layers or 36
+    gen = torch.Generator(device=device).manual_seed(0)
+    weights, inputs, outputs = [], {}, []
+    d = torch.tensor([2e-3, 2e-3], dtype=torch.float16).view(torch.uint8).to(device)
+    for _ in range(layers):
+        for n, k in KQ_SHAPES:
+            w = torch.randint(0, 256, (n * (k // 256), 144), generator=gen, device=device, dtype=torch.uint8)
+            w[:, 0:4] = d
+            weights.append((w.reshape(-1), n, k))
+            outputs.append(torch.empty((b, n), dtype=torch.float32, device=device))
+    for n, k in KQ_SHAPES:
+        inputs.setdefault(k, torch.randn((b, k), generator=gen, device=device))
+    ws = kernels.workspace(max(kernels.kq_workspace_bytes(k, b) for _, k in KQ_SHAPES), device)
+    stream = torch.cuda.current_stream(device)
+
+    def step():
+        for (w, n, k), y in zip(weights, outputs):
+            kernels.kq_gemv(kernels.Q4_K, w, inputs[k], n, out=y, ws=ws)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    g.replay()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    sec = e0.elapsed_time(e1) / 1000 / args.steps
+    wbytes = sum(w.numel() for w, _, _ in weights)
+    algo = wbytes + layers * sum(4 * b * (n + k) for n, k in KQ_SHAPES)
+    achieved = algo / sec / 1e9
+    # the CPU port: one layer's seven matrices at b tokens, one thread
+    host = [(w.cpu().numpy(), n, k) for w, n, k in weights[:len(KQ_SHAPES)]]
+    xs = {k: v.cpu().numpy() for k, v in inputs.items()}
+    t0 = time.perf_counter()
+    for w, n, k in host:
+        kq.gemv(kq.Q4_K, w, n, xs[k])
+    cpu_sec = time.perf_counter() - t0
+    cpu_gbs = sum(w.size for w, _, _ in host) / cpu_sec / 1e9
+    line = {"metric": f"Q4_K matmul GB/s (all Q4_K matmuls of a Qwen3-4B token step, {b} token(s))",
+            "value": round(achieved, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": round(sec * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x 4/6-bit integer dot, fp32 scales",
+            "data": "synthetic (random Q4_K blocks, normal activations)",
+            "config": {"workload": f"GGUF Q4_K matmuls of one Qwen3-4B token step ({layers} x 7 projections)",
+                       "tokens": b, "weight_bytes": wbytes, "l2": f"{wbytes / 1e9:.2f} GB of weights per step > "
+                                                                    "126 MB L2"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                         "kernel": f"kq_q4k_kernel + kq_quant_kernel, {len(weights)} pairs per step"},
+            "cpu_baseline": {"value": round(cpu_gbs, 3), "unit": "GB/s", "cores": 1, "kind": "port",
+                             "sample": f"one layer's 7 Q4_K matrices at {b} token(s), oracle/kquant_oracle.c"},
+            "gpu_launches": 2 * len(weights) * args.steps, "clocks": clk, "peak_source": pk["source"]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def run_rounds_workload(args, world: int, rank: int, local: int, kind: str) -> None:
     """Config 3 (stochastic, batched) or config 4 (tree) rounds: timed like the default workload."""
     import torch
@@ -649,6 +736,8 @@ def main() -> int:
             run_verify_step(args, world, rank, local)
         elif args.workload == "attention":
             run_attention(args, world, rank, local)
+        elif args.workload == "kquant":
+            run_kquant(args, world, rank, local)
         elif args.workload in ("stochastic", "tree", "tp"):
             run_rounds_workload(args, world, rank, local, args.workload)
         else:

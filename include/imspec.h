@@ -352,6 +352,29 @@ int im_sample_rows(const uint16_t* logits, int64_t rows, int64_t V, int64_t ld, 
                    int32_t* out, int64_t out_stride, void* workspace, size_t workspace_bytes, void* stream);
 int im_philox4x32_10(uint64_t seed, uint64_t offset, uint32_t stream_id, uint32_t n, uint32_t* out, void* stream);
 
+/* ---- GGUF k-quant matmul (the ggml path) ------------------------------------------------------------------
+ *
+ * y[B][N] = x[B][K] . W^T for W in llama.cpp's GGUF blocks of 256 weights: type 12 = Q4_K (144-byte blocks, W 16-byte
+ * aligned) or 14 = Q6_K (210-byte blocks, W 2-byte aligned), N rows of K/256 blocks each; x and y float32 on the
+ * device; 1 <= B <= 32 tokens, K a multiple of 256. The activations are rounded to 8 bits per 32 values and each
+ * sub-block's dot product is exact in integers, as llama.cpp's own quantized matmuls compute; a token's results do
+ * not depend on B or on the other tokens.
+ *
+ * im_kq_mul_mat replaces the reference's llama.cpp hook ironmule_kg_mul_mat (ironmule/kernel_gen.py:803-862) with the
+ * same arguments and contract: IM_OK (0) when it computed y, non-zero (IM_UNSUPPORTED for a type, K or token count it
+ * does not serve) when llama.cpp's own kernel should run. Its scratch is one static device array per GPU (B x K up to
+ * about 1.5 M), looked up on the first call on a device: overlapping calls race and must not be issued.
+ * im_kq_gemv takes a caller workspace of im_kq_workspace_bytes(K, B) bytes, 256-byte aligned, instead.
+ */
+int im_kq_mul_mat(int type, const void* w, const float* x, float* y, int64_t N, int64_t K, int64_t B, void* stream);
+/* im_kq_mul_mat under the name llama.cpp's patched mul_mat looks up (dlsym) in the library IRONMULE_KG_LIB names
+ * (the reference's native/ggml_patches/kg1/ggml-cuda.cu.diff:6-18), so this library loads there as it is. */
+int ironmule_kg_mul_mat(int type, const void* w, const float* x, float* y, int64_t N, int64_t K, int64_t B,
+                        void* stream);
+int im_kq_gemv(int type, const void* w, const float* x, float* y, int64_t N, int64_t K, int64_t B, void* workspace,
+               size_t workspace_bytes, void* stream);
+size_t im_kq_workspace_bytes(int64_t K, int64_t B);
+
 #ifdef __cplusplus
 }
 #endif

@@ -52,6 +52,10 @@ SIGNATURES: dict[str, tuple] = {
                                _P, _SZ, _P]),
     "im_argmax_rows": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _P, _P, _SZ, _P]),
     "im_argmax_workspace_bytes": (_SZ, [_I64, _I64]),
+    "im_kq_mul_mat": (_INT, [ctypes.c_int, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "im_kq_gemv": (_INT, [ctypes.c_int, _P, _P, _P, _I64, _I64, _I64, _P, _SZ, _P]),
+    "ironmule_kg_mul_mat": (_INT, [ctypes.c_int, _P, _P, _P, _I64, _I64, _I64, _P]),
+    "im_kq_workspace_bytes": (_SZ, [_I64, _I64]),
     "im_verify_greedy": (_INT, [_P, _I64, _I64, _I64, _I64, _P, _I64, _P, _P, _P, _P, _SZ, _P]),
     "im_quantize_w4g64": (_INT, [_P, _I64, _I64, _P, _P, _P, _P]),
     "im_rmsnorm": (_INT, [_P, _I64, _P, _P, _I64, _I64, ctypes.c_float, _INT, _P]),

@@ -485,3 +485,49 @@ def qgemm_packed(x: torch.Tensor, p: Packed, *, epilogue: str = "store", residua
               epi, _ptr_or_none(norm_sq), norm_parts, _ptr_or_none(norm_weight), float(eps), int(gemma_norm),
               _ptr_or_none(out_sq), sq_ld, ws_ptr, ws_bytes, _stream(device))
     return out
+
+
+# ---- GGUF k-quants (the ggml path) ----------------------------------------------------------------------------
+Q4_K, Q6_K = 12, 14
+KQ_BLOCK_BYTES = {Q4_K: 144, Q6_K: 210}
+
+
+def kq_workspace_bytes(k: int, b: int) -> int:
+    return int(_lib.load().im_kq_workspace_bytes(k, b))
+
+
+def _kq_args(kind: int, w: torch.Tensor, x: torch.Tensor, n: int, out: torch.Tensor | None):
+    if kind not in KQ_BLOCK_BYTES:
+        raise ValueError(f"weight type {kind}: 12 (Q4_K) or 14 (Q6_K)")
+    _check(w, "w", (torch.uint8,))
+    _check(x, "x", (torch.float32,), w.device)
+    if x.dim() != 2:
+        raise ValueError("x must be [B, K]")
+    b, k = x.shape
+    if k % 256 or w.numel() != n * (k // 256) * KQ_BLOCK_BYTES[kind]:
+        raise ValueError(f"w holds {w.numel()} bytes, expected {n} rows of {k // 256} blocks")
+    y = torch.empty((b, n), dtype=torch.float32, device=w.device) if out is None else out
+    _check(y, "out", (torch.float32,), w.device)
+    if tuple(y.shape) != (b, n):
+        raise ValueError(f"out must be [{b}, {n}]")
+    return b, k, y
+
+
+def kq_gemv(kind: int, w: torch.Tensor, x: torch.Tensor, n: int, *, out: torch.Tensor | None = None,
+            ws: torch.Tensor | None = None) -> torch.Tensor:
+    """y [B, N] float32 = x [B, K] float32 . W^T, W = N rows of GGUF Q4_K / Q6_K blocks as raw bytes (uint8)."""
+    b, k, y = _kq_args(kind, w, x, n, out)
+    ws_ptr, ws_bytes = _scratch(ws, w.device, kq_workspace_bytes(k, b), "kq")
+    _lib.call("im_kq_gemv", kind, w.data_ptr(), x.data_ptr(), y.data_ptr(), n, k, b, ws_ptr, ws_bytes,
+              _stream(w.device))
+    return y
+
+
+def kq_mul_mat(kind: int, w: torch.Tensor, x: torch.Tensor, n: int, *,
+               out: torch.Tensor | None = None) -> tuple[int, torch.Tensor]:
+    """The llama.cpp hook's call (`ironmule_kg_mul_mat`): (0, y) when y was computed, else (the library's refusal
+    code, y unwritten) and the caller runs its own kernel."""
+    b, k, y = _kq_args(kind, w, x, n, out)
+    rc = int(_lib.load().im_kq_mul_mat(kind, w.data_ptr(), x.data_ptr(), y.data_ptr(), n, k, b,
+                                       _stream(w.device)))
+    return rc, y

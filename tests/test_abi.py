@@ -15,13 +15,13 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "imspec.h"
 
 def declared() -> list[str]:
     text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
-    return sorted(set(re.findall(r"\b(im_[a-z0-9_]+)\s*\(", text)))
+    return sorted(set(re.findall(r"\b((?:im|ironmule_kg)_[a-z0-9_]+)\s*\(", text)))
 
 
 def test_every_declared_symbol_is_exported_and_typed():
     lib = _lib.load()
     names = declared()
-    assert len(names) >= 9
+    assert len(names) >= 9 and "ironmule_kg_mul_mat" in names
     for name in names:
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
@@ -85,3 +85,13 @@ def test_errors_raise_typed_exceptions():
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(_lib.KernelLibraryMissing):
         _lib.load(tmp_path / "libimspec.so")
+
+
+def test_kquant_rejects_bad_arguments_without_launching():
+    rc, msg = _status("im_kq_mul_mat", 2, None, None, None, 1, 256, 1, None)
+    assert rc == _lib.IM_UNSUPPORTED and "type" in msg
+    rc, msg = _status("ironmule_kg_mul_mat", 12, None, None, None, 1, 300, 1, None)
+    assert rc == _lib.IM_UNSUPPORTED
+    rc, msg = _status("im_kq_gemv", 12, None, None, None, 1, 256, 1, None, 0, None)
+    assert rc == _lib.IM_INVALID and "null" in msg
+    assert _lib.load().im_kq_workspace_bytes(2560, 4) >= 4 * 2560 + 2 * 4 * 80 * 4
