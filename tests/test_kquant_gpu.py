@@ -83,3 +83,17 @@ def test_gguf_matrix_on_the_device(cuda):
         y = lin(torch.from_numpy(x).cuda()).cpu().numpy()
         want = kq.gemv(lin.kind, np.asarray(f.raw(name)), lin.n, x)
         assert np.array_equal(y.view(np.uint32), want.view(np.uint32)), name
+
+
+@pytest.mark.parametrize("kind", [kq.Q4_K, kq.Q6_K])
+def test_unaligned_activations(cuda, kind):
+    """Activations only 4-byte aligned (a view one float into a buffer) give the same bits."""
+    n, k, b = 96, 1024, 3
+    w = kq.random_blocks(kind, n * k // 256, seed=31)
+    x = np.random.default_rng(32).normal(0, 1, (b, k)).astype(np.float32)
+    buf = torch.zeros(b * k + 1, dtype=torch.float32, device="cuda")
+    xd = buf[1:].view(b, k)
+    xd.copy_(torch.from_numpy(x))
+    assert xd.data_ptr() % 16 == 4
+    y = kernels.kq_gemv(kind, torch.from_numpy(w.reshape(-1)).cuda(), xd, n).cpu().numpy()
+    assert np.array_equal(y.view(np.uint32), kq.gemv(kind, w, n, x).view(np.uint32))
