@@ -293,6 +293,121 @@ __global__ void __launch_bounds__(KQ_WARPS * 32) kq_q6k_kernel(const unsigned ch
   }
 }
 
+// Q4_K for 3-32 tokens on int8 tensor-core MMA (mma.sync m16n8k32 s8 x s8 -> s32): a CTA of 4 warps takes 16 rows
+// and one 8-token tile (grid.y); warp j takes the blocks ib = j mod 4 of all 16 rows. For sub-block sb of a block, one MMA gives sum(q * xq) exactly
+// for the 16 rows x 8 tokens: lane (g = lane / 4, t = lane % 4) holds A = quant bytes 32c + 4t .. + 3 and 32c + 16 +
+// 4t .. + 3 (nibble sb & 1, c = sb / 2) of rows g and g + 8, B = the 8-bit activations of the tile's token g at the
+// same k, and C = rows g, g + 8 x the tile's tokens 2t, 2t + 1. Each (row, token) keeps one accumulator per chunk c, updated in the dp4a
+// kernel's order (blocks ib = j mod 4 in order, sub-block 2c then 2c + 1) and summed in its tree: ((c0 + c1) +
+// (c2 + c3)) within the warp, then ((T0 + T1) + (T2 + T3)) over the four warps. So the bits equal the dp4a kernel's.
+__device__ __forceinline__ void kq_mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+struct KqMmaRow {
+  uint32_t q[8];  // per chunk c: quant word 32c + 4t (q[2c]) and 32c + 16 + 4t (q[2c + 1])
+  uint4 h;        // d, dmin, packed scales
+};
+__device__ __forceinline__ void kq_mma_load(KqMmaRow& r, const unsigned char* bp, int t) {
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    r.q[2 * c] = __ldg(reinterpret_cast<const uint32_t*>(bp + 16 + 32 * c + 4 * t));
+    r.q[2 * c + 1] = __ldg(reinterpret_cast<const uint32_t*>(bp + 16 + 32 * c + 16 + 4 * t));
+  }
+  r.h = __ldg(reinterpret_cast<const uint4*>(bp));
+}
+
+constexpr int KQ_MMA_MIN_TOKENS = 3;  // 1-2 tokens stay on dp4a (faster there)
+
+__global__ void __launch_bounds__(128) kq_q4k_mma_kernel(const unsigned char* __restrict__ w,
+                                                         const int8_t* __restrict__ xq, const float* __restrict__ dx,
+                                                         const int* __restrict__ xs, float* __restrict__ y, int N,
+                                                         int K, int B) {
+  __shared__ float part[4][32][4];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int row0 = blockIdx.x * 16, tb = blockIdx.y * 8;  // rows, and this CTA's 8-token tile
+  const int nb = K >> 8, S = K >> 5;
+  const int ra = row0 + g, rb = row0 + g + 8;
+  const bool va = ra < N, vb = rb < N;
+  const unsigned char* pa = w + (size_t)(va ? ra : 0) * nb * 144;
+  const unsigned char* pb = w + (size_t)(vb ? rb : 0) * nb * 144;
+  if (warp == 0 && t == 0) {  // the 16 rows into L2 (each lane its two rows)
+    if (va) kq_prefetch_row(pa, (size_t)nb * 144);
+    if (vb) kq_prefetch_row(pb, (size_t)nb * 144);
+  }
+  KqMmaRow na, nbr;
+  if (warp < nb) {
+    kq_mma_load(na, pa + (size_t)warp * 144, t);
+    kq_mma_load(nbr, pb + (size_t)warp * 144, t);
+  }
+  pdl_wait();
+  pdl_trigger();
+  const int t0 = tb + 2 * t, t1 = tb + 2 * t + 1, tg = tb + g;  // this lane's tokens in C, and in B
+  float acc[4][4];
+#pragma unroll
+  for (int c = 0; c < 4; c++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) acc[c][e] = 0.0f;
+#pragma unroll 1
+  for (int ib = warp; ib < nb; ib += 4) {
+    const KqMmaRow qa = na, qb = nbr;
+    if (ib + 4 < nb) {
+      kq_mma_load(na, pa + (size_t)(ib + 4) * 144, t);
+      kq_mma_load(nbr, pb + (size_t)(ib + 4) * 144, t);
+    }
+    const float da = kq_half(qa.h.x & 0xFFFFu), dma = kq_half(qa.h.x >> 16);
+    const float db = kq_half(qb.h.x & 0xFFFFu), dmb = kq_half(qb.h.x >> 16);
+    const int8_t* xr = xq + (size_t)(tg < B ? tg : 0) * K + ib * 256 + 4 * t;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      int sca0, ma0, sca1, ma1, scb0, mb0, scb1, mb1;
+      kq_scale_min(qa.h.y, qa.h.z, qa.h.w, 2 * c, sca0, ma0);
+      kq_scale_min(qa.h.y, qa.h.z, qa.h.w, 2 * c + 1, sca1, ma1);
+      kq_scale_min(qb.h.y, qb.h.z, qb.h.w, 2 * c, scb0, mb0);
+      kq_scale_min(qb.h.y, qb.h.z, qb.h.w, 2 * c + 1, scb1, mb1);
+#pragma unroll
+      for (int n = 0; n < 2; n++) {
+        const int sb = 2 * c + n;
+        const uint32_t a0 = (qa.q[2 * c] >> (4 * n)) & 0x0F0F0F0Fu, a2 = (qa.q[2 * c + 1] >> (4 * n)) & 0x0F0F0F0Fu;
+        const uint32_t a1 = (qb.q[2 * c] >> (4 * n)) & 0x0F0F0F0Fu, a3 = (qb.q[2 * c + 1] >> (4 * n)) & 0x0F0F0F0Fu;
+        const uint32_t b0 = tg < B ? __ldg(reinterpret_cast<const uint32_t*>(xr + 32 * sb)) : 0u;
+        const uint32_t b1 = tg < B ? __ldg(reinterpret_cast<const uint32_t*>(xr + 32 * sb + 16)) : 0u;
+        int cc[4] = {0, 0, 0, 0};
+        kq_mma_s8(cc, a0, a1, a2, a3, b0, b1);
+        const float dsa = __fmul_rn(da, (float)(n ? sca1 : sca0)), dsma = __fmul_rn(dma, (float)(n ? ma1 : ma0));
+        const float dsb = __fmul_rn(db, (float)(n ? scb1 : scb0)), dsmb = __fmul_rn(dmb, (float)(n ? mb1 : mb0));
+        if (t0 < B) {
+          const size_t xo = (size_t)t0 * S + ib * 8 + sb;
+          const float xsv = (float)__ldg(xs + xo), dxv = __ldg(dx + xo);
+          acc[c][0] = __fmaf_rn(__fmaf_rn(dsa, (float)cc[0], -__fmul_rn(dsma, xsv)), dxv, acc[c][0]);
+          acc[c][2] = __fmaf_rn(__fmaf_rn(dsb, (float)cc[2], -__fmul_rn(dsmb, xsv)), dxv, acc[c][2]);
+        }
+        if (t1 < B) {
+          const size_t xo = (size_t)t1 * S + ib * 8 + sb;
+          const float xsv = (float)__ldg(xs + xo), dxv = __ldg(dx + xo);
+          acc[c][1] = __fmaf_rn(__fmaf_rn(dsa, (float)cc[1], -__fmul_rn(dsma, xsv)), dxv, acc[c][1]);
+          acc[c][3] = __fmaf_rn(__fmaf_rn(dsb, (float)cc[3], -__fmul_rn(dsmb, xsv)), dxv, acc[c][3]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 4; e++) part[warp][lane][e] = (acc[0][e] + acc[1][e]) + (acc[2][e] + acc[3][e]);
+  __syncthreads();
+  if (warp == 0) {
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float v = (part[0][lane][e] + part[1][lane][e]) + (part[2][lane][e] + part[3][lane][e]);
+      const int row = e < 2 ? ra : rb, tok = (e & 1) ? t1 : t0;
+      if ((e < 2 ? va : vb) && tok < B) y[(size_t)tok * N + row] = v;
+    }
+  }
+}
+
 template <int BT>
 static int kq_launch_bt(int type, const void* w, const int8_t* xq, const float* dx, const int* xs, float* y, int N,
                         int K, int B, cudaStream_t st) {
@@ -330,6 +445,10 @@ static int kq_run(const char* who, int type, const void* w, const float* x, floa
                   xs, blocks);
   if (rc) return rc;
   const int n = (int)N, k = (int)K, b = (int)B;
+  if (type == KQ_Q4K && B >= KQ_MMA_MIN_TOKENS)
+    return launch("kq_q4k_mma_kernel", kq_q4k_mma_kernel, dim3((unsigned)((N + 15) / 16), (unsigned)((B + 7) / 8)),
+                  dim3(128), 0, st,
+                  static_cast<const unsigned char*>(w), xq, dx, xs, y, n, k, b);
   if (B <= 1) return kq_launch_bt<1>(type, w, xq, dx, xs, y, n, k, b, st);
   if (B <= 2) return kq_launch_bt<2>(type, w, xq, dx, xs, y, n, k, b, st);
   if (B <= 4) return kq_launch_bt<4>(type, w, xq, dx, xs, y, n, k, b, st);

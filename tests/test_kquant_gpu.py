@@ -1,7 +1,7 @@
 """The GGUF k-quant matmul on the B200 (im_kq_gemv / im_kq_mul_mat) against the CPU oracle's restatement of its
-arithmetic (oracle/kquant_oracle.c): bit for bit for Q4_K and Q6_K at 1-32 tokens, ragged row counts and K from one
-block up; a token's results alone equal its results in a batch; the relative L2 error against float64 within the
-reference's bound (1.25 x 6e-3, ironmule/kernel_gen.py:615, 1001, 1023); the hook's refusals for what it does not
+arithmetic (oracle/kquant_oracle.c): bit for bit for Q4_K and Q6_K at 1-32 tokens (Q4_K from 3 tokens runs on int8
+tensor-core MMA, the rest on dp4a: the same bits), ragged row counts and K from one block up; a token's results
+alone equal its results in a batch; the relative L2 error against float64 within the reference's bound (1.25 x 6e-3, ironmule/kernel_gen.py:615, 1001, 1023); the hook's refusals for what it does not
 serve (ironmule/kernel_gen.py:803-806); a Q4_K matrix read from a GGUF file."""
 from __future__ import annotations
 
@@ -33,7 +33,8 @@ def run(kind, n, k, b, seed, hook=False):
 
 @pytest.mark.parametrize("kind", [kq.Q4_K, kq.Q6_K])
 @pytest.mark.parametrize("n,k,b", [(1, 256, 1), (7, 512, 2), (264, 2048, 3), (100, 1280, 5), (64, 768, 8),
-                                   (33, 2560, 13), (300, 1024, 16), (17, 4096, 32)])
+                                   (33, 2560, 13), (300, 1024, 16), (17, 4096, 32), (7, 256, 6), (1, 1792, 4),
+                                   (529, 2560, 5)])
 def test_bit_exact_against_the_oracle(cuda, kind, n, k, b):
     w, x, y = run(kind, n, k, b, seed=n + k + b)
     want = kq.gemv(kind, w, n, x)
