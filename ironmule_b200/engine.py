@@ -635,8 +635,13 @@ class SpecDecoder:
             self.offset.zero_()
 
     def request_limit(self) -> int:
-        """The most prompt + answer tokens one request may have: the cache less the slots a round writes ahead."""
-        return self.cap - self.reserve - 1
+        """The most prompt + answer tokens one request may have: the cache less the slots a round writes ahead. With
+        a page pool a request also takes at most the pool's pages / slots, so every slot's request fits at once
+        (sharing only lowers a request's need, and cached pages are evicted on demand)."""
+        limit = self.cap - self.reserve - 1
+        if self.pool is not None:
+            limit = min(limit, self.pool.pages // self.batch * PAGE - self.reserve - 1)
+        return limit
 
     def _check_prompt(self, length: int, max_new: int) -> None:
         if length < 2 or max_new < 1 or length + max_new > self.request_limit():
