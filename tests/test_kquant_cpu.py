@@ -92,3 +92,81 @@ def test_reader_refusals(tmp_path):
     v9.write_bytes(data[:4] + struct.pack("<I", 9) + data[8:])
     with pytest.raises(gguf.GGUFError, match="version"):
         gguf.GGUFFile(v9)
+
+
+def _gguf_bytes(version, kvs, tensors, alignment=None):
+    """A GGUF file from the format: kvs [(key, type, value)], tensors [(name, dims innermost first, type, bytes)]."""
+    def s(text):
+        b = text.encode()
+        return struct.pack("<Q", len(b)) + b
+
+    def value(t, v):
+        scalar = {0: "<B", 1: "<b", 2: "<H", 3: "<h", 4: "<I", 5: "<i", 6: "<f", 7: "<?", 10: "<Q", 11: "<q",
+                  12: "<d"}
+        if t in scalar:
+            return struct.pack(scalar[t], v)
+        if t == 8:
+            return s(v)
+        et, items = v
+        return struct.pack("<IQ", et, len(items)) + b"".join(value(et, i) for i in items)
+
+    if alignment is not None:
+        kvs = kvs + [("general.alignment", 4, alignment)]
+    out = b"GGUF" + struct.pack("<IQQ", version, len(tensors), len(kvs))
+    for key, t, v in kvs:
+        out += s(key) + struct.pack("<I", t) + value(t, v)
+    align = alignment or 32
+    offsets, off = [], 0
+    for _, _, _, data in tensors:
+        offsets.append(off)
+        off += -(-len(data) // align) * align
+    for (name, dims, t, _), o in zip(tensors, offsets):
+        out += s(name) + struct.pack("<I", len(dims)) + b"".join(struct.pack("<Q", d) for d in dims)
+        out += struct.pack("<IQ", t, o)
+    out += bytes(-len(out) % align)
+    for (_, _, _, data), o in zip(tensors, offsets):
+        out += data + bytes(-(len(data)) % align)
+    return out
+
+
+def test_reader_alignment_v2_arrays_and_bf16(tmp_path):
+    bf = (np.array([1.5, -2.0, 0.25], dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16).tobytes()
+    q4 = kq.random_blocks(kq.Q4_K, 2, seed=3).tobytes()
+    path = tmp_path / "edge.gguf"
+    path.write_bytes(_gguf_bytes(
+        2, [("a.bools", 9, (7, [True, False, True])), ("a.nested", 9, (9, [(4, [1, 2]), (4, [3])])),
+            ("a.f64", 12, 0.125), ("a.i8", 1, -5), ("a.strs", 9, (8, ["x", "yz"]))],
+        [("w", (256, 2), gguf.Q4_K, q4), ("b", (3,), gguf.BF16, bf)], alignment=64))
+    f = gguf.GGUFFile(path)
+    assert f.version == 2 and f.alignment == 64
+    assert f.metadata["a.bools"] == [True, False, True] and f.metadata["a.nested"] == [[1, 2], [3]]
+    assert f.metadata["a.f64"] == 0.125 and f.metadata["a.i8"] == -5 and f.metadata["a.strs"] == ["x", "yz"]
+    assert f.tensors["w"].offset % 64 == 0 and f.tensors["b"].offset % 64 == 0
+    assert f.raw("w").tobytes() == q4
+    assert f.array("b").tolist() == [1.5, -2.0, 0.25]
+
+
+def test_reader_refuses_malformed_tables(tmp_path):
+    bad_type = tmp_path / "t.gguf"
+    bad_type.write_bytes(_gguf_bytes(3, [], [("w", (256,), 99, bytes(8))]))
+    with pytest.raises(gguf.GGUFError, match="type 99"):
+        gguf.GGUFFile(bad_type)
+    ragged = tmp_path / "r.gguf"
+    ragged.write_bytes(_gguf_bytes(3, [], [("w", (100, 2), gguf.Q4_K, bytes(288))]))
+    with pytest.raises(gguf.GGUFError, match="whole number of blocks"):
+        gguf.GGUFFile(ragged)
+    odd = tmp_path / "a.gguf"
+    odd.write_bytes(_gguf_bytes(3, [("general.alignment", 4, 48)], []))
+    with pytest.raises(gguf.GGUFError, match="power of two"):
+        gguf.GGUFFile(odd)
+    badv = tmp_path / "v.gguf"
+    badv.write_bytes(b"GGUF" + struct.pack("<IQQ", 3, 0, 1) + struct.pack("<Q", 1) + b"k" + struct.pack("<I", 42))
+    with pytest.raises(gguf.GGUFError, match="value type 42"):
+        gguf.GGUFFile(badv)
+
+
+def test_kquant_linear_refuses_bad_shapes():
+    with pytest.raises(gguf.GGUFError):
+        gguf.KQuantLinear(gguf.F32, b"", 1, 256, device="cpu")
+    with pytest.raises(gguf.GGUFError):
+        gguf.KQuantLinear(gguf.Q4_K, bytes(100), 1, 256, device="cpu")
