@@ -5,9 +5,10 @@ prefix that any running or finished sequence holds, computing only the rest; fin
 and are evicted least recently used first when a request needs room (`SharedPool`,
 ironmule/ggml_engine.py:280-432, its prefix trie at :218-278). Here the unit is a page of 16 KV slots, the
 granularity the attention kernels read through the page table: a request shares the FULL pages of its longest
-cached prefix (a page is indexed by the whole token chain up to its end, and a position's K/V depends only on the
-tokens up to it, so an equal chain means equal K/V bits), links them into its page-table row, and computes only
-the tokens after them. Shared pages are never written again: every shared slot lies below the request's first
+cached prefix, links them into its page-table row, and computes only the tokens after them. A position's K/V depend
+only on the tokens up to it, so pages are indexed as a trie of pages: an indexed page has a node id (never reused)
+and is found under (its parent page's node id, its own 16 tokens), so a lookup or a commit costs O(tokens) and equal
+paths mean equal K/V bits. A child indexed under an evicted parent is unreachable, never mistaken for another chain. Shared pages are never written again: every shared slot lies below the request's first
 written position (`lead` below). Pages are reference-counted; pages that no running sequence holds stay indexed as
 a cache until evicted, deepest page of a chain first.
 
@@ -42,8 +43,10 @@ class PagePool:
         self.pages, self.slots, self.row_pages, self.lead = pages, slots, row_pages, lead
         self.free: list[int] = list(range(pages - 1, -1, -1))  # popped from the end: page 0 first
         self.ref: dict[int, int] = {}  # page -> running sequences that hold it (absent: free or cached)
-        self.index: dict[tuple[int, ...], int] = {}  # token chain through a full page -> that page
-        self.key_of: dict[int, tuple[int, ...]] = {}  # page -> its index key
+        self.index: dict[tuple[int, tuple[int, ...]], int] = {}  # (parent node, the page's tokens) -> page
+        self.key_of: dict[int, tuple[int, tuple[int, ...]]] = {}  # indexed page -> its key
+        self.node_of: dict[int, int] = {}  # indexed page -> its node id (0 is the root)
+        self._next_node = 1
         self.cached: OrderedDict[int, None] = OrderedDict()  # indexed pages nobody holds, evicted first to last
         self.seqs: dict[int, _Seq] = {}
         self.shared_tokens = 0
@@ -52,19 +55,34 @@ class PagePool:
     def longest(self, ids) -> list[int]:
         """The indexed pages that hold the longest full-page prefix of `ids`, in position order."""
         ids = list(ids)
-        out = []
-        for end in range(PAGE, len(ids) + 1, PAGE):
-            page = self.index.get(tuple(ids[:end]))
+        out, parent = [], 0
+        for j in range(len(ids) // PAGE):
+            page = self.index.get((parent, tuple(ids[j * PAGE:(j + 1) * PAGE])))
             if page is None:
                 break
             out.append(page)
+            parent = self.node_of[page]
         return out
+
+    def _unindex(self, page: int) -> None:
+        del self.index[self.key_of.pop(page)]
+        del self.node_of[page]
+
+    def _index(self, key, page: int) -> None:
+        old = self.key_of.get(page)
+        if old is None:
+            self.node_of[page] = self._next_node
+            self._next_node += 1
+        else:  # re-keyed under a live parent (its old parent was evicted); its node id, and so its children, stay
+            del self.index[old]
+        self.index[key] = page
+        self.key_of[page] = key
 
     def _take(self) -> int:
         if self.free:
             return self.free.pop()
         page, _ = self.cached.popitem(last=False)  # the least recently released, deepest first
-        del self.index[self.key_of.pop(page)]
+        self._unindex(page)
         return page
 
     def place(self, ids, limit: int, slot: int | None = None) -> tuple[int, int] | None:
@@ -132,13 +150,15 @@ class PagePool:
         if len(tokens) < fixed or tokens[:fixed] != seq.tokens[:fixed]:
             raise ValueError("the tokens contradict the slot's indexed pages")
         seq.tokens = tokens
-        for j in range(seq.indexed, len(tokens) // PAGE):
-            key = tuple(tokens[:(j + 1) * PAGE])
-            page = seq.pages[j]
-            if key not in self.index:
-                self.index[key] = page
-                self.key_of[page] = key
-            seq.indexed = j + 1
+        parent = 0
+        for j in range(len(tokens) // PAGE):  # walk the trie; index this slot's page where the chain has none
+            key = (parent, tuple(tokens[j * PAGE:(j + 1) * PAGE]))
+            page = self.index.get(key)
+            if page is None:
+                page = seq.pages[j]
+                self._index(key, page)
+            parent = self.node_of[page]
+        seq.indexed = len(tokens) // PAGE
 
     def release(self, slot: int, keep: bool = True) -> None:
         """The request in `slot` ends: its indexed pages stay cached (keep) or are dropped from the index, and the
@@ -154,7 +174,7 @@ class PagePool:
                 self.cached[page] = None
             else:
                 if page in self.key_of:
-                    del self.index[self.key_of.pop(page)]
+                    self._unindex(page)
                 self.free.append(page)
 
     def held(self, slot: int) -> bool:

@@ -146,6 +146,8 @@ def _check_accounting(pool):
     assert held | cached | free == set(range(pool.pages))
     assert len(pool.free) == len(free)
     assert set(pool.key_of) == set(pool.index.values()) and cached <= set(pool.key_of)
+    assert set(pool.node_of) == set(pool.key_of) and all(pool.index[k] == p for p, k in pool.key_of.items())
+    assert len(set(pool.node_of.values())) == len(pool.node_of)
     counts = {}
     for seq in pool.seqs.values():
         for p in seq.pages:
@@ -204,3 +206,35 @@ def test_randomized_page_contents(seed):
             del running[slot]
         _check_accounting(pool)
     assert pool.shared_tokens > 0
+
+
+def test_a_child_under_a_dropped_parent_is_never_matched():
+    pool = PagePool(pages=8, slots=2, row_pages=4)
+    x, y, w = toks(16, 100), toks(16, 200), toks(16, 300)
+    pool.place(x + y + [1], 0, slot=0)
+    pool.commit(0, x + y)
+    a0, a1 = pool.row(0)[:2]
+    _, keep = pool.place(x + [5, 6], 0, slot=1)
+    assert keep == 16 and pool.row(1)[0] == a0
+    pool.release(0)  # a1 cached; a0 still held by slot 1
+    pool.release(1, keep=False)  # a0 unindexed and freed; a1 stays cached under a0's old node
+    assert a1 in pool.cached and a0 in pool.free
+    pool.place(w + y + [2], 0, slot=0)  # reuses a0's id for another chain
+    pool.commit(0, w + y)
+    assert pool.row(0)[0] == a0 and pool.longest(w + y) == pool.row(0)[:2]
+    assert pool.row(0)[1] != a1 or a1 not in pool.cached
+
+
+def test_a_chain_whose_canonical_page_was_dropped_is_reindexed():
+    pool = PagePool(pages=12, slots=2, row_pages=4)
+    x, y = toks(16, 10), toks(16, 40)
+    pool.place(x + [0], 0, slot=0)
+    pool.place(x + y + [0], 0, slot=1)  # computed apart: nothing was indexed yet
+    pool.commit(0, x)
+    pool.commit(1, x + y)  # x is slot 0's page; slot 1's second page goes under it
+    b0, b1 = pool.row(1)[:2]
+    assert pool.longest(x + y) == [pool.row(0)[0], b1]
+    pool.release(0, keep=False)  # the canonical x page goes
+    assert pool.longest(x + y) == []
+    pool.commit(1, x + y + toks(3))
+    assert pool.longest(x + y) == [b0, b1]
