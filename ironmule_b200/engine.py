@@ -996,6 +996,8 @@ class DeviceDraftEngine:
             raise ValueError(f"the draft model needs max_logit_rows >= {step}")
         self.model = model
         self.seqs = model.max_seqs
+        self.seq_ctx = model.max_ctx  # positions per sequence (the reference engine's name)
+        self.max_rows = min(model.max_rows, model.max_logit_rows, MAX_QGEMM_ROWS)  # rows of one forward with logits
         self.memory = None
         self.filled = [0] * model.max_seqs  # positions of each sequence whose K/V are written
         self.eog_ids = frozenset(int(t) for t in eog_ids)
