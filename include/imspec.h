@@ -89,8 +89,8 @@ int im_qgemm_w4g64_ex(const uint32_t* w, const uint16_t* scales, const uint16_t*
  * im_qgemm_w4g64_ex given a workspace (so the results are bit-identical), keeping the scratch in one static
  * device array of im_qgemm_noalloc_capacity() bytes that every GPU loading the library holds until exit.
  * Shapes whose scratch would exceed it return IM_UNSUPPORTED. The first call on a device looks the array up and
- * zeroes its counters synchronously, so make it before any stream capture. Calls share the array: calls that
- * overlap on the GPU race and must not be issued.
+ * queues the zeroing of its counters on the caller's stream, ahead of its kernel; make it before any stream
+ * capture. Calls share the array: calls that overlap on the GPU race and must not be issued.
  */
 int im_qgemm_w4g64_noalloc(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const uint16_t* x,
                            uint16_t* y, int64_t M, int64_t N, int64_t K, void* stream);

@@ -543,10 +543,11 @@ extern "C" int im_qgemm_w4g64(const uint32_t* w, const uint16_t* scales, const u
 //
 // The array is allocated when the library is loaded, on every GPU that loads it, and held until the process
 // exits. Its address is looked up once per device with cudaGetSymbolAddress (the host-side name of a __device__
-// array is not a device address). The first call on a device does that set-up and zeroes the counters with a
-// synchronous cudaMemset, so it must come before any stream capture on that device. Calls never allocate.
-// Every call shares the one array: the kernel returns its counters to zero, but calls that overlap on the GPU
-// (two streams, or two host threads) race on it and must not be issued.
+// array is not a device address). The first call on a device does that set-up and queues a cudaMemsetAsync of
+// the counters on the caller's stream, ahead of its kernel, so the zeroing is ordered before the kernel whatever
+// kind of stream the caller uses; make that first call before any stream capture on the device. Calls never
+// allocate. Every call shares the one array: the kernel returns its counters to zero, but calls that overlap on
+// the GPU (two streams, or two host threads) race on it and must not be issued.
 constexpr size_t QG_NOALLOC_BYTES = (size_t)8 << 20;  // 16 KiB of counters + ~8 MiB of partials
 static __device__ __align__(256) unsigned char g_qgemm_noalloc_scratch[QG_NOALLOC_BYTES];
 
@@ -556,7 +557,7 @@ std::mutex g_noalloc_mutex;
 void* g_noalloc_ptr[QG_NOALLOC_MAX_DEVICES] = {};
 }  // namespace
 
-static int noalloc_scratch(void** out) {
+static int noalloc_scratch(void** out, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -572,7 +573,7 @@ static int noalloc_scratch(void** out) {
       set_error("im_qgemm_w4g64_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
       return IM_CUDA_ERROR;
     }
-    e = cudaMemset(ptr, 0, QG_COUNTER_BYTES);
+    e = cudaMemsetAsync(ptr, 0, QG_COUNTER_BYTES, stream);
     if (e != cudaSuccess) {
       set_error("im_qgemm_w4g64_noalloc: zeroing the counters: %s", cudaGetErrorString(e));
       return IM_CUDA_ERROR;
@@ -605,7 +606,7 @@ extern "C" int im_qgemm_w4g64_noalloc(const uint32_t* w, const uint16_t* scales,
              p.workspace, QG_NOALLOC_BYTES);
   void* scratch = nullptr;
   if (p.splits > 1) {
-    const int rc = noalloc_scratch(&scratch);
+    const int rc = noalloc_scratch(&scratch, reinterpret_cast<cudaStream_t>(stream));
     if (rc) return rc;
   }
   dispatch_mma<IM_EPI_STORE>(p, w, scales, biases, x, y, nullptr, (int)M, (int)N, (int)K, scratch,

@@ -7,6 +7,11 @@ through the C ABI against the workspace entry point, twice in a row (the shared 
 that a shape too large for the static array is refused without launching."""
 from __future__ import annotations
 
+import subprocess
+import sys
+import textwrap
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -48,3 +53,39 @@ def test_noalloc_refuses_shapes_beyond_its_scratch(cuda):
     sb = torch.zeros((35200, 16), dtype=torch.bfloat16, device=cuda)
     with pytest.raises(_lib.KernelUnsupported, match="static scratch"):
         noalloc(x, w, sb, sb)
+
+
+FIRST_CALL_ON_A_SIDE_STREAM = textwrap.dedent("""
+    import sys
+    import numpy as np
+    import torch
+    sys.path.insert(0, sys.argv[1])
+    from ironmule_b200 import _lib, kernels
+    from tests.gpu_util import case, to_device, torch_to_bf16_bits
+    dev = torch.device("cuda:0")
+    wq, s, b, x = case(2560, 9728, 5, seed=7)
+    w_t, s_t, b_t, x_t = to_device(wq, s, b, x, dev)
+    want = torch_to_bf16_bits(kernels.qgemm(x_t, w_t, s_t, b_t, split_k=True))
+    side = torch.cuda.Stream(dev)   # a non-blocking stream: not ordered behind the legacy default stream
+    side.wait_stream(torch.cuda.current_stream(dev))
+    outs = []
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            y = torch.empty((5, 2560), dtype=torch.bfloat16, device=dev)
+            _lib.call("im_qgemm_w4g64_noalloc", w_t.data_ptr(), s_t.data_ptr(), b_t.data_ptr(), x_t.data_ptr(),
+                      y.data_ptr(), 5, 2560, 9728, side.cuda_stream)
+            outs.append(y)
+    side.synchronize()
+    for y in outs:
+        assert np.array_equal(torch_to_bf16_bits(y), want), "no-alloc call on a side stream changed the bits"
+    print("ok")
+""")
+
+
+def test_noalloc_first_call_on_a_side_stream(cuda):
+    """The first call on a device zeroes the shared counters; on a non-blocking stream that zeroing must still
+    come before the kernel. A fresh process makes this call the device's first."""
+    root = Path(__file__).resolve().parents[1]
+    run = subprocess.run([sys.executable, "-c", FIRST_CALL_ON_A_SIDE_STREAM, str(root)], capture_output=True,
+                         text=True, timeout=300, cwd=root)
+    assert run.returncode == 0 and run.stdout.strip().endswith("ok"), run.stdout + run.stderr
