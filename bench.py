@@ -53,8 +53,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["spec_decode", "verify_step", "stochastic", "tree", "tp", "attention",
-                                           "kquant"],
+    ap.add_argument("--workload", choices=["spec_decode", "verify_step", "qgemm_pass", "stochastic", "tree", "tp",
+                                           "attention", "kquant"],
                     default="spec_decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -82,7 +82,8 @@ def peaks() -> dict:
 
 
 class Clocks:
-    """nvidia-smi samples (200 ms) of the SM clock and throttle reasons while the timed region runs."""
+    """nvidia-smi samples (every 50 ms) of the SM clock and throttle reasons, started before the warm-up steps and
+    stopped after the timed region, so that the samples under load cover the timed region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -94,7 +95,7 @@ class Clocks:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -102,7 +103,7 @@ class Clocks:
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.25)
+        time.sleep(0.1)
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
@@ -226,6 +227,13 @@ def run_reference(args, world: int, rank: int) -> None:
 
 
 # ---- GPU side --------------------------------------------------------------------------------------------
+# DRAM bytes (read + write) per launch of the verify pass's packed qGEMMs, the mean over the pass's 145 launches
+# from one ncu capture of `python bench.py --workload qgemm_pass` (the command and the per-kernel figures are in
+# the profile named below). Re-captured whenever the kernel changes.
+VERIFY_PASS_DRAM_BYTES_PER_LAUNCH = 15_727_116
+VERIFY_PASS_DRAM_SOURCE = "profiles/qgemm_packed_verify_pass_traffic.md (ncu, 145 launches, one B200)"
+
+
 def qgemm_roofline(target, peak_gbs: float, reps: int = 20) -> dict:
     """The dominant kernel: every packed qGEMM of one verify pass (M = k+1 = 5 rows: 36 x [qkv, o, gate_up,
     down] and the head), launched as the forward launches them (RMSNorm prologues on qkv / gate_up / head,
@@ -282,12 +290,9 @@ def qgemm_roofline(target, peak_gbs: float, reps: int = 20) -> dict:
     sec = e0.elapsed_time(e1) / 1000 / reps
     launches = len(calls)
     achieved = total_bytes / sec / 1e9
-    traffic = None
-    tfile = ROOT / "profiles" / "qgemm_verify_pass_traffic.json"
-    if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch_mean")
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
-            "frac": round(achieved / peak_gbs, 4), "traffic": traffic,
+            "frac": round(achieved / peak_gbs, 4), "traffic": VERIFY_PASS_DRAM_BYTES_PER_LAUNCH,
+            "traffic_source": VERIFY_PASS_DRAM_SOURCE,
             "kernel": "qgemm_packed_kernel (all 145 qGEMMs of one Qwen3-4B verify pass, M=5)",
             "launches": launches, "us_per_launch": round(sec / launches * 1e6, 2),
             "algorithmic_bytes_per_launch": total_bytes // launches, "pass_us": round(sec * 1e6, 1)}
@@ -313,14 +318,14 @@ def run_spec_decode(args, world: int, rank: int, local: int) -> None:
     dec.round()
     torch.cuda.synchronize()
     dec.capture()
+    clocks = Clocks(local)
+    clocks.start()
     dec.run_rounds(args.warmup)
     torch.cuda.synchronize()
     before = dec.read_stats()
     stream = torch.cuda.current_stream(device)
-    clocks = Clocks(local)
     barrier(world)
     torch.cuda.synchronize()
-    clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("timed_rounds")
     e0.record(stream)
@@ -392,6 +397,30 @@ def run_spec_decode(args, world: int, rank: int, local: int) -> None:
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": dec.launches_per_round() * args.steps,
             "peak_source": pk["source"]}
+        print(json.dumps(line), flush=True)
+
+
+def run_qgemm_pass(args, world: int, rank: int, local: int) -> None:
+    """The dominant kernel alone: the 145 packed qGEMMs of one Qwen3-4B verify pass (M = 5), as the default
+    workload's roofline measures them, on the target model only (2.3 GB of weights). The ncu capture of the
+    pass's DRAM traffic runs this workload."""
+    import torch
+
+    from ironmule_b200.engine import PRESETS, QuantModel
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pk = peaks()
+    target = QuantModel(PRESETS["qwen3-4b"], device, seed=0, max_ctx=64, max_rows=32, max_logit_rows=8)
+    roof = qgemm_roofline(target, pk["hbm_gbs"], reps=max(args.steps, 1))
+    if rank == 0:
+        line = {"metric": "qGEMM HBM GB/s (the 145 packed qGEMMs of one Qwen3-4B verify pass, M=5)",
+                "value": roof["achieved"], "unit": "GB/s", "n_gpus": world, "steps": max(args.steps, 1),
+                "warmup": 2, "ms_per_step": round(roof["pass_us"] / 1000, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16/4-bit", "data": "synthetic",
+                "config": {"workload": "verify pass qGEMMs, Qwen3-4B, M=5, graph-replayed",
+                           "l2": "2.26 GB of weights per pass >> 126 MB L2"},
+                "roofline": roof, "peak_source": pk["source"]}
         print(json.dumps(line), flush=True)
 
 
@@ -676,14 +705,14 @@ def run_rounds_workload(args, world: int, rank: int, local: int, kind: str) -> N
     dec.round()
     torch.cuda.synchronize()
     dec.capture()
+    clocks = Clocks(local)
+    clocks.start()
     dec.run_rounds(args.warmup)
     torch.cuda.synchronize()
     before = dec.read_stats()
     stream = torch.cuda.current_stream(device)
-    clocks = Clocks(local)
     barrier(world)
     torch.cuda.synchronize()
-    clocks.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     torch.cuda.nvtx.range_push("timed_rounds")
@@ -734,6 +763,8 @@ def main() -> int:
     try:
         if args.workload == "verify_step":
             run_verify_step(args, world, rank, local)
+        elif args.workload == "qgemm_pass":
+            run_qgemm_pass(args, world, rank, local)
         elif args.workload == "attention":
             run_attention(args, world, rank, local)
         elif args.workload == "kquant":
