@@ -315,9 +315,14 @@ class QuantModel:
                 (c.hidden, c.inter)]
 
     # ---- forward ------------------------------------------------------------------------------------------
-    def forward(self, meta: RowMeta, max_kv_len: int, logit_rows: int = 0) -> torch.Tensor | None:
+    def forward(self, meta: RowMeta, max_kv_len: int, logit_rows: int = 0,
+                trace: list | None = None) -> torch.Tensor | None:
         """Run M = meta.rows rows through the model, writing their K/V at their slots; the logits of the first
-        `logit_rows` rows land in self.logits[:logit_rows] (returned; None when logit_rows is 0)."""
+        `logit_rows` rows land in self.logits[:logit_rows] (returned; None when logit_rows is 0). With a `trace`
+        list, one dict per layer is appended holding copies of the rows at each op boundary -- "h_in" (the layer's
+        input), "qkv", "attn", "h_mid" (after the attention residual) and "act" (after the gated MLP activation) --
+        and a last dict with the final hidden rows as "h_in" (the parity tests feed each op's device input to the
+        CPU restatement of that op); never inside a captured graph."""
         c, m = self.lc, meta.rows
         if m > min(self.max_rows, MAX_QGEMM_ROWS):
             raise ValueError(f"{m} rows exceed this model's per-forward limit")
@@ -329,9 +334,16 @@ class QuantModel:
         kernels.embed(meta.tokens, self.embed.w, self.embed.s, self.embed.b, mult=mult, out=h, rows=m,
                       stride=meta.token_stride, out_sq=self.sq_embed)
         sq, parts = self.sq_embed, 1
+        def tr(key: str, t: torch.Tensor) -> None:
+            if trace is not None:
+                trace[-1][key] = t[:m].clone()
+
         for li, layer in enumerate(self.layers):
+            if trace is not None:
+                trace.append({"h_in": h[:m].clone()})
             kernels.qgemm_packed(h, layer.qkv.p, out=self.qkv, rows=m, norm_sq=sq, norm_parts=parts,
                                  norm_weight=layer.in_norm, eps=c.eps, gemma_norm=gemma, sq_ld=self.sq_ld, ws=ws)
+            tr("qkv", self.qkv)
             glob = c.is_global(li)
             kernels.attention_qkv(self.qkv, layer.q_norm, layer.k_norm, self.inv_freq if glob else self.inv_freq_local,
                                   meta.pos, self.k_cache[li], self.v_cache[li], self.page_table, meta.seq_rows,
@@ -340,6 +352,7 @@ class QuantModel:
                                   max_rows_per_seq=meta.max_rows_per_seq, max_kv_len=max_kv_len, scale=c.scale,
                                   keys_per_split=self.keys_per_split, window=0 if glob else c.sliding_window,
                                   out=self.attn, rows=m, ws=self.ws_attn, seq_slot=meta.seq_slot)
+            tr("attn", self.attn)
             if self.tp > 1:  # partial sums of the row-sharded o and down, all-reduced before the residual add
                 kernels.qgemm_packed(self.attn, layer.o.p, out=self.y, rows=m, sq_ld=self.sq_ld, ws=ws)
                 self._all_reduce(self.y[:m])
@@ -357,8 +370,10 @@ class QuantModel:
                 kernels.qgemm_packed(self.attn, layer.o.p, out=self.y, rows=m, sq_ld=self.sq_ld, ws=ws)
                 kernels.rmsnorm_residual(self.y, layer.post_attn_norm, h, c.eps, gemma=True, rows=m,
                                          out_sq=self.sq_attn)
+                tr("h_mid", h)
                 kernels.qgemm_packed(h, layer.gate_up.p, epilogue="geglu", out=self.act, rows=m, norm_sq=self.sq_attn,
                                      norm_parts=1, norm_weight=layer.post_norm, eps=c.eps, gemma_norm=True, sq_ld=self.sq_ld, ws=ws)
+                tr("act", self.act)
                 kernels.qgemm_packed(self.act, layer.down.p, out=self.y, rows=m, sq_ld=self.sq_ld, ws=ws)
                 kernels.rmsnorm_residual(self.y, layer.post_ff_norm, h, c.eps, gemma=True, rows=m,
                                          out_sq=self.sq_mlp)
@@ -366,12 +381,16 @@ class QuantModel:
                 continue
             kernels.qgemm_packed(self.attn, layer.o.p, epilogue="residual", residual=h, out=h, rows=m,
                                  out_sq=self.sq_attn, sq_ld=self.sq_ld, ws=ws)
+            tr("h_mid", h)
             kernels.qgemm_packed(h, layer.gate_up.p, epilogue="swiglu", out=self.act, rows=m,
                                  norm_sq=self.sq_attn, norm_parts=self.h_tiles, norm_weight=layer.post_norm,
                                  eps=c.eps, gemma_norm=gemma, sq_ld=self.sq_ld, ws=ws)
+            tr("act", self.act)
             kernels.qgemm_packed(self.act, layer.down.p, epilogue="residual", residual=h, out=h, rows=m,
                                  out_sq=self.sq_mlp, sq_ld=self.sq_ld, ws=ws)
             sq, parts = self.sq_mlp, self.h_tiles
+        if trace is not None:
+            trace.append({"h_in": h[:m].clone()})
         if not logit_rows:
             return None
         if self.tp == 1:

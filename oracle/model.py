@@ -147,41 +147,96 @@ class OracleModel:
             self.k[li] = np.zeros((slots, c.kv_heads, c.head_dim), dtype=np.uint16)
             self.v[li] = np.zeros((slots, c.kv_heads, c.head_dim), dtype=np.uint16)
 
-    def forward(self, tokens: list[int], slots: list[int], logits: bool = True) -> np.ndarray | None:
-        """Rows of sequence 0 at the given slots (written to the cache); returns logits bits [M, V]."""
+    def embed_rows(self, tokens: list[int]) -> np.ndarray:
+        """The rows' hidden states after the embedding gather (bf16 bits [M, H])."""
         c = self.cfg
-        gemma = c.family == "gemma3"
-        m = len(tokens)
         wq, s, b = self.embed
         h = quant.dequantize_bf16(wq[tokens], s[tokens], b[tokens])
-        if gemma:
+        if c.family == "gemma3":
             h = bf16.from_f32(bf16.to_f32(h) * R(np.float32(math.sqrt(c.hidden))))
-        pos = np.asarray(slots)
-        for li, layer in enumerate(self.layers):
-            glob = c.is_global(li)
-            xn = rmsnorm(h, layer.in_norm, c.eps, gemma)
-            qkv = self.proj(*layer.qkv, xn).reshape(m, c.heads + 2 * c.kv_heads, c.head_dim)
-            q, k, v = qkv[:, :c.heads], qkv[:, c.heads:c.heads + c.kv_heads], qkv[:, c.heads + c.kv_heads:]
-            inv_freq = self.inv_freq if glob else self.inv_freq_local
-            qn = bf16.to_f32(rmsnorm(q, layer.q_norm, c.eps, gemma))
-            kn = bf16.to_f32(rmsnorm(k, layer.k_norm, c.eps, gemma))
-            q_rot, k_rot = rope(qn, pos, inv_freq), rope(kn, pos, inv_freq)
-            self.k[li][pos] = k_rot
-            self.v[li][pos] = v
-            att = attention(q_rot, self.k[li], self.v[li], pos, c.scale, 0 if glob else c.sliding_window)
-            y = self.proj(*layer.o, att.reshape(m, -1))
-            if gemma:  # Gemma-3: post_attention_layernorm on the attention output
-                y = rmsnorm(y, layer.post_attn_norm, c.eps, gemma)
-            h = residual(h, y)
-            xn = rmsnorm(h, layer.post_norm, c.eps, gemma)
-            gu = self.proj(*layer.gate_up, xn).reshape(m, -1, 2, 16)
-            gate, up = gu[:, :, 0, :].reshape(m, -1), gu[:, :, 1, :].reshape(m, -1)
-            act = gelu_mul(gate, up) if gemma else silu_mul(gate, up)
-            y = self.proj(*layer.down, act)
-            if gemma:  # Gemma-3: post_feedforward_layernorm on the MLP output
-                y = rmsnorm(y, layer.post_ff_norm, c.eps, gemma)
-            h = residual(h, y)
-        if not logits:
-            return None
-        hn = rmsnorm(h, self.final_norm, c.eps, gemma)
+        return h
+
+    def layer_forward(self, li: int, h: np.ndarray, slots, positions=None, tree_mask=None,
+                      tree_base: int = 0) -> np.ndarray:
+        """Decoder layer `li` over hidden rows h (bits [M, H]) of sequence 0: writes the rows' K/V at `slots` of
+        this layer's cache and returns the layer's output rows. Positions (RoPE) default to the slots; a tree
+        verify passes both, with each row's ancestor bits over the slots from tree_base on."""
+        c = self.cfg
+        gemma = c.family == "gemma3"
+        layer = self.layers[li]
+        m = h.shape[0]
+        slots = np.asarray(slots)
+        pos = slots if positions is None else np.asarray(positions)
+        glob = c.is_global(li)
+        xn = rmsnorm(h, layer.in_norm, c.eps, gemma)
+        qkv = self.proj(*layer.qkv, xn).reshape(m, c.heads + 2 * c.kv_heads, c.head_dim)
+        q, k, v = qkv[:, :c.heads], qkv[:, c.heads:c.heads + c.kv_heads], qkv[:, c.heads + c.kv_heads:]
+        inv_freq = self.inv_freq if glob else self.inv_freq_local
+        qn = bf16.to_f32(rmsnorm(q, layer.q_norm, c.eps, gemma))
+        kn = bf16.to_f32(rmsnorm(k, layer.k_norm, c.eps, gemma))
+        q_rot, k_rot = rope(qn, pos, inv_freq), rope(kn, pos, inv_freq)
+        self.k[li][slots] = k_rot
+        self.v[li][slots] = v
+        att = attention(q_rot, self.k[li], self.v[li], slots, c.scale, 0 if glob else c.sliding_window,
+                        tree_mask=tree_mask, tree_base=tree_base)
+        y = self.proj(*layer.o, att.reshape(m, -1))
+        if gemma:  # Gemma-3: post_attention_layernorm on the attention output
+            y = rmsnorm(y, layer.post_attn_norm, c.eps, gemma)
+        h = residual(h, y)
+        xn = rmsnorm(h, layer.post_norm, c.eps, gemma)
+        gu = self.proj(*layer.gate_up, xn).reshape(m, -1, 2, 16)
+        gate, up = gu[:, :, 0, :].reshape(m, -1), gu[:, :, 1, :].reshape(m, -1)
+        act = gelu_mul(gate, up) if gemma else silu_mul(gate, up)
+        y = self.proj(*layer.down, act)
+        if gemma:  # Gemma-3: post_feedforward_layernorm on the MLP output
+            y = rmsnorm(y, layer.post_ff_norm, c.eps, gemma)
+        return residual(h, y)
+
+    def layer_steps(self, li: int, dev: dict, slots, positions=None, tree_mask=None, tree_base: int = 0) -> dict:
+        """Each op of layer `li` restated from the DEVICE's input to that op (bits in `dev`: "h_in", "qkv", "attn",
+        "h_mid", "act", and "h_out" = the next layer's input), so every op is checked with identical inputs:
+          "qkv"    projection of the input RMSNorm of h_in
+          "attn"   q/k RMSNorm + RoPE of the device's qkv, K/V written at `slots`, attention over the cache
+          "h_mid"  h_in + o(attn)                     (Gemma-3: + RMSNorm of o(attn))
+          "act"    SwiGLU / GeGLU of gate_up(RMSNorm(h_mid))
+          "h_out"  h_mid + down(act)                  (Gemma-3: + RMSNorm of down(act))"""
+        c = self.cfg
+        gemma = c.family == "gemma3"
+        layer = self.layers[li]
+        m = dev["h_in"].shape[0]
+        slots = np.asarray(slots)
+        pos = slots if positions is None else np.asarray(positions)
+        glob = c.is_global(li)
+        out = {"qkv": self.proj(*layer.qkv, rmsnorm(dev["h_in"], layer.in_norm, c.eps, gemma))}
+        qkv = dev["qkv"].reshape(m, c.heads + 2 * c.kv_heads, c.head_dim)
+        q, k, v = qkv[:, :c.heads], qkv[:, c.heads:c.heads + c.kv_heads], qkv[:, c.heads + c.kv_heads:]
+        inv_freq = self.inv_freq if glob else self.inv_freq_local
+        q_rot = rope(bf16.to_f32(rmsnorm(q, layer.q_norm, c.eps, gemma)), pos, inv_freq)
+        self.k[li][slots] = rope(bf16.to_f32(rmsnorm(k, layer.k_norm, c.eps, gemma)), pos, inv_freq)
+        self.v[li][slots] = v
+        out["attn"] = attention(q_rot, self.k[li], self.v[li], slots, c.scale, 0 if glob else c.sliding_window,
+                                tree_mask=tree_mask, tree_base=tree_base).reshape(m, -1)
+        y = self.proj(*layer.o, dev["attn"])
+        if gemma:
+            y = rmsnorm(y, layer.post_attn_norm, c.eps, gemma)
+        out["h_mid"] = residual(dev["h_in"], y)
+        gu = self.proj(*layer.gate_up, rmsnorm(dev["h_mid"], layer.post_norm, c.eps, gemma)).reshape(m, -1, 2, 16)
+        gate, up = gu[:, :, 0, :].reshape(m, -1), gu[:, :, 1, :].reshape(m, -1)
+        out["act"] = gelu_mul(gate, up) if gemma else silu_mul(gate, up)
+        y = self.proj(*layer.down, dev["act"])
+        if gemma:
+            y = rmsnorm(y, layer.post_ff_norm, c.eps, gemma)
+        out["h_out"] = residual(dev["h_mid"], y)
+        return out
+
+    def head(self, h: np.ndarray) -> np.ndarray:
+        """Final RMSNorm and the tied head: logits bits [M, V]."""
+        hn = rmsnorm(h, self.final_norm, self.cfg.eps, self.cfg.family == "gemma3")
         return self.proj(*self.embed, hn)
+
+    def forward(self, tokens: list[int], slots: list[int], logits: bool = True) -> np.ndarray | None:
+        """Rows of sequence 0 at the given slots (written to the cache); returns logits bits [M, V]."""
+        h = self.embed_rows(tokens)
+        for li in range(self.cfg.layers):
+            h = self.layer_forward(li, h, slots)
+        return self.head(h) if logits else None

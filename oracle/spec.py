@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import numpy as np
 
+from . import bf16
 from .accept import greedy_accept, row_stats
 from .model import OracleModel
 
@@ -18,12 +19,15 @@ class CpuSpecDecoder:
     def __init__(self, target: OracleModel, draft: OracleModel, k: int = 4, slots: int = 1024):
         self.target, self.draft, self.k, self.slots = target, draft, k, slots
         self.hist: list[int] = []
+        self.margins: list[float] = []  # per committed token: top-2 logit margin of the verify row that chose it
+        self.tops: list[float] = []     # ... and that row's top logit
         self.rounds = self.accepted = 0
 
     def start(self, prompt: list[int]) -> None:
         self.target.reset(self.slots)
         self.draft.reset(self.slots)
         self.hist = list(prompt)
+        self.margins, self.tops = [], []
         if len(prompt) > 1:
             pos = list(range(len(prompt) - 1))
             self.target.forward(prompt[:-1], pos, logits=False)
@@ -40,10 +44,19 @@ class CpuSpecDecoder:
         vlog = self.target.forward([self.hist[n - 1]] + drafts, list(range(n - 1, n + k)))
         picks = row_stats(vlog)[0].tolist()
         kept = greedy_accept(drafts, picks)
+        self.margins.extend(top2_margin(vlog[i]) for i in range(len(kept)))
+        self.tops.extend(float(bf16.to_f32(vlog[i]).max()) for i in range(len(kept)))
         self.hist.extend(kept)
         self.rounds += 1
         self.accepted += len(kept) - 1
         return kept
+
+
+def top2_margin(row_bits: np.ndarray) -> float:
+    """The gap between the largest and the second-largest logit of a row (0 for a tie at the top)."""
+    f = bf16.to_f32(row_bits).astype(np.float64)
+    top2 = np.partition(f, -2)[-2:]
+    return float(top2[1] - top2[0])
 
 
 def random_model(cfg, seed: int = 0, slots: int = 256, fast: bool = True) -> OracleModel:
