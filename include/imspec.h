@@ -147,6 +147,10 @@ int im_qgemm_packed_tune(int split_override, int target_ctas, int max_split);
  * warp MMA otherwise), 1 = warp MMA always, 2 = tensor cores always. Process-wide; every choice gives the same
  * bits; changes workspace sizes, so set it before sizing workspaces. */
 int im_qgemm_packed_path(int path);
+/* Split-K reduction of the warp-MMA kernel: 1 (default) = the K splits of a CTA column run as one thread-block
+ * cluster and their partials are summed through distributed shared memory (when the device can schedule the
+ * cluster), 0 = through the workspace and a global arrival counter. Process-wide; both give the same bits. */
+int im_qgemm_packed_cluster(int on);
 /* The error word of a workspace last used by a call of more than 32 rows (the tensor-core kernel): 0 when
  * every bounded wait of that kernel completed, 1 when one ran out. Synchronous (reads device memory). */
 int im_qgemm_packed_status(const void* workspace);

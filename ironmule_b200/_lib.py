@@ -41,6 +41,7 @@ SIGNATURES: dict[str, tuple] = {
     "im_qgemm_packed_tune": (_INT, [_INT, _INT, _INT]),
     "im_qgemm_packed_status": (_INT, [_P]),
     "im_qgemm_packed_path": (_INT, [_INT]),
+    "im_qgemm_packed_cluster": (_INT, [_INT]),
     "im_set_launch_overlap": (_INT, [_INT]),
     "im_rmsnorm_residual": (_INT, [_P, _P, _P, _I64, _I64, ctypes.c_float, _INT, _P, _P]),
     "im_topk_workspace_bytes": (_SZ, [_I64, _I64, _I64]),

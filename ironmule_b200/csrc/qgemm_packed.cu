@@ -26,7 +26,8 @@ constexpr int Q4_THREADS = Q4_WARPS * 32;
 constexpr int Q4_DEPTH = 3;               // units in flight per warp
 static int g_q4_split_override = 0;       // sweep hook (0 = automatic)
 static int g_q4_target_ctas = 148 * 4;    // split policy: aim for this many CTAs
-static int g_q4_max_split = 64;
+static int g_q4_max_split = Q4_MAX_SPLITS;
+static int g_q4_cluster = 1;             // reduce split-K partials inside a thread-block cluster when possible
 static int g_q4_path = 0;                 // 0: automatic, 1: warp MMA always, 2: tensor cores always
 
 // The tensor-core kernel wins where an item streams many groups for many rows. Measured on B200 whole rounds:
@@ -105,16 +106,116 @@ __global__ void q4_pack_kernel(const uint32_t* __restrict__ w, const uint16_t* _
 }
 
 // ---- the GEMM -------------------------------------------------------------------------------------------
-// Dynamic shared memory: xf [rmax][NT][32 lanes][2 x 16 B] activation fragments, sx [rmax][NT*8] group sums,
-// inv [32] RMSNorm factors.
-__host__ __device__ constexpr size_t q4_smem_bytes(int nt) {
-  return (size_t)Q4_RMAX * nt * 32 * 32 + (size_t)Q4_RMAX * nt * 8 * 4 + 32 * 4;
+// Dynamic shared memory, for rg = the most groups a split holds:
+//   xf   [rg][NT][32 lanes][2 x 16 B]  activation fragments (the RMSNorm partial sums are staged here first)
+//   sxs  [rg][NT*8]                    group sums of the activations
+//   inv  [32]                          RMSNorm factors
+//   part [4 warps][2*NT*4][32 lanes]   this CTA's split-K partials, read by the cluster's reducing CTA
+struct Q4Smem {
+  size_t xf, sxs, inv, part, total;
+};
+__host__ __device__ inline Q4Smem q4_smem(int nt, int rg, int norm_parts) {
+  Q4Smem m;
+  const size_t xf = (size_t)rg * nt * 32 * 32;
+  const size_t nsum = (size_t)norm_parts * nt * 8 * 4;
+  m.xf = 0;
+  m.sxs = (xf > nsum ? xf : nsum + 15) / 16 * 16;
+  m.inv = m.sxs + (size_t)rg * nt * 8 * 4;
+  m.part = m.inv + 32 * 4;
+  m.total = m.part + (size_t)Q4_WARPS * 2 * nt * 4 * 32 * 4;
+  return m;
+}
+
+// ---- thread-block cluster helpers (split-K partials reduced through distributed shared memory) -------------
+__device__ __forceinline__ unsigned q4_cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void q4_cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void q4_cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// The shared::cluster address of the same shared-memory location in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t q4_mapa(const void* local, unsigned rank) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(local);
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float q4_ld_dsmem(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// The epilogue of one tile's warp: SwiGLU / GeGLU, or store / residual add with the per-row sums of squares of the
+// written rows. rres holds the residual when it was loaded before the main loop (RES_EARLY).
+template <int NT, int EPI, bool RES_EARLY>
+__device__ __forceinline__ void q4_epilogue(const Q4Args& a, const float (&tot)[2][NT][4],
+                                            const uint16_t (&rres)[2][NT][4], int tile, int g, int t) {
+  const int rbase = tile * 32;
+  if constexpr (EPI == IM_EPI_SWIGLU || EPI == IM_EPI_GEGLU) {
+    const int nout = a.N >> 1;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const int f = (rbase >> 1) + g + ((e >> 1) << 3);
+        const int m = nt * 8 + 2 * t + (e & 1);
+        if (m < a.M && f < nout) {
+          const float ga = round_bf(tot[0][nt][e]), uu = round_bf(tot[1][nt][e]);
+          float o;
+          if (EPI == IM_EPI_SWIGLU) {
+            const float sig = round_bf(1.0f / (1.0f + expf(-ga)));
+            o = round_bf(ga * sig) * uu;
+          } else {
+            const float inner = 0.7978845608028654f * (ga + 0.044715f * ga * ga * ga);
+            o = round_bf(0.5f * ga * (1.0f + tanhf(inner))) * uu;
+          }
+          a.y[(size_t)m * nout + f] = to_bf(o);
+        }
+      }
+  } else {
+    float sq[NT][2] = {};
+#pragma unroll
+    for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int r = rbase + tt * 16 + g + ((e >> 1) << 3);
+          const int m = nt * 8 + 2 * t + (e & 1);
+          if (m < a.M && r < a.N) {
+            const size_t o = (size_t)m * a.N + r;
+            const uint16_t rv = EPI != IM_EPI_RESIDUAL ? (uint16_t)0 : (RES_EARLY ? rres[tt][nt][e] : a.res[o]);
+            const uint16_t h = EPI == IM_EPI_RESIDUAL ? to_bf(bf(rv) + round_bf(tot[tt][nt][e])) : to_bf(tot[tt][nt][e]);
+            a.y[o] = h;
+            const float hv = bf(h);
+            sq[nt][e & 1] = fmaf(hv, hv, sq[nt][e & 1]);
+          }
+        }
+    if (a.out_sq) {
+      // per activation row m: the sum over this tile's 32 rows, fixed order (lanes with the same t)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          float v = sq[nt][e];
+          v += __shfl_xor_sync(0xffffffffu, v, 4);
+          v += __shfl_xor_sync(0xffffffffu, v, 8);
+          v += __shfl_xor_sync(0xffffffffu, v, 16);
+          const int m = nt * 8 + 2 * t + e;
+          if (g == 0 && m < a.M) a.out_sq[(size_t)tile * a.sq_ld + m] = v;
+        }
+    }
+  }
 }
 
 // grid (CTA columns of 4 tiles, K splits, 32-row chunks). A chunk is computed exactly as a call of its rows alone
-// would be: the same plan, its own split-K counters and partials.
-template <int NT, int EPI>
-__global__ void __launch_bounds__(Q4_THREADS)
+// would be: the same plan, its own split-K counters and partials. CL: the K splits of a CTA column form one
+// thread-block cluster and their partials are summed through distributed shared memory (no global atomics);
+// otherwise the last split to arrive at a global counter sums them. Both sum in split order: the same bits.
+template <int NT, int EPI, bool CL>
+__global__ void __launch_bounds__(Q4_THREADS, NT == 1 ? 5 : 1)
 qgemm_packed_kernel(Q4Args a) {
   extern __shared__ __align__(16) unsigned char q4_raw[];
   if (gridDim.z > 1) {  // this CTA's 32-row chunk
@@ -129,9 +230,11 @@ qgemm_packed_kernel(Q4Args a) {
     a.partial += (size_t)blockIdx.z * a.tiles * a.splits * (2 * 4 * 4 * 32);
     a.M = min(32, a.M - m0);
   }
-  uint4 (*xf)[NT][32][2] = reinterpret_cast<uint4 (*)[NT][32][2]>(q4_raw);
-  float (*sxs)[NT * 8] = reinterpret_cast<float (*)[NT * 8]>(q4_raw + (size_t)Q4_RMAX * NT * 32 * 32);
-  float* inv_s = reinterpret_cast<float*>(q4_raw + (size_t)Q4_RMAX * NT * 32 * 32 + (size_t)Q4_RMAX * NT * 8 * 4);
+  const Q4Smem lay = q4_smem(NT, a.rg, a.norm_w ? a.norm_parts : 0);
+  uint4 (*xf)[NT][32][2] = reinterpret_cast<uint4 (*)[NT][32][2]>(q4_raw + lay.xf);
+  float (*sxs)[NT * 8] = reinterpret_cast<float (*)[NT * 8]>(q4_raw + lay.sxs);
+  float* inv_s = reinterpret_cast<float*>(q4_raw + lay.inv);
+  float* part_s = reinterpret_cast<float*>(q4_raw + lay.part);
   const int G = a.K >> 6;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -141,6 +244,9 @@ qgemm_packed_kernel(Q4Args a) {
   const int ng = cg1 - cg0;
   const int tile = blockIdx.x * Q4_WARPS + warp;
   const bool live = tile < a.tiles;
+  // the warp that finishes this tile: the last split to arrive (global counter), or in a cluster the CTA of rank
+  // warp % splits (so the four tiles of a column are finished by up to four CTAs)
+  const bool reducer = CL && a.splits > 1 ? (int)q4_cluster_rank() == warp % a.splits : true;
 
   // ---- before the dependency wait: this warp's weights (which no earlier kernel writes). Its slice is ng
   // consecutive 1152-byte units; the first Q4_DEPTH go to registers, the rest are prefetched into L2.
@@ -163,18 +269,67 @@ qgemm_packed_kernel(Q4Args a) {
   pdl_wait();
   pdl_trigger();
 
-  // ---- prologue: RMSNorm factors, then the activation fragments and group sums of [cg0, cg1)
+  // the residual this warp's epilogue adds, loaded now so that its latency hides behind the main loop
+  constexpr bool RES_EARLY = EPI == IM_EPI_RESIDUAL && NT <= 2;
+  uint16_t rres[2][NT][4];
+  if constexpr (RES_EARLY) {
+#pragma unroll
+    for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const int r = tile * 32 + tt * 16 + g + ((e >> 1) << 3);
+          const int m = nt * 8 + 2 * t + (e & 1);
+          rres[tt][nt][e] = live && reducer && m < a.M && r < a.N ? a.res[(size_t)m * a.N + r] : (uint16_t)0;
+        }
+  }
+
+  // ---- prologue: RMSNorm factors, then the activation fragments and group sums of [cg0, cg1). This thread's
+  // first activation slice is loaded before the RMSNorm factors, so that the two loads are in flight together.
+  uint4 pre_lo = make_uint4(0, 0, 0, 0), pre_hi = pre_lo;
+  {
+    const int job = threadIdx.x;
+    const int tq = job & 3, m = (job >> 2) % (NT * 8), gl = (job >> 2) / (NT * 8);
+    if (job < ng * NT * 32 && m < a.M) {
+      const uint16_t* xp = a.x + (size_t)m * a.K + (size_t)(cg0 + gl) * 64 + 16 * tq;
+      pre_lo = __ldg(reinterpret_cast<const uint4*>(xp));
+      pre_hi = __ldg(reinterpret_cast<const uint4*>(xp + 8));
+    }
+  }
   if (a.norm_w) {
-    for (int m = threadIdx.x; m < NT * 8; m += Q4_THREADS) {
+    // the per-tile sums of squares of every activation row, all loaded at once, then summed in tile order
+    constexpr int ROWS = NT * 8;
+    float* nsum = reinterpret_cast<float*>(q4_raw + lay.xf);  // the fragments are written after this
+    const int total = a.norm_parts * ROWS;
+    for (int i0 = 0; i0 < total; i0 += 8 * Q4_THREADS) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int i = i0 + j * Q4_THREADS + threadIdx.x;
+        const int pp = i / ROWS, m = i - pp * ROWS;
+        v[j] = i < total && m < a.M ? a.norm_sq[(size_t)pp * a.sq_ld + m] : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int i = i0 + j * Q4_THREADS + threadIdx.x;
+        if (i < total) nsum[i] = v[j];
+      }
+    }
+    __syncthreads();
+    for (int m = threadIdx.x; m < ROWS; m += Q4_THREADS) {
       float s = 0.f;
-      if (m < a.M)
-        for (int p = 0; p < a.norm_parts; p++) s += a.norm_sq[(size_t)p * a.sq_ld + m];
+      if (m < a.M) {
+#pragma unroll 8
+        for (int pp = 0; pp < a.norm_parts; pp++) s += nsum[pp * ROWS + m];
+      }
       inv_s[m] = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(s, (float)a.K) + a.eps));
     }
     __syncthreads();
   }
   // one thread per (group, activation row m, quarter t): 16 values -> fragment order + partial sum
   for (int job = threadIdx.x; job < ng * NT * 32; job += Q4_THREADS) {
+    const bool first = job == (int)threadIdx.x;
     const int tq = job & 3;
     const int m = (job >> 2) % (NT * 8);
     const int gl = (job >> 2) / (NT * 8);
@@ -182,9 +337,14 @@ qgemm_packed_kernel(Q4Args a) {
     uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
     float part = 0.f;
     if (m < a.M) {
-      const uint16_t* xp = a.x + (size_t)m * a.K + (size_t)grp * 64 + 16 * tq;
-      lo = __ldg(reinterpret_cast<const uint4*>(xp));
-      hi = __ldg(reinterpret_cast<const uint4*>(xp + 8));
+      if (first) {
+        lo = pre_lo;
+        hi = pre_hi;
+      } else {
+        const uint16_t* xp = a.x + (size_t)m * a.K + (size_t)grp * 64 + 16 * tq;
+        lo = __ldg(reinterpret_cast<const uint4*>(xp));
+        hi = __ldg(reinterpret_cast<const uint4*>(xp + 8));
+      }
       if (a.norm_w) {
         const float inv = inv_s[m];
         const uint16_t* wv = a.norm_w + (size_t)grp * 64 + 16 * tq;
@@ -225,7 +385,8 @@ qgemm_packed_kernel(Q4Args a) {
     if (tq == 0) sxs[gl][m] = part;
   }
   __syncthreads();
-  if (!live) return;
+  constexpr bool CLUSTER = CL;
+  if (!CLUSTER && !live) return;  // in a cluster every thread takes part in the cluster barriers
 
   // ---- main loop: this warp's tile over [cg0, cg1), one 1152-byte unit per group, Q4_DEPTH units in flight
   float tot[2][NT][4];
@@ -235,19 +396,16 @@ qgemm_packed_kernel(Q4Args a) {
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
       for (int e = 0; e < 4; e++) tot[tt][nt][e] = 0.f;
-  // the register ring: Q4_DEPTH units in flight per warp (two 16-byte code loads + one scale/bias load per lane)
-#pragma unroll 1
-  for (int gl0 = 0; gl0 < ng; gl0 += Q4_DEPTH) {
-#pragma unroll
-  for (int d = 0; d < Q4_DEPTH; d++) {
-    const int gl = gl0 + d;
-    if (gl >= ng) break;
-    const uint4 c0 = rc0[d], c1 = rc1[d], sb = rsb[d];
+  const int ng_live = live ? ng : 0;
+  // the register ring: Q4_DEPTH units in flight per warp (two 16-byte code loads + one scale/bias load per lane).
+  // One unit: its codes and scales leave the ring, the unit Q4_DEPTH groups on is loaded in their place.
+  auto unit = [&](const int gl, uint4& r0, uint4& r1, uint4& rb) {
+    const uint4 c0 = r0, c1 = r1, sb = rb;
     if (gl + Q4_DEPTH < ng) {
       const unsigned char* nu = up + (size_t)(gl + Q4_DEPTH) * Q4_UNIT;
-      rc0[d] = q4_ld_stream(nu + lane * 32);
-      rc1[d] = q4_ld_stream(nu + lane * 32 + 16);
-      rsb[d] = __ldg(reinterpret_cast<const uint4*>(nu + 1024 + g * 16));
+      r0 = q4_ld_stream(nu + lane * 32);
+      r1 = q4_ld_stream(nu + lane * 32 + 16);
+      rb = __ldg(reinterpret_cast<const uint4*>(nu + 1024 + g * 16));
     }
     uint32_t px[NT][8];
     float sx[NT][2];
@@ -291,11 +449,83 @@ qgemm_packed_kernel(Q4Args a) {
         tot[tt][nt][3] = fmaf(b1, sx[nt][1], fmaf(s1, acc[nt][3], tot[tt][nt][3]));
       }
     }
-  }
+  };
+  // whole rounds of Q4_DEPTH units as straight-line code (independent units' MMA chains can interleave), then
+  // the last partial round
+  // the last partial round (with more rows, where registers are scarcer, every round checks its units instead)
+  if constexpr (NT == 1) {
+    int gl0 = 0;
+#pragma unroll 1
+    for (; gl0 + Q4_DEPTH <= ng_live; gl0 += Q4_DEPTH) {
+#pragma unroll
+      for (int d = 0; d < Q4_DEPTH; d++) unit(gl0 + d, rc0[d], rc1[d], rsb[d]);
+    }
+#pragma unroll
+    for (int d = 0; d < Q4_DEPTH - 1; d++)
+      if (gl0 + d < ng_live) unit(gl0 + d, rc0[d], rc1[d], rsb[d]);
+  } else {
+#pragma unroll 1
+    for (int gl0 = 0; gl0 < ng_live; gl0 += Q4_DEPTH) {
+#pragma unroll
+      for (int d = 0; d < Q4_DEPTH; d++) {
+        if (gl0 + d >= ng_live) break;
+        unit(gl0 + d, rc0[d], rc1[d], rsb[d]);
+      }
+    }
   }
 
-  // ---- split-K: per-warp partial, the last split of a tile sums them in split order
+  // ---- split-K: per-warp partial, summed in split order
   constexpr int NV = 2 * NT * 4;
+  if (CLUSTER && a.splits > 1) {
+    // each CTA of the cluster keeps its partials in its own shared memory; the reducing warp of a tile reads the
+    // split partials of every CTA of the cluster in split order (CTA rank = split)
+    float* mine = part_s + warp * NV * 32;
+#pragma unroll
+    for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+      for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) mine[((tt * NT + nt) * 4 + e) * 32 + lane] = tot[tt][nt][e];
+    q4_cluster_arrive();
+    q4_cluster_wait();
+    const bool finish = live && reducer;
+    if (finish) {
+#pragma unroll
+      for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+          for (int e = 0; e < 4; e++) tot[tt][nt][e] = 0.f;
+      constexpr int SB = NV <= 8 ? 8 : (NV <= 16 ? 4 : 2);
+      for (int s0 = 0; s0 < a.splits; s0 += SB) {
+        float buf[SB][NV];
+#pragma unroll
+        for (int j = 0; j < SB; j++) {
+          if (s0 + j < a.splits) {
+            const uint32_t src = q4_mapa(mine, (unsigned)(s0 + j)) + (uint32_t)lane * 4u;
+#pragma unroll
+            for (int v = 0; v < NV; v++) buf[j][v] = q4_ld_dsmem(src + (uint32_t)v * 128u);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < SB; j++) {
+          if (s0 + j < a.splits) {
+#pragma unroll
+            for (int tt = 0; tt < 2; tt++)
+#pragma unroll
+              for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) tot[tt][nt][e] += buf[j][(tt * NT + nt) * 4 + e];
+          }
+        }
+      }
+    }
+    q4_cluster_arrive();  // this CTA has read what it needs from its peers
+    if (finish) q4_epilogue<NT, EPI, RES_EARLY>(a, tot, rres, tile, g, t);
+    q4_cluster_wait();    // no CTA leaves while a peer may still read its partials
+    return;
+  }
+  if (!live) return;
   if (a.splits > 1) {
     float* mine = a.partial + ((size_t)tile * a.splits + split) * NV * 32;
 #pragma unroll
@@ -344,62 +574,7 @@ qgemm_packed_kernel(Q4Args a) {
     if (lane == 0) a.counters[tile] = 0u;
   }
 
-  // ---- epilogue
-  const int rbase = tile * 32;
-  if constexpr (EPI == IM_EPI_SWIGLU || EPI == IM_EPI_GEGLU) {
-    const int nout = a.N >> 1;
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        const int f = (rbase >> 1) + g + ((e >> 1) << 3);
-        const int m = nt * 8 + 2 * t + (e & 1);
-        if (m < a.M && f < nout) {
-          const float ga = round_bf(tot[0][nt][e]), uu = round_bf(tot[1][nt][e]);
-          float o;
-          if (EPI == IM_EPI_SWIGLU) {
-            const float sig = round_bf(1.0f / (1.0f + expf(-ga)));
-            o = round_bf(ga * sig) * uu;
-          } else {
-            const float inner = 0.7978845608028654f * (ga + 0.044715f * ga * ga * ga);
-            o = round_bf(0.5f * ga * (1.0f + tanhf(inner))) * uu;
-          }
-          a.y[(size_t)m * nout + f] = to_bf(o);
-        }
-      }
-  } else {
-    float sq[NT][2] = {};
-#pragma unroll
-    for (int tt = 0; tt < 2; tt++)
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          const int r = rbase + tt * 16 + g + ((e >> 1) << 3);
-          const int m = nt * 8 + 2 * t + (e & 1);
-          if (m < a.M && r < a.N) {
-            const size_t o = (size_t)m * a.N + r;
-            const uint16_t h = EPI == IM_EPI_RESIDUAL ? to_bf(bf(a.res[o]) + round_bf(tot[tt][nt][e])) : to_bf(tot[tt][nt][e]);
-            a.y[o] = h;
-            const float hv = bf(h);
-            sq[nt][e & 1] = fmaf(hv, hv, sq[nt][e & 1]);
-          }
-        }
-    if (a.out_sq) {
-      // per activation row m: the sum over this tile's 32 rows, fixed order (lanes with the same t)
-#pragma unroll
-      for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-          float v = sq[nt][e];
-          v += __shfl_xor_sync(0xffffffffu, v, 4);
-          v += __shfl_xor_sync(0xffffffffu, v, 8);
-          v += __shfl_xor_sync(0xffffffffu, v, 16);
-          const int m = nt * 8 + 2 * t + e;
-          if (g == 0 && m < a.M) a.out_sq[(size_t)tile * a.sq_ld + m] = v;
-        }
-    }
-  }
+  q4_epilogue<NT, EPI, RES_EARLY>(a, tot, rres, tile, g, t);
 }
 
 Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
@@ -417,6 +592,7 @@ Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
   if (s < need) s = need;
   if (g_q4_split_override > 0) s = g_q4_split_override < need ? need : (g_q4_split_override > G ? G : g_q4_split_override);
   p.splits = s;
+  p.rg = (G + s - 1) / s;
   p.chunks = (int)((M + 31) / 32);
   if (q4_tensor_cores(M, s))  // the tensor-core path always needs the counter region (its error word)
     p.workspace = Q4_COUNTER_BYTES + qtc_workspace_bytes(p, M, K);
@@ -425,16 +601,73 @@ Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
   return p;
 }
 
+// Whether clusters of `splits` CTAs of this kernel can be scheduled at all (asked once per split count, before
+// any launch, so a refusal never happens inside a stream capture).
+template <int NT, int EPI>
+static bool q4_cluster_ok(int splits, size_t smem) {
+  static int known[Q4_MAX_SPLITS + 1] = {};  // 0 unknown, 1 yes, 2 no
+  if (splits < 2 || splits > Q4_MAX_SPLITS) return false;
+  if (!known[splits]) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, splits, 1);
+    cfg.blockDim = dim3(Q4_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = splits;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, qgemm_packed_kernel<NT, EPI, true>, &cfg);
+    known[splits] = e == cudaSuccess && clusters > 0 ? 1 : 2;
+    if (e != cudaSuccess) (void)cudaGetLastError();
+  }
+  return known[splits] == 1;
+}
+
 template <int NT, int EPI>
 static int q4_launch(const Q4Plan& p, const Q4Args& a, cudaStream_t st) {
-  constexpr size_t smem = q4_smem_bytes(NT);
+  const size_t smem = q4_smem(NT, a.rg, a.norm_w ? a.norm_parts : 0).total;
   static bool configured = false;
   if (!configured) {
-    cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int most = (int)q4_smem(NT, Q4_RMAX, Q4_MAX_NORM_PARTS).total;
+    cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     configured = true;
   }
   dim3 grid(p.ctas_x, p.splits, p.chunks);
-  return launch("qgemm_packed_kernel", qgemm_packed_kernel<NT, EPI>, grid, dim3(Q4_THREADS), smem, st, a);
+  const bool cluster = g_q4_cluster && p.splits > 1 && q4_cluster_ok<NT, EPI>(p.splits, smem);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(Q4_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (launch_overlap()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    n++;
+  }
+  if (cluster) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = p.splits;
+    attr[n].val.clusterDim.z = 1;
+    n++;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t e = cluster ? cudaLaunchKernelEx(&cfg, qgemm_packed_kernel<NT, EPI, true>, a)
+                                : cudaLaunchKernelEx(&cfg, qgemm_packed_kernel<NT, EPI, false>, a);
+  if (e != cudaSuccess) {
+    set_error("qgemm_packed_kernel: %s", cudaGetErrorString(e));
+    return IM_CUDA_ERROR;
+  }
+  return IM_OK;
 }
 
 template <int EPI>
@@ -456,6 +689,12 @@ extern "C" int im_qgemm_packed_tune(int split_override, int target_ctas, int max
   g_q4_split_override = split_override;
   g_q4_target_ctas = target_ctas;
   g_q4_max_split = max_split;
+  return IM_OK;
+}
+
+extern "C" int im_qgemm_packed_cluster(int on) {
+  IM_REQUIRE(on == 0 || on == 1, IM_INVALID, "im_qgemm_packed_cluster: 0 or 1");
+  g_q4_cluster = on;
   return IM_OK;
 }
 
@@ -521,6 +760,8 @@ extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* 
   IM_REQUIRE(!glu || !out_sq, IM_INVALID, "im_qgemm_packed: sums of squares come from store/residual epilogues");
   IM_REQUIRE(!norm_weight || (norm_sq && norm_parts >= 1 && aligned(norm_weight, 2)), IM_INVALID,
              "im_qgemm_packed: the RMSNorm prologue needs norm_sq partials and a weight");
+  IM_REQUIRE(!norm_weight || norm_parts <= Q4_MAX_NORM_PARTS, IM_UNSUPPORTED,
+             "im_qgemm_packed: %lld sum-of-squares parts exceed %d", (long long)norm_parts, Q4_MAX_NORM_PARTS);
   const int64_t ld = sq_ld > 0 ? sq_ld : (M + 31) / 32 * 32;
   IM_REQUIRE(ld >= M, IM_INVALID, "im_qgemm_packed: sq_ld %lld below M", (long long)ld);
   const Q4Plan p = q4_plan(M, N, K);
@@ -552,6 +793,7 @@ extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* 
   a.norm_parts = (int)norm_parts;
   a.gemma_norm = gemma_norm;
   a.sq_ld = (int)ld;
+  a.rg = p.rg;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (tc) return qtc_launch(p, a, epilogue, workspace, st);
   switch (epilogue) {

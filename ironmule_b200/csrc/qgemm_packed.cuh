@@ -11,7 +11,9 @@
 namespace im {
 
 constexpr int Q4_UNIT = 1152;                // packed bytes per (32-row tile, 64-wide group)
-constexpr int Q4_RMAX = 16;                  // groups per CTA K range (the split plan never exceeds it)
+constexpr int Q4_RMAX = 24;                  // groups per CTA K range (the split plan never exceeds it)
+constexpr int Q4_MAX_SPLITS = 16;            // K splits per tile: one thread-block cluster reduces them
+constexpr int Q4_MAX_NORM_PARTS = 256;       // partial sums of squares per activation row (RMSNorm prologue)
 constexpr size_t Q4_COUNTER_BYTES = 524288;  // split-K arrival counters; the last word is the error word
 constexpr int Q4_MAX_ROWS = 320;             // activation rows per call
 
@@ -27,10 +29,12 @@ struct Q4Args {
   unsigned* counters;
   float eps;
   int M, N, K, tiles, splits, norm_parts, gemma_norm, sq_ld;
+  int rg;                   // the most groups any split holds (sizes the activation staging)
 };
 
 struct Q4Plan {
   int tiles, ctas_x, splits, nt, chunks;
+  int rg;  // the most groups one split holds
   size_t workspace;
 };
 

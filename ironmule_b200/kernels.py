@@ -458,7 +458,13 @@ def qgemm_packed_path(path: int) -> None:
     _lib.call("im_qgemm_packed_path", int(path))
 
 
-def qgemm_packed_tune(split_override: int = 0, target_ctas: int = 592, max_split: int = 64) -> None:
+def qgemm_packed_cluster(on: bool) -> None:
+    """Split-K partials of the warp-MMA kernel summed inside a thread-block cluster (True, default) or through
+    the workspace and a global counter (False). Both give the same bits."""
+    _lib.call("im_qgemm_packed_cluster", int(bool(on)))
+
+
+def qgemm_packed_tune(split_override: int = 0, target_ctas: int = 592, max_split: int = 16) -> None:
     """The K-split policy (process-wide; changes workspace sizes)."""
     _lib.call("im_qgemm_packed_tune", split_override, target_ctas, max_split)
 

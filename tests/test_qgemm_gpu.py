@@ -421,3 +421,34 @@ def test_tensor_core_path_for_few_rows_gives_the_same_bits(cuda, m):
             kernels.qgemm_packed_path(0)
     for a, c in zip(*outs):
         assert torch.equal(a, c)
+
+
+@pytest.mark.parametrize("n,k", [(6144, 2560), (2560, 4096), (2560, 9728), (1024, 3072), (4096, 1024),
+                                 (3840, 15360), (5376, 21504), (200, 640)])
+@pytest.mark.parametrize("m", [1, 5, 17, 40])
+def test_cluster_split_k_equals_the_counter_reduction(cuda, n, k, m):
+    """The K splits of a CTA column summed inside a thread-block cluster (through distributed shared memory) give
+    the bits of the workspace-and-counter reduction, for every epilogue, with the fused RMSNorm and the sums of
+    squares, at one to several 32-row chunks."""
+    rng = np.random.default_rng(n + k + m)
+    _, _, _, _, p, x_t = packed_case(cuda, n, k, m, n + 3 * k + m)
+    res = torch.from_numpy(bf16.from_f32(rng.normal(0, 1, (m, n)).astype(np.float32)).view(np.int16)).view(
+        torch.bfloat16).to(cuda)
+    parts = 7
+    sq_in = torch.from_numpy((rng.random((parts, 64)) * 50 + 1).astype(np.float32)).to(cuda)
+    nw = torch.from_numpy(bf16.from_f32(rng.normal(1, 0.1, k).astype(np.float32)).view(np.int16)).view(
+        torch.bfloat16).to(cuda)
+    outs = {}
+    for on in (True, False):
+        kernels.qgemm_packed_cluster(on)
+        try:
+            sq = torch.full((p.tiles, 64), -1.0, dtype=torch.float32, device=cuda)
+            store = kernels.qgemm_packed(x_t, p, norm_sq=sq_in, norm_parts=parts, norm_weight=nw, sq_ld=64)
+            resid = kernels.qgemm_packed(x_t, p, epilogue="residual", residual=res.clone(), out_sq=sq, sq_ld=64)
+            glu = kernels.qgemm_packed(x_t, p, epilogue="swiglu") if n % 32 == 0 else store
+            torch.cuda.synchronize()
+            outs[on] = [t.view(torch.int16).cpu() for t in (store, resid, glu)] + [sq.cpu()]
+        finally:
+            kernels.qgemm_packed_cluster(True)
+    for a, b in zip(outs[True], outs[False]):
+        assert torch.equal(a, b)
