@@ -65,15 +65,19 @@ struct AttnArgs {
   float scale, eps;
 };
 
-template <int D, int NQ, bool FUSED>
+template <int D, int NQ, bool FUSED, int NBUF>
 struct AttnSmem {
   // new keys one CTA may hold: a query block of at most 8 vectors comes from at most 8 rows per sequence
   static constexpr int NEW = FUSED ? (NQ <= 8 ? 8 : AT_MAXNEW) : 1;
   static constexpr int QM = NQ < 16 ? 16 : NQ;  // rows of the m16 MMA tiles (rows >= nq stay zero)
+  // key blocks staged at once: with two, a 128-key split is staged whole before the kernel waits for the previous
+  // one and later blocks load while the block before them is computed (for launches of few groups, where the
+  // second buffer costs no occupancy that matters)
+  static constexpr int NB = NBUF;
   // Row strides are padded by 16 bytes so the MMA fragment loads (and ldmatrix rows) hit distinct banks.
   uint16_t qs[QM][D + 8];         // bf16 queries
-  uint32_t ks[AT_KB][D / 2 + 4];  // keys as bf16 pairs
-  uint16_t vs[AT_KB][D + 8];      // values
+  uint32_t ks[NB][AT_KB][D / 2 + 4];  // keys as bf16 pairs
+  uint16_t vs[NB][AT_KB][D + 8];      // values
   float s[NQ][AT_KB + 4];         // scores; in the merge, the splits' sums
   uint16_t ph[QM][AT_KB + 8];     // probabilities split into bf16 high and low parts: p = ph + pl
   uint16_t pl[QM][AT_KB + 8];
@@ -84,8 +88,8 @@ struct AttnSmem {
   unsigned long long tmask[NQ];
   int new_row[NEW], new_slot[NEW];
   int nnew, kv_len;
-  int page[AT_KB / 16];  // pages of the block being staged
-  int newidx[AT_KB];  // per key of the block being staged: index into nk/nv, or -1
+  int page[NB][AT_KB / 16];  // pages of the blocks being staged
+  int newidx[NB][AT_KB];  // per key of the blocks being staged: index into nk/nv, or -1
   float mw[NQ][AT_MW];  // merge: per (query vector, split) weights
   int last;
 };
@@ -110,6 +114,9 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t& r0, uint32_t& r1, uint32
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
@@ -144,12 +151,12 @@ __device__ __forceinline__ void norm_rope_vals(const float (&v)[D / 32], const u
   }
 }
 
-template <int D, int NQ, bool FUSED, int W>
-__global__ void __launch_bounds__(32 * W)
+template <int D, int NQ, bool FUSED, int W, int NB>
+__global__ void __launch_bounds__(32 * W, W == 4 ? 4 : 2)
 attn_kernel(AttnArgs a) {
   constexpr int TH = 32 * W;  // W warps
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  using Smem = AttnSmem<D, NQ, FUSED>;
+  using Smem = AttnSmem<D, NQ, FUSED, NB>;
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   if constexpr (!FUSED) {
     pdl_wait();  // q and every key were written by earlier kernels
@@ -228,17 +235,17 @@ attn_kernel(AttnArgs a) {
   int k_end = min(kv_len, k_begin + a.kpc);
 
   // stage keys [kb0, kb0 + 64): K as bf16 pairs and V; slots written by this launch come from nk/nv later
-  auto stage_old = [&](int kb0) {
+  auto stage_old = [&](int kb0, int buf) {
     if (tid < AT_KB / 16) {
       const int slot = kb0 + tid * 16;
-      sm.page[tid] = slot < k_end ? a.page_table[(size_t)prow * a.max_pages + (slot >> 4)] : 0;
+      sm.page[buf][tid] = slot < k_end ? a.page_table[(size_t)prow * a.max_pages + (slot >> 4)] : 0;
     }
     if constexpr (FUSED) {
       for (int j = tid; j < AT_KB; j += TH) {
         int idx = -1;
         for (int n = 0; n < sm.nnew; n++)
           if (sm.new_slot[n] == kb0 + j) idx = n;
-        sm.newidx[j] = idx;
+        sm.newidx[buf][j] = idx;
       }
     }
     __syncthreads();
@@ -249,29 +256,36 @@ attn_kernel(AttnArgs a) {
       const int j = i / (D / 8), c = i % (D / 8);
       const int slot = kb0 + j;
       bool skip = false;
-      if constexpr (FUSED) skip = sm.newidx[j] >= 0;  // filled from nk/nv by plain stores: no async copy here
+      if constexpr (FUSED) skip = sm.newidx[buf][j] >= 0;  // filled from nk/nv by plain stores: no async copy here
       if (!skip) {
         const bool load = slot < k_end;  // past the end: zero-filled
-        const size_t off = load ? (((size_t)sm.page[j >> 4] * a.Hkv + kvh) * 16 + (slot & 15)) * D + c * 8 : 0;
-        cp_async16(&sm.ks[j][c * 4], a.kc + off, load);
-        cp_async16(&sm.vs[j][c * 8], a.vc + off, load);
+        const size_t off = load ? (((size_t)sm.page[buf][j >> 4] * a.Hkv + kvh) * 16 + (slot & 15)) * D + c * 8 : 0;
+        cp_async16(&sm.ks[buf][j][c * 4], a.kc + off, load);
+        cp_async16(&sm.vs[buf][j][c * 8], a.vc + off, load);
       }
     }
+    cp_async_commit();
   };
-  auto fill_new = [&]() {
+  auto fill_new = [&](int buf) {
     if constexpr (FUSED) {
       for (int i = tid; i < AT_KB * (D / 8); i += TH) {
         const int j = i / (D / 8), c = i % (D / 8);
-        const int idx = sm.newidx[j];
+        const int idx = sm.newidx[buf][j];
         if (idx >= 0) {
-          *reinterpret_cast<uint4*>(&sm.ks[j][c * 4]) = *reinterpret_cast<const uint4*>(&sm.nk[idx][c * 8]);
-          *reinterpret_cast<uint4*>(&sm.vs[j][c * 8]) = *reinterpret_cast<const uint4*>(&sm.nv[idx][c * 8]);
+          *reinterpret_cast<uint4*>(&sm.ks[buf][j][c * 4]) = *reinterpret_cast<const uint4*>(&sm.nk[idx][c * 8]);
+          *reinterpret_cast<uint4*>(&sm.vs[buf][j][c * 8]) = *reinterpret_cast<const uint4*>(&sm.nv[idx][c * 8]);
         }
       }
     }
   };
 
-  if (any) stage_old(k_begin);
+  // the split's first block (and its second, with two buffers) before the wait: no earlier kernel writes them
+  bool second = false;
+  if (any) {
+    stage_old(k_begin, 0);
+    second = Smem::NB > 1 && k_begin + AT_KB < k_end;
+    if (second) stage_old(k_begin + AT_KB, Smem::NB - 1);
+  }
 
   if constexpr (FUSED) {
     pdl_wait();
@@ -330,7 +344,8 @@ attn_kernel(AttnArgs a) {
         }
       }
       __syncthreads();
-      fill_new();
+      fill_new(0);
+      if (second) fill_new(Smem::NB - 1);
     }
   } else {
     for (int i = tid; i < nq * D; i += TH) {
@@ -375,16 +390,36 @@ attn_kernel(AttnArgs a) {
         for (int nt = 0; nt < NTO; nt++)
 #pragma unroll
           for (int e = 0; e < 4; e++) o_acc[mt][nt][e] = 0.f;
-      stage_old(k_begin);
-      fill_new();
+      stage_old(k_begin, 0);
+      second = Smem::NB > 1 && k_begin + AT_KB < k_end;
+      if (second) stage_old(k_begin + AT_KB, Smem::NB - 1);
+      fill_new(0);
+      if (second) fill_new(Smem::NB - 1);
     }
-    for (int kb0 = k_begin; kb0 < k_end; kb0 += AT_KB) {
-      if (kb0 != k_begin) {
+    int bi = 0;
+    for (int kb0 = k_begin; kb0 < k_end; kb0 += AT_KB, bi++) {
+      const int buf = bi % Smem::NB;
+      bool ahead = false;  // the next block's copies are in flight behind this block's
+      if (Smem::NB > 1) {
+        if (bi == 0) {
+          ahead = second;
+        } else {
+          __syncthreads();  // block bi - 1 is consumed: its buffer takes block bi + 1
+          if (kb0 + AT_KB < k_end) {
+            stage_old(kb0 + AT_KB, (bi + 1) % Smem::NB);
+            fill_new((bi + 1) % Smem::NB);
+            ahead = true;
+          }
+        }
+      } else if (bi > 0) {
         __syncthreads();  // the previous block's K/V and probabilities are consumed
-        stage_old(kb0);
-        fill_new();
+        stage_old(kb0, 0);
+        fill_new(0);
       }
-      cp_async_wait_all();
+      if (ahead)
+        cp_async_wait<1>();
+      else
+        cp_async_wait<0>();
       __syncthreads();
       // scores
       {
@@ -401,8 +436,8 @@ attn_kernel(AttnArgs a) {
           uint32_t bk[NTK][2];
 #pragma unroll
           for (int nt = 0; nt < NTK; nt++) {
-            bk[nt][0] = sm.ks[n0 + nt * 8 + g][kk * 8 + t];
-            bk[nt][1] = sm.ks[n0 + nt * 8 + g][kk * 8 + 4 + t];
+            bk[nt][0] = sm.ks[buf][n0 + nt * 8 + g][kk * 8 + t];
+            bk[nt][1] = sm.ks[buf][n0 + nt * 8 + g][kk * 8 + 4 + t];
           }
 #pragma unroll
           for (int mt = 0; mt < MT; mt++) {
@@ -492,7 +527,7 @@ attn_kernel(AttnArgs a) {
         for (int nt = 0; nt < NTO; nt += 2) {
           const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
           const int d0 = warp * DW + nt * 8 + (lane >> 4) * 8;
-          ldsm_x4_trans(bv[nt][0], bv[nt][1], bv[nt + 1][0], bv[nt + 1][1], &sm.vs[key][d0]);
+          ldsm_x4_trans(bv[nt][0], bv[nt][1], bv[nt + 1][0], bv[nt + 1][1], &sm.vs[buf][key][d0]);
         }
 #pragma unroll
         for (int mt = 0; mt < MT; mt++) {
@@ -542,96 +577,84 @@ attn_kernel(AttnArgs a) {
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
-  // merge the splits in split order. Pass 1: per query vector, the max over splits and the split weights
-  // w_s = exp(m_s - max) (one warp per vector, lane per split); pass 2: every thread owns (vector, 4 dims)
-  // and sums its splits in order with all loads issued first.
+  // merge the splits in split order, in one pass: every thread owns (query vector, 4 dims), loads every split's
+  // max, sum and 4 accumulators together, and forms the split weights w_s = exp(m_s - max) itself; the
+  // denominator sum_s l_s w_s and the numerator sum_s o_s w_s are both summed in split order
   int used = a.nsplit;
   while (used > 1 && (used - 1) * a.kpc >= kv_len) used--;
-  if (nq == 0) {
-    if (tid == 0) a.counters[group] = 0u;
-    return;
-  }
-  float* L = &sm.alpha[0];  // reuse: per-vector denominators
-  if (used <= AT_MW) {
-    // every (vector, split) max and sum loaded at once into shared memory (mw: maxima then weights, s: sums)
-    for (int job = tid; job < nq * used; job += TH) {
-      const int i = job / used, sp = job % used;
-      const float* p = a.part + ((group * a.nsplit + sp) * NQ + i) * (D + AT_PAD);
-      sm.mw[i][sp] = __ldcg(p + D);
-      sm.s[i][sp] = __ldcg(p + D + 1);
-    }
-    __syncthreads();
-  }
-  for (int i = warp; i < nq; i += TH / 32) {
-    auto m_of = [&](int sp) {
-      return used <= AT_MW ? sm.mw[i][sp] : __ldcg(a.part + ((group * a.nsplit + sp) * NQ + i) * (D + AT_PAD) + D);
-    };
-    auto l_of = [&](int sp) {
-      return used <= AT_MW ? sm.s[i][sp] : __ldcg(a.part + ((group * a.nsplit + sp) * NQ + i) * (D + AT_PAD) + D + 1);
-    };
-    float mx = -INFINITY;
-    for (int s0 = lane; s0 < used; s0 += 32) mx = fmaxf(mx, m_of(s0));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float lsum = 0.f;
-    // weights of 32 splits per pass (lane per split); the denominator adds them in split order
-    for (int s0 = 0; s0 < used; s0 += 32) {
-      const int sp = s0 + lane;
-      float w = 0.f, ls = 0.f;
-      if (sp < used) {
-        const float ms = m_of(sp);
-        ls = l_of(sp);
-        w = (ms == -INFINITY || mx == -INFINITY) ? 0.f : expf(ms - mx);
-      }
-      __syncwarp();
-      if (sp < AT_MW) sm.mw[i][sp] = w;
-      for (int t = 0; t < 32 && s0 + t < used; t++) {
-        const float wt = __shfl_sync(0xffffffffu, w, t), lt = __shfl_sync(0xffffffffu, ls, t);
-        lsum = fmaf(lt, wt, lsum);
-      }
-    }
-    if (lane == 0) {
-      L[i] = lsum;
-      sm.m[i] = mx;
-    }
-  }
-  __syncthreads();
   constexpr int C4 = D / 4;
+  constexpr int SB = 8;  // splits whose loads are in flight together
   for (int job = tid; job < nq * C4; job += TH) {
     const int i = job / C4, d4 = (job % C4) * 4;
-    const float mx = sm.m[i];
+    const float* base = a.part + (group * a.nsplit * NQ + i) * (size_t)(D + AT_PAD);
+    const size_t sstride = (size_t)NQ * (D + AT_PAD);
+    float mx = -INFINITY, lsum = 0.f;
     float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s0 = 0; s0 < used; s0 += 8) {
-      float4 v[8];
-      float ms[8];
+    if (used <= SB) {  // every split's loads in flight at once: one round trip
+      float4 v[SB];
+      float ms[SB], ls[SB];
 #pragma unroll
-      for (int j = 0; j < 8; j++) {
-        if (s0 + j < used) {
-          const float* p = a.part + ((group * a.nsplit + s0 + j) * NQ + i) * (D + AT_PAD);
+      for (int j = 0; j < SB; j++) {
+        if (j < used) {
+          const float* p = base + j * sstride;
           v[j] = __ldcg(reinterpret_cast<const float4*>(p + d4));
-          ms[j] = s0 + j < AT_MW ? 0.f : __ldcg(p + D);
+          ms[j] = __ldcg(p + D);
+          ls[j] = __ldcg(p + D + 1);
         }
       }
 #pragma unroll
-      for (int j = 0; j < 8; j++) {
-        if (s0 + j < used) {
-          const int s = s0 + j;
-          const float w = s < AT_MW ? sm.mw[i][s]
-                                    : ((ms[j] == -INFINITY || mx == -INFINITY) ? 0.f : expf(ms[j] - mx));
+      for (int j = 0; j < SB; j++)
+        if (j < used) mx = fmaxf(mx, ms[j]);
+#pragma unroll
+      for (int j = 0; j < SB; j++) {
+        if (j < used) {
+          const float w = (ms[j] == -INFINITY || mx == -INFINITY) ? 0.f : expf(ms[j] - mx);
+          lsum = fmaf(ls[j], w, lsum);
           o.x = fmaf(v[j].x, w, o.x);
           o.y = fmaf(v[j].y, w, o.y);
           o.z = fmaf(v[j].z, w, o.z);
           o.w = fmaf(v[j].w, w, o.w);
         }
       }
+    } else {
+      for (int s0 = 0; s0 < used; s0 += SB) {
+        float ms[SB];
+#pragma unroll
+        for (int j = 0; j < SB; j++) ms[j] = s0 + j < used ? __ldcg(base + (s0 + j) * sstride + D) : -INFINITY;
+#pragma unroll
+        for (int j = 0; j < SB; j++) mx = fmaxf(mx, ms[j]);
+      }
+      for (int s0 = 0; s0 < used; s0 += SB) {
+        float4 v[SB];
+        float ms[SB], ls[SB];
+#pragma unroll
+        for (int j = 0; j < SB; j++) {
+          if (s0 + j < used) {
+            const float* p = base + (s0 + j) * sstride;
+            v[j] = __ldcg(reinterpret_cast<const float4*>(p + d4));
+            ms[j] = __ldcg(p + D);
+            ls[j] = __ldcg(p + D + 1);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < SB; j++) {
+          if (s0 + j < used) {
+            const float w = (ms[j] == -INFINITY || mx == -INFINITY) ? 0.f : expf(ms[j] - mx);
+            lsum = fmaf(ls[j], w, lsum);
+            o.x = fmaf(v[j].x, w, o.x);
+            o.y = fmaf(v[j].y, w, o.y);
+            o.z = fmaf(v[j].z, w, o.z);
+            o.w = fmaf(v[j].w, w, o.w);
+          }
+        }
+      }
     }
-    const float den = L[i];
     const int row = r0 + (q0 + i) / G, head = kvh * G + (q0 + i) % G;
     uint16_t* dst = a.out + ((size_t)row * a.Hq + head) * D + d4;
-    dst[0] = to_bf(den > 0.f ? __fdiv_rn(o.x, den) : 0.f);
-    dst[1] = to_bf(den > 0.f ? __fdiv_rn(o.y, den) : 0.f);
-    dst[2] = to_bf(den > 0.f ? __fdiv_rn(o.z, den) : 0.f);
-    dst[3] = to_bf(den > 0.f ? __fdiv_rn(o.w, den) : 0.f);
+    dst[0] = to_bf(lsum > 0.f ? __fdiv_rn(o.x, lsum) : 0.f);
+    dst[1] = to_bf(lsum > 0.f ? __fdiv_rn(o.y, lsum) : 0.f);
+    dst[2] = to_bf(lsum > 0.f ? __fdiv_rn(o.z, lsum) : 0.f);
+    dst[3] = to_bf(lsum > 0.f ? __fdiv_rn(o.w, lsum) : 0.f);
   }
   if (tid == 0) a.counters[group] = 0u;
 }
@@ -641,19 +664,19 @@ attn_kernel(AttnArgs a) {
 // way whichever CTA walks it.
 static int g_attn_waves = 2;
 
-template <int D, int NQ, bool FUSED, int W>
+template <int D, int NQ, bool FUSED, int W, int NB>
 static int launch_attn(const AttnArgs& args, int B, cudaStream_t st) {
-  const size_t smem = sizeof(AttnSmem<D, NQ, FUSED>);
+  const size_t smem = sizeof(AttnSmem<D, NQ, FUSED, NB>);
   static bool configured = false;  // per instantiation
   static int resident = 1, sms = 148;
   if (!configured) {
     cudaError_t e =
-        cudaFuncSetAttribute(attn_kernel<D, NQ, FUSED, W>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(attn_kernel<D, NQ, FUSED, W, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int dev = 0;
     if (e == cudaSuccess) e = cudaGetDevice(&dev);
     if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (e == cudaSuccess)
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, attn_kernel<D, NQ, FUSED, W>, 32 * W, smem);
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, attn_kernel<D, NQ, FUSED, W, NB>, 32 * W, smem);
     if (e != cudaSuccess) {
       set_error("attention: cannot configure the kernel for %zu bytes of shared memory: %s", smem,
                 cudaGetErrorString(e));
@@ -666,7 +689,7 @@ static int launch_attn(const AttnArgs& args, int B, cudaStream_t st) {
   const long long want = ((long long)sms * resident * g_attn_waves + groups - 1) / groups;
   const int per_group = (int)(want < 1 ? 1 : (want > args.nsplit ? args.nsplit : want));
   dim3 grid(per_group, args.Hkv, B * args.qblocks);
-  return launch("attn_kernel", attn_kernel<D, NQ, FUSED, W>, grid, dim3(32 * W), smem, st, args);
+  return launch("attn_kernel", attn_kernel<D, NQ, FUSED, W, NB>, grid, dim3(32 * W), smem, st, args);
 }
 
 template <bool FUSED>
@@ -675,12 +698,13 @@ static int dispatch_attn(const AttnArgs& args, int64_t D, int nq, int B, cudaStr
   // for small blocks of head_dim 128 when the (sequence, kv head) groups are fewer than the SMs (one sequence:
   // each split's chain is shorter); 4 warps for small blocks of large batches (more CTAs per SM). Every score and
   // output element is computed the same way whatever the warp count.
+  const long long groups = (long long)B * args.Hkv * args.qblocks;
   if (D == 128) {
-    if (nq != 8) return launch_attn<128, 32, FUSED, 8>(args, B, st);
-    const long long groups = (long long)B * args.Hkv * args.qblocks;
-    return groups < 148 ? launch_attn<128, 8, FUSED, 8>(args, B, st) : launch_attn<128, 8, FUSED, 4>(args, B, st);
+    if (nq != 8)
+      return groups < 148 ? launch_attn<128, 32, FUSED, 8, 2>(args, B, st) : launch_attn<128, 32, FUSED, 8, 1>(args, B, st);
+    return groups < 148 ? launch_attn<128, 8, FUSED, 8, 2>(args, B, st) : launch_attn<128, 8, FUSED, 4, 1>(args, B, st);
   }
-  return nq == 8 ? launch_attn<256, 8, FUSED, 4>(args, B, st) : launch_attn<256, 32, FUSED, 8>(args, B, st);
+  return nq == 8 ? launch_attn<256, 8, FUSED, 4, 1>(args, B, st) : launch_attn<256, 32, FUSED, 8, 1>(args, B, st);
 }
 
 static void attn_geometry(int64_t rows_per_seq, int64_t G, int* nq, int* qblocks) {
