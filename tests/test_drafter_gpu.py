@@ -1,4 +1,4 @@
-"""The reference's host Drafter (ironmule_b200.draft_model, the restatement of ironmule/draft_model.py) driving a
+"""The host Drafter (ironmule_b200.draft_model, the drop-in for ironmule/draft_model.py) driving a
 draft model on the B200 through DeviceDraftEngine: the top token and its probability per logits row against the
 host's scan of the same logits (ironmule/ggml_engine.py:669-683), drafts equal to the draft model's own greedy
 continuation (also after a rejection trims its cache), and the host speculative loop with the confidence-stopped
