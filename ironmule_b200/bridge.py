@@ -11,6 +11,9 @@ one, as the reference's `take` does (ggml_engine.py:1037-1056):
   "length" at its limit.
 A request that ends frees its slot at once (`SpecDecoder.stop_slot`: with a page pool its K/V stay cached for
 later requests with the same prefix). The decoder's round runs as one CUDA graph, captured after the first round.
+Requests are checked when they arrive: invalid ones among those `serve` is called with raise before any slot starts;
+an invalid one that `admit` hands over ends at once as "invalid" (its message in `error`) while the others run on. If
+anything raises while requests run, their slots are stopped before the exception leaves `serve`.
 """
 from __future__ import annotations
 
@@ -35,6 +38,16 @@ class Job:
     reused: int = 0  # prompt tokens whose K/V were linked from the page pool instead of computed
     first_ns: int = 0
     finished_ns: int = 0
+    error: str | None = None
+
+
+def _invalid(job: Job, limit: int) -> str | None:
+    """Why the decoder cannot serve the request, or None."""
+    if len(job.ids) < 2 or job.limit < 1:
+        return "a request needs at least two prompt tokens and a positive limit"
+    if len(job.ids) + job.limit > limit:
+        return f"{len(job.ids) + job.limit} tokens do not fit a {limit}-token sequence"
+    return None
 
 
 @dataclass
@@ -54,10 +67,23 @@ def serve(dec, jobs: list[Job], admit: Callable[[int], list[Job]] | None = None,
     """Serve `jobs`, and every job `admit(free slots)` hands over while they run, on `dec` (a `SpecDecoder` or
     anything with its `batch`, `start_slots`, `stop_slot`, `step`, `capture`, `graph`, `device` and
     `request_limit`); returns them all in arrival order."""
+    limit = dec.request_limit()
+    for job in jobs:
+        why = _invalid(job, limit)
+        if why is not None:
+            raise ValueError(why)
     served, pending = list(jobs), list(jobs)
     active: dict[int, Job] = {}
     rounds = 0
-    limit = dec.request_limit()
+
+    def arrive(more: list[Job]) -> None:
+        served.extend(more)
+        for job in more:
+            why = _invalid(job, limit)
+            if why is None:
+                pending.append(job)
+            else:
+                job.reason, job.error, job.finished_ns = "invalid", why, time.monotonic_ns()
 
     def finish(slot: int, job: Job, reason: str) -> None:
         job.reason, job.finished_ns = reason, time.monotonic_ns()
@@ -81,12 +107,19 @@ def serve(dec, jobs: list[Job], admit: Callable[[int], list[Job]] | None = None,
             return True
         return False
 
+    try:
+        return _loop(dec, admit, active, pending, arrive, take, served, rounds)
+    except BaseException:
+        for b in list(active):
+            dec.stop_slot(b)
+        raise
+
+
+def _loop(dec, admit, active, pending, arrive, take, served, rounds) -> list[Job]:
     while True:
         free = [b for b in range(dec.batch) if b not in active]
         if admit is not None and free:
-            more = admit(len(free))
-            served.extend(more)
-            pending.extend(more)
+            arrive(admit(len(free)))
         fresh = []
         for job in sorted(pending, key=lambda j: len(j.ids)):
             if job.cancelled is not None and job.cancelled():
@@ -95,10 +128,6 @@ def serve(dec, jobs: list[Job], admit: Callable[[int], list[Job]] | None = None,
                 continue
             if not free:
                 break
-            if len(job.ids) < 2 or job.limit < 1:
-                raise ValueError("a request needs at least two prompt tokens and a positive limit")
-            if len(job.ids) + job.limit > limit:
-                raise ValueError(f"{len(job.ids) + job.limit} tokens do not fit a {limit}-token sequence")
             pending.remove(job)
             fresh.append((free.pop(0), job))
         if fresh:
@@ -113,8 +142,7 @@ def serve(dec, jobs: list[Job], admit: Callable[[int], list[Job]] | None = None,
             if admit is not None:
                 more = admit(dec.batch)
                 if more:
-                    served.extend(more)
-                    pending.extend(more)
+                    arrive(more)
                     continue
             return served
         if dec.graph is None and rounds == 1:
@@ -189,7 +217,7 @@ class DeviceBridge:
 
         eos = set(self._eos)
         served = serve(self._dec, jobs, admit=take if admit is not None else None, eog=lambda t: t in eos)
-        reasons = {"eos": "stop", "length": "length", "cancelled": "cancelled"}
+        reasons = {"eos": "stop", "length": "length", "cancelled": "cancelled", "invalid": "error"}
         results = []
         for job in served:
             kept = [t for t in job.tokens if t not in eos]
@@ -201,7 +229,8 @@ class DeviceBridge:
                                         token_count=len(job.tokens),
                                         metrics={"reused_prompt_tokens": job.reused,
                                                  "first_token_ns": job.first_ns, "finished_ns": job.finished_ns},
-                                        metadata={**self.metadata(), **self.counters()}))
+                                        metadata={**self.metadata(), **self.counters(),
+                                                  **({"error": job.error} if job.error else {})}))
         return results
 
     def close(self) -> None:

@@ -7,7 +7,8 @@ Format (GGUF v2/v3, little-endian): magic "GGUF", version u32, tensor count u64,
 (string key, u32 value type, value); tensor infos as (string name, u32 dimension count, u64 dimensions innermost
 first, u32 ggml type, u64 offset into the data section); the data section starts at the next multiple of
 `general.alignment` (32 by default). A string is a u64 length and its bytes; an array a u32 element type, a u64 count
-and the elements.
+and the elements. A tensor of a ggml type this reader has no block size for (the IQ types, integer tensors, ...) stays
+in the table with an unknown size: the file opens, and only asking for that tensor's bytes raises.
 """
 from __future__ import annotations
 
@@ -39,7 +40,7 @@ class GGUFTensor:
     type: int
     dims: tuple[int, ...]  # innermost first, as the file stores them
     offset: int            # absolute byte offset of the data in the file
-    n_bytes: int
+    n_bytes: int | None    # None: a ggml type without a known block size
 
     @property
     def shape(self) -> tuple[int, ...]:
@@ -111,7 +112,8 @@ class GGUFFile:
         self.tensors: dict[str, GGUFTensor] = {}
         for name, ttype, dims, offset in infos:
             if ttype not in TYPES:
-                raise GGUFError(f"{name}: ggml type {ttype} is not read here")
+                self.tensors[name] = GGUFTensor(name, ttype, dims, data + offset, None)
+                continue
             per, size = TYPES[ttype]
             count = int(np.prod(dims, dtype=np.int64)) if dims else 1
             if dims and dims[0] % per:
@@ -125,6 +127,8 @@ class GGUFFile:
     def raw(self, name: str) -> np.ndarray:
         """The tensor's bytes (a read-only view of the file)."""
         t = self.tensors[name]
+        if t.n_bytes is None:
+            raise GGUFError(f"{name}: ggml type {t.type} is not read here")
         return self._map[t.offset:t.offset + t.n_bytes]
 
     def array(self, name: str) -> np.ndarray:

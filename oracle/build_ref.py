@@ -29,7 +29,8 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-REF = Path(os.environ.get("IRONMULE_REFERENCE", "/root/reference")) / "ironmule"
+# the IronMule checkout: $IRONMULE_REFERENCE, else a directory named "reference" beside this repository
+REF = Path(os.environ.get("IRONMULE_REFERENCE", HERE.parents[1] / "reference")) / "ironmule"
 
 
 def _module_constants(path: Path) -> tuple[dict, ast.Module]:

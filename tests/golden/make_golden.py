@@ -1,6 +1,7 @@
 """Generates the committed golden fixtures in tests/golden/ from the reference itself.
 
-Run in a container that holds the reference tree (default /root/reference, or $IRONMULE_REFERENCE):
+Run where the reference tree is checked out ($IRONMULE_REFERENCE, else a directory named "reference" beside
+this repository):
 
     python tests/golden/make_golden.py
 
@@ -28,7 +29,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("IRONMULE_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("IRONMULE_REFERENCE", REPO.parent / "reference"))
 sys.path.insert(0, str(REPO))
 
 QMV_CASES = [

@@ -186,3 +186,36 @@ def test_serve_passes_device_prompts():
     dec.start_slots = spy
     bridge.serve(dec, [bridge.Job([4, 5, 6], 2)])
     assert seen[0].dtype == torch.int32 and seen[0].tolist() == [4, 5, 6]
+
+
+def test_an_invalid_admitted_request_ends_alone():
+    """A request admitted while others run that cannot be served (one prompt token, or too long) ends at once with
+    an error; the running requests finish normally."""
+    dec = FakeDecoder(batch=2, limit=60)
+    ps = prompts(2, seed=11)
+    handed = []
+
+    def admit(free):
+        if handed:
+            return []
+        handed.append(free)
+        return [([7], 4, None), ([1] * 50, 20, None)]
+
+    res = bridge.DeviceBridge(dec).generate_many(ps, 6, admit=admit)
+    assert [r.finish_reason for r in res] == ["length", "length", "error", "error"]
+    assert res[2].token_count == 0 and "two prompt tokens" in res[2].metadata["error"]
+    assert "do not fit" in res[3].metadata["error"]
+    assert res[0].tokens == expected(ps[0], 6) and res[1].tokens == expected(ps[1], 6)
+    assert not any(dec.running)
+
+
+def test_an_exception_while_serving_stops_the_running_slots():
+    dec = FakeDecoder(batch=2)
+    ps = prompts(2, seed=12)
+
+    def boom(token):
+        raise RuntimeError("the client went away")
+
+    with pytest.raises(RuntimeError):
+        bridge.serve(dec, [bridge.Job(ps[0], 20, emit=boom), bridge.Job(ps[1], 20)])
+    assert not any(dec.running) and sorted(dec.stops) == [0, 1]

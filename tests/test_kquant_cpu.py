@@ -129,6 +129,24 @@ def _gguf_bytes(version, kvs, tensors, alignment=None):
     return out
 
 
+def test_a_tensor_of_an_unknown_type_does_not_refuse_the_file(tmp_path):
+    """An IQ4_XS tensor (ggml type 23: 256-value blocks of 136 bytes, no block size here) beside a Q4_K matrix: the
+    file opens with both in its table; the Q4_K bytes read, and only asking for the IQ4_XS tensor's bytes raises."""
+    rng = np.random.default_rng(4)
+    q4k = rng.integers(0, 256, 2 * 144, dtype=np.uint8).tobytes()
+    iq4 = rng.integers(0, 256, 3 * 136, dtype=np.uint8).tobytes()
+    path = tmp_path / "mixed.gguf"
+    path.write_bytes(_gguf_bytes(3, [("general.architecture", 8, "qwen3")],
+                                 [("blk.0.ffn_down.weight", (256, 3), 23, iq4), ("blk.0.attn_q.weight", (256, 2), 12, q4k)]))
+    f = gguf.GGUFFile(path)
+    assert set(f.tensors) == {"blk.0.ffn_down.weight", "blk.0.attn_q.weight"}
+    assert f.tensors["blk.0.ffn_down.weight"].n_bytes is None
+    assert bytes(f.raw("blk.0.attn_q.weight")) == q4k
+    for read in (f.raw, f.array, lambda name: gguf.kquant_linear(f, name, device="cpu")):
+        with pytest.raises(gguf.GGUFError, match="not read here"):
+            read("blk.0.ffn_down.weight")
+
+
 def test_reader_alignment_v2_arrays_and_bf16(tmp_path):
     bf = (np.array([1.5, -2.0, 0.25], dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16).tobytes()
     q4 = kq.random_blocks(kq.Q4_K, 2, seed=3).tobytes()
@@ -150,7 +168,7 @@ def test_reader_refuses_malformed_tables(tmp_path):
     bad_type = tmp_path / "t.gguf"
     bad_type.write_bytes(_gguf_bytes(3, [], [("w", (256,), 99, bytes(8))]))
     with pytest.raises(gguf.GGUFError, match="type 99"):
-        gguf.GGUFFile(bad_type)
+        gguf.GGUFFile(bad_type).raw("w")  # the file opens; the tensor's bytes are refused
     ragged = tmp_path / "r.gguf"
     ragged.write_bytes(_gguf_bytes(3, [], [("w", (100, 2), gguf.Q4_K, bytes(288))]))
     with pytest.raises(gguf.GGUFError, match="whole number of blocks"):
