@@ -58,6 +58,7 @@ def parse():
                     default="spec_decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-tp", action="store_true", help="default workload: skip the tensor-parallel config-5a record")
     ap.add_argument("--rows", type=int, default=0,
                     help="verify_step: activation rows of the qGEMM (default 5); attention: rows per sequence (5)")
     ap.add_argument("--attn-case", choices=["config3-verify", "config3-draft", "config2-draft"],
@@ -372,6 +373,10 @@ def run_spec_decode(args, world: int, rank: int, local: int) -> None:
                        f"each round's tokens copied to pinned host memory and handed to the caller",
                "rounds": rounds}
 
+    tp = None
+    if not args.no_tp:
+        tp = tp_record(world, rank, local)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         n = cores()
@@ -394,7 +399,7 @@ def run_spec_decode(args, world: int, rank: int, local: int) -> None:
                        "accepted_per_round": round(accepted / args.steps, 4),
                        "round_weight_bytes": round_bytes,
                        "round_hbm_frac": round(round_bytes / (max_ms / args.steps / 1000) / 1e9 / pk["hbm_gbs"], 4)},
-            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "tp": tp,
             "gpu_launches": dec.launches_per_round() * args.steps,
             "peak_source": pk["source"]}
         print(json.dumps(line), flush=True)
@@ -640,6 +645,87 @@ def run_kquant(args, world: int, rank: int, local: int) -> None:
         print(json.dumps(line), flush=True)
 
 
+TP_SEQS, TP_PROMPT, TP_CTX = 64, 512, 512 + 256
+
+
+def tp_decoder(device, world: int, rank: int, group):
+    """BASELINE config 5a: Gemma-3-27B shapes tensor-parallel over the `world` ranks of `group` (NCCL all-reduce
+    after o and down, the vocabulary-sharded head all-gathered), a replicated Gemma-3-1B-shaped draft, greedy,
+    k = 4, 64 sequences of 512-token prompts (the same sequences on every rank: one job)."""
+    import torch
+
+    from ironmule_b200.engine import PRESETS, QuantModel, SpecDecoder
+
+    b = TP_SEQS
+    gen = torch.Generator().manual_seed(0)
+    target = QuantModel(PRESETS["gemma3-27b"], device, seed=0, max_ctx=TP_CTX, max_seqs=b, max_rows=b * (K_DRAFTS + 1),
+                        max_logit_rows=b * (K_DRAFTS + 1), tp=world, rank=rank, group=group)
+    draft = QuantModel(PRESETS["gemma3-1b"], device, seed=1, max_ctx=TP_CTX, max_seqs=b, max_rows=2 * b,
+                       max_logit_rows=2 * b)
+    dec = SpecDecoder(target, draft, k=K_DRAFTS, batch=b)
+    prompts = [torch.randint(0, target.cfg.vocab, (TP_PROMPT,), generator=gen, dtype=torch.int32) for _ in range(b)]
+    return target, draft, dec, prompts
+
+
+def tp_record(world: int, rank: int, local: int, steps: int = 5, warmup: int = 2) -> dict:
+    """Config 5a at TP = world beside the replicas line: tokens/s and ms per round from graph-replayed rounds (CUDA
+    events, max over ranks), and the collectives' share of a round, from one eager round with CUDA events around
+    each NCCL call (all-reduces after o and down, the head's all-gather), against that eager round's time."""
+    import gc
+
+    import torch
+
+    device = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+        group = dist.group.WORLD
+    target, draft, dec, prompts = tp_decoder(device, world, rank, group)
+    try:
+        dec.start([p.to(device) for p in prompts], max_new=TP_CTX - TP_PROMPT - dec.reserve - 8)
+        dec.round()
+        torch.cuda.synchronize()
+        dec.capture()
+        dec.run_rounds(warmup)
+        torch.cuda.synchronize()
+        before = dec.read_stats()
+        barrier(world)
+        stream = torch.cuda.current_stream(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dec.run_rounds(steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = reduce_max(e0.elapsed_time(e1), world) / steps
+        tokens = dec.read_stats().tokens - before.tokens
+        dec.graph = None  # a graph holding NCCL calls goes before anything else touches the group
+        target.collective_events = []
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        dec.round()
+        g1.record(stream)
+        torch.cuda.synchronize()
+        coll_ms = sum(a.elapsed_time(b) for a, b in target.collective_events)
+        calls = len(target.collective_events)
+        eager_ms = g0.elapsed_time(g1)
+        target.collective_events = None
+        coll_ms, eager_ms = reduce_max(coll_ms, world), reduce_max(eager_ms, world)
+        return {"workload": "config 5a: Gemma-3-27B shapes (4-bit) tensor-parallel, Gemma-3-1B-shaped draft replicated, "
+                            f"greedy, k=4, {TP_SEQS} sequences, {TP_PROMPT}-token prompts",
+                "tp": world, "value": round(tokens / (ms * steps / 1000), 2), "unit": "tokens/s",
+                "ms_per_round": round(ms, 3), "steps": steps, "warmup": warmup, "scaling": "strong",
+                "accepted_per_round": round((dec.read_stats().accepted - before.accepted) / steps, 3),
+                "collectives_per_round": calls, "collective_ms_eager_round": round(coll_ms, 3),
+                "eager_round_ms": round(eager_ms, 3),
+                "collective_share": round(coll_ms / eager_ms, 4) if eager_ms > 0 else None}
+    finally:
+        dec.graph = None
+        del dec, target, draft
+        gc.collect()
+        torch.cuda.empty_cache()
+
+
 def run_rounds_workload(args, world: int, rank: int, local: int, kind: str) -> None:
     """Config 3 (stochastic, batched) or config 4 (tree) rounds: timed like the default workload."""
     import torch
@@ -655,14 +741,8 @@ def run_rounds_workload(args, world: int, rank: int, local: int, kind: str) -> N
         import torch.distributed as dist
         tp_group = dist.group.WORLD
     if kind == "tp":
-        b, ctx = 64, 512 + 256
-        gen = torch.Generator().manual_seed(0)  # the same sequences on every rank: one tensor-parallel job
-        target = QuantModel(PRESETS["gemma3-27b"], device, seed=0, max_ctx=ctx, max_seqs=b, max_rows=b * (K_DRAFTS + 1),
-                            max_logit_rows=b * (K_DRAFTS + 1), tp=world, rank=rank, group=tp_group)
-        draft = QuantModel(PRESETS["gemma3-1b"], device, seed=1, max_ctx=ctx, max_seqs=b, max_rows=2 * b,
-                           max_logit_rows=2 * b)
-        dec = SpecDecoder(target, draft, k=K_DRAFTS, batch=b)
-        prompts = [torch.randint(0, target.cfg.vocab, (512,), generator=gen, dtype=torch.int32) for _ in range(b)]
+        ctx = TP_CTX
+        target, draft, dec, prompts = tp_decoder(device, world, rank, tp_group)
         round_bytes = K_DRAFTS * draft.cfg.weight_bytes() + target.cfg.weight_bytes() // world
         workload = (f"BASELINE config 5a: Gemma-3-27B shapes (4-bit) tensor-parallel over {world} GPU(s), NCCL "
                     "all-reduce after o and down, vocabulary-sharded head all-gathered; replicated Gemma-3-1B-shaped "

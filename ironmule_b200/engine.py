@@ -402,13 +402,34 @@ class QuantModel:
                              norm_weight=self.final_norm, eps=c.eps, gemma_norm=gemma, sq_ld=self.sq_ld, ws=ws)
         import torch.distributed as dist
         gathered = self.logits_gather[:self.tp * lr * vl]
-        dist.all_gather_into_tensor(gathered, self.logits_local[:lr], group=self.group)
+        with self._timed_collective():
+            dist.all_gather_into_tensor(gathered, self.logits_local[:lr], group=self.group)
         self.logits[:lr].view(lr, self.tp, vl).copy_(gathered.view(self.tp, lr, vl).permute(1, 0, 2))
         return self.logits[:lr]
 
     def _all_reduce(self, t: torch.Tensor) -> None:
         import torch.distributed as dist
-        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+        with self._timed_collective():
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+
+    def _timed_collective(self):
+        """CUDA events around a collective when `collective_events` is a list (an eager, measured forward): the
+        tensor-parallel bench sums their durations into the collectives' share of a round."""
+        import contextlib
+
+        events = getattr(self, "collective_events", None)
+        if events is None:
+            return contextlib.nullcontext()
+
+        @contextlib.contextmanager
+        def timed():
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            yield
+            end.record()
+            events.append((start, end))
+
+        return timed()
 
     # ---- eager helpers (prefill, plain decode, tests) -----------------------------------------------------
     def _meta(self, tokens: torch.Tensor, positions: list[int], seq: int) -> RowMeta:
