@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["spec_decode", "verify_step", "qgemm_pass", "stochastic", "tree", "tp",
-                                           "attention", "kquant"],
+                                           "attention", "kquant", "small_kernels"],
                     default="spec_decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -426,6 +426,142 @@ def run_qgemm_pass(args, world: int, rank: int, local: int) -> None:
                 "config": {"workload": "verify pass qGEMMs, Qwen3-4B, M=5, graph-replayed",
                            "l2": "2.26 GB of weights per pass >> 126 MB L2"},
                 "roofline": roof, "peak_source": pk["source"]}
+        print(json.dumps(line), flush=True)
+
+
+def run_small_kernels(args, world: int, rank: int, local: int) -> None:
+    """The kernels around the projections and attention, each alone through the entry point the engine calls, at
+    the shapes of the configurations that launch them: greedy verification and the draft argmax (config 2), the
+    stochastic acceptance and draft sampling (config 3: 32 sequences, k = 4, vocabulary 151,936), the tree's top-k
+    (config 4: vocabulary 262,144) and bookkeeping, and the embedding gather. Inputs rotate over copies larger than
+    the 126 MB L2 together; each kernel is timed from graph replays with CUDA events. Algorithmic bytes: the logits
+    read once (2 B each), the embedding rows read once (0.5625 B per weight), the K/V a tree compaction moves."""
+    import torch
+
+    from ironmule_b200 import kernels
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pk = peaks()
+    gen = torch.Generator(device=device).manual_seed(0)
+    stream = torch.cuda.current_stream(device)
+    V, VG, K = 151936, 262144, K_DRAFTS
+    bf = torch.bfloat16
+    i32 = dict(dtype=torch.int32, device=device)
+
+    def logits(rows, v, copies):
+        return [(torch.randn((rows, v), generator=gen, device=device) * 2).to(bf) for _ in range(copies)]
+
+    def timed(fn, copies, reps=64):
+        for i in range(3):
+            fn(i % copies)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(reps):
+                fn(i % copies)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(max(2, args.steps // reps)):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1000 / (max(2, args.steps // reps) * reps)  # us per call
+
+    out = {}
+
+    def record(name, us, nbytes, launches, what):
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"us_per_call": round(us, 3), "algorithmic_bytes": int(nbytes), "gbs": round(gbs, 1),
+                     "frac": round(gbs / pk["hbm_gbs"], 4), "launches_per_call": launches, "what": what}
+
+    # config 2: greedy verification of 4 drafts (5 rows) and one draft row's argmax
+    ver = logits(K + 1, V, 40)
+    drafts = torch.randint(0, V, (K,), generator=gen, device=device, dtype=torch.int32)
+    tok, cnt = torch.zeros((1, K + 1), **i32), torch.zeros((1,), **i32)
+    ws_v = kernels.workspace(kernels.argmax_workspace_bytes(K + 1, V), device)
+    record("verify_greedy", timed(lambda i: kernels.verify_greedy(ver[i], drafts, b=1, k=K, drafts_ld=K, tokens=tok,
+                                                                  count=cnt, ws=ws_v), 40),
+           (K + 1) * V * 2, 1, "argmax_kernel: 5 rows x 151,936 + greedy acceptance (config 2 verify)")
+    one = logits(1, V, 200)
+    pick = torch.zeros((1,), **i32)
+    ws_1 = kernels.workspace(kernels.argmax_workspace_bytes(1, V), device)
+    record("argmax_draft_row", timed(lambda i: kernels.argmax_rows(one[i], out=pick, ws=ws_1), 200), V * 2, 1,
+           "argmax_kernel: 1 row x 151,936 (config 2 draft pick)")
+    del ver, one
+    # config 3: stochastic acceptance over 32 sequences x 5 rows and the draft sampling of 32 rows
+    b = 32
+    tl, dl = logits(b * (K + 1), V, 3), [x.view(K, b, V) for x in logits(K * b, V, 3)]
+    dr = torch.randint(0, V, (b, K + 1), generator=gen, device=device, dtype=torch.int32)
+    tok3, cnt3 = torch.zeros((b, K + 1), **i32), torch.zeros((b,), **i32)
+    ws_a = kernels.workspace(kernels.sampling_workspace_bytes(b * (2 * K + 1)), device)
+    off = torch.zeros((1,), dtype=torch.int64, device=device)
+    record("accept_stochastic", timed(lambda i: kernels.accept_stochastic(
+        tl[i], dl[i], dr[:, 1:], b=b, k=K, drafts_ld=K + 1, temperature=0.7, top_p=0.95, seed=0, offset_dev=off,
+        tokens=tok3, count=cnt3, ws=ws_a), 3), (2 * K + 1) * b * V * 2, 3,
+        "row_dist_kernel + accept_stochastic_kernel (+ residual resample): 32 x (5 target + 4 draft) rows x 151,936 "
+        "(config 3)")
+    ws_s = kernels.workspace(kernels.sampling_workspace_bytes(b), device)
+    streams = torch.arange(b, **i32)
+    smp = torch.zeros((b,), **i32)
+    record("sample_rows", timed(lambda i: kernels.sample_rows(dl[i][0], 0.7, 0.95, 0, offset_dev=off, streams=streams,
+                                                              draw=1000, out=smp, ws=ws_s), 3), b * V * 2, 2,
+           "row_dist_kernel + sample_kernel: 32 draft rows x 151,936 (config 3 draft pick)")
+    del tl, dl
+    # config 4: top-k of the draft tree's levels (8 trees, 8 parents x 2 children at the widest level)
+    rows_t = 8 * 8
+    tk = logits(rows_t, VG, 5)
+    kids = torch.zeros((rows_t * 2,), **i32)
+    ws_t = kernels.workspace(kernels.topk_workspace_bytes(rows_t, VG, 4), device)
+    record("topk_rows", timed(lambda i: kernels.topk_rows(tk[i], 2, out=kids, ws=ws_t), 5), rows_t * VG * 2, 1,
+           "topk_kernel: 64 rows x 262,144, 2 children each (config 4 tree level)")
+    del tk
+    # the embedding gather of a verify pass (Qwen3-4B table, 5 rows) and of config 3's 160 rows
+    from ironmule_b200.engine import PRESETS, QuantModel
+    tgt = QuantModel(PRESETS["qwen3-4b"], device, seed=0, max_ctx=64, max_rows=160, max_logit_rows=8)
+    ids = [torch.randint(0, V, (160,), generator=gen, device=device, dtype=torch.int32) for _ in range(16)]
+    h = torch.zeros((160, 2560), dtype=bf, device=device)
+    sq = torch.zeros((160,), dtype=torch.float32, device=device)
+    for rows in (5, 160):
+        record(f"embed_{rows}_rows", timed(lambda i: kernels.embed(ids[i], tgt.embed.w, tgt.embed.s, tgt.embed.b,
+                                                                   out=h, rows=rows, out_sq=sq), 16),
+               rows * 2560 * 9 // 16 + rows * 2560 * 2, 1, f"embed_kernel: {rows} rows of the 4-bit Qwen3-4B table")
+    del tgt
+    # config 4's tree bookkeeping: prepare, accept, compact over 8 trees of 4 x 2 x 2 (Gemma-3-12B caches)
+    branch, bt = (4, 2, 2), 8
+    nodes, layers, hkv, d, ctx = 28, 48, 8, 256, 1216
+    pages = -(-ctx // 16)
+    hist = torch.randint(0, VG, (bt, ctx), generator=gen, device=device, dtype=torch.int32)
+    n = torch.full((bt,), 1024, **i32)
+    d0t, d0p = torch.zeros((2 * bt,), **i32), torch.zeros((2 * bt,), **i32)
+    vt, vp, vs = (torch.zeros((bt * (nodes + 1),), **i32) for _ in range(3))
+    vm = torch.zeros((bt * (nodes + 1),), dtype=torch.int64, device=device)
+    tb = torch.zeros((bt,), **i32)
+    record("tree_prepare", timed(lambda i: kernels.tree_prepare(hist, n, branch, ctx, d0t, d0p, vt, vp, vs, vm, tb), 1),
+           0, 1, "tree_prepare_kernel: rows, positions, slots and ancestor masks of 8 trees (launch-bound)")
+    am = torch.randint(0, 4, (bt * (nodes + 1),), generator=gen, device=device, dtype=torch.int32)
+    vt.copy_(torch.randint(0, 4, (bt * (nodes + 1),), generator=gen, device=device, dtype=torch.int32))
+    ot, oc, acc = torch.zeros((bt, 4), **i32), torch.zeros((bt,), **i32), torch.zeros((bt * 3,), **i32)
+    record("tree_accept", timed(lambda i: kernels.tree_accept(am, vt, bt, branch, ot, oc, acc), 1), 0, 1,
+           "tree_accept_kernel: the walk down 8 trees (launch-bound)")
+    kc = torch.zeros((layers, bt * pages, hkv, 16, d), dtype=bf, device=device)
+    vc = torch.zeros_like(kc)
+    table = torch.arange(bt * pages, **i32).view(bt, pages)
+    tb.fill_(1024)
+    acc.copy_(torch.tensor([0, 4, 12] * bt, dtype=torch.int32))
+    moved = bt * 3 * layers * hkv * d * 2 * 2 * 2  # 3 accepted nodes: read + write K and V
+    record("tree_compact", timed(lambda i: kernels.tree_compact(kc, vc, table, tb, acc, 3, 3, bt), 1), moved, 1,
+           "tree_compact_kernel: 3 accepted nodes x 48 layers of K/V moved per tree, 8 trees (Gemma-3-12B)")
+    if rank == 0:
+        total_us = sum(v["us_per_call"] for v in out.values())
+        line = {"metric": "small-kernel times (acceptance, sampling, top-k, tree bookkeeping, embedding)",
+                "value": round(total_us, 3), "unit": "us (sum over the kernels, one call each)", "n_gpus": world,
+                "steps": args.steps, "warmup": 3, "ms_per_step": round(total_us / 1000, 5), "higher_is_better": False,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16 logits, int32 ids", "data": "synthetic",
+                "config": {"workload": "small kernels at the configurations' shapes", "kernels": out,
+                           "l2": "inputs rotate over copies larger than the 126 MB L2 where the data is that large"},
+                "peak_source": pk["source"]}
         print(json.dumps(line), flush=True)
 
 
@@ -845,6 +981,8 @@ def main() -> int:
             run_verify_step(args, world, rank, local)
         elif args.workload == "qgemm_pass":
             run_qgemm_pass(args, world, rank, local)
+        elif args.workload == "small_kernels":
+            run_small_kernels(args, world, rank, local)
         elif args.workload == "attention":
             run_attention(args, world, rank, local)
         elif args.workload == "kquant":
