@@ -103,22 +103,6 @@ size_t im_qgemm_workspace_bytes(int64_t M, int64_t N, int64_t K);
 int im_qgemm_set_splits(int splits);
 
 /*
- * qGEMM v3: the same product and epilogues as im_qgemm_w4g64_ex, computed by a persistent kernel (one CTA per
- * SM) whose producer warp streams 32-row x 1024-k tiles of codes into a shared-memory ring with bulk async
- * copies while 8 consumer warps run the tensor-core math; the (tile, k-chunk) units are split evenly across the
- * CTAs, a tile split across CTAs being summed in CTA order by the last of them (deterministic). K % 256 == 0,
- * M <= 32, scales/biases 4-byte aligned. `workspace` (required): >= im_qgemm_tma_workspace_bytes(M, N, K) bytes,
- * 256-byte aligned, zero-filled before first use; calls sharing it must not overlap. Every wait inside the kernel
- * is bounded (1 s); a wait that gave up leaves a non-zero word that im_qgemm_tma_status copies out (synchronous).
- * Replaces the same reference interfaces as im_qgemm_w4g64.
- */
-int im_qgemm_tma(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, const uint16_t* x, uint16_t* y,
-                 const uint16_t* residual, int64_t M, int64_t N, int64_t K, int epilogue, void* workspace,
-                 size_t workspace_bytes, void* stream);
-size_t im_qgemm_tma_workspace_bytes(int64_t M, int64_t N, int64_t K);
-int im_qgemm_tma_status(const void* workspace, uint32_t* status);
-
-/*
  * qGEMM v4 over weights repacked once into MMA-fragment order (the engine's resident format).
  * im_qgemm_pack_w4g64 converts MLX-layout w/scales/biases [N, K] into `packed` (16-byte aligned,
  * im_qgemm_packed_bytes(N, K) bytes): rows padded to 32-row tiles, one contiguous 1152-byte unit per

@@ -32,9 +32,6 @@ SIGNATURES: dict[str, tuple] = {
     "im_qgemm_w4g64_noalloc": (_INT, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _P]),
     "im_qgemm_noalloc_capacity": (_SZ, []),
     "im_qgemm_set_splits": (_INT, [_INT]),
-    "im_qgemm_tma": (_INT, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _INT, _P, _SZ, _P]),
-    "im_qgemm_tma_workspace_bytes": (_SZ, [_I64, _I64, _I64]),
-    "im_qgemm_tma_status": (_INT, [_P, _P]),
     "im_qgemm_packed_bytes": (_SZ, [_I64, _I64]),
     "im_qgemm_pack_w4g64": (_INT, [_P, _P, _P, _I64, _I64, _P, _P]),
     "im_qgemm_packed_workspace_bytes": (_SZ, [_I64, _I64, _I64]),

@@ -20,7 +20,6 @@ from . import _lib
 _EPILOGUES = {"store": _lib.EPI_STORE, "residual": _lib.EPI_RESIDUAL, "swiglu": _lib.EPI_SWIGLU,
               "geglu": _lib.EPI_GEGLU}
 _VARIANTS = {"auto": _lib.QGEMM_AUTO, "mma": _lib.QGEMM_MMA, "fma": _lib.QGEMM_FMA}
-TMA = "tma"  # the persistent bulk-copy pipelined kernel (im_qgemm_tma)
 
 
 def _stream(device: torch.device) -> int:
@@ -83,20 +82,8 @@ def _scratch(ws, device, need, purpose):
     return _ws(buf, need)
 
 
-def qgemm_workspace_bytes(m: int, n: int, k: int, variant: str = "auto") -> int:
-    if variant == TMA:
-        return int(_lib.load().im_qgemm_tma_workspace_bytes(m, n, k))
+def qgemm_workspace_bytes(m: int, n: int, k: int) -> int:
     return int(_lib.load().im_qgemm_workspace_bytes(m, n, k))
-
-
-def qgemm_tma_status(ws: torch.Tensor) -> int:
-    """The error word of the v3 kernel's workspace (0: every wait completed). Synchronous."""
-    import ctypes
-
-    ptr, _ = _ws(ws, 0)
-    out = ctypes.c_uint32(0)
-    _lib.call("im_qgemm_tma_status", ptr, ctypes.addressof(out))
-    return int(out.value)
 
 
 def qgemm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, *,
@@ -126,16 +113,10 @@ def qgemm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.
         if residual is None or residual.dtype != torch.bfloat16 or residual.numel() < m * n:
             raise ValueError("the residual epilogue needs a bf16 `residual` of the output's size")
         res_ptr = residual.data_ptr()
-    if variant == TMA:
-        need = int(_lib.load().im_qgemm_tma_workspace_bytes(m, n, k))
-        ws_ptr, ws_bytes = _scratch(ws, device, need, "qgemm_tma")
-        _lib.call("im_qgemm_tma", w.data_ptr(), scales.data_ptr(), biases.data_ptr(), x.data_ptr(), out.data_ptr(),
-                  res_ptr, m, n, k, epi, ws_ptr, ws_bytes, _stream(device))
-    else:
-        need = qgemm_workspace_bytes(m, n, k) if split_k else 0
-        ws_ptr, ws_bytes = _scratch(ws, device, need, "qgemm")
-        _lib.call("im_qgemm_w4g64_ex", w.data_ptr(), scales.data_ptr(), biases.data_ptr(), x.data_ptr(),
-                  out.data_ptr(), res_ptr, m, n, k, epi, _VARIANTS[variant], ws_ptr, ws_bytes, _stream(device))
+    need = qgemm_workspace_bytes(m, n, k) if split_k else 0
+    ws_ptr, ws_bytes = _scratch(ws, device, need, "qgemm")
+    _lib.call("im_qgemm_w4g64_ex", w.data_ptr(), scales.data_ptr(), biases.data_ptr(), x.data_ptr(),
+              out.data_ptr(), res_ptr, m, n, k, epi, _VARIANTS[variant], ws_ptr, ws_bytes, _stream(device))
     if rows is None and out.numel() == m * n_out:
         return out.view(*x.shape[:-1], n_out)
     return out

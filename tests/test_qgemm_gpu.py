@@ -185,49 +185,6 @@ def test_k3840_enable_and_variant_install(cuda):
     assert qmv_variant.uninstall(model) == 1
 
 
-# ---- v3: persistent bulk-copy pipelined kernel ------------------------------------------------------------
-@pytest.mark.parametrize("n,k,m", [(15360, 3840, 1), (15360, 3840, 5), (6144, 2560, 5), (2560, 9728, 5),
-                                   (151936, 2560, 5), (1024, 1024, 2), (96, 256, 13), (50, 768, 32), (4104, 2048, 8)])
-def test_tma_kernel_matches_oracle(cuda, n, k, m):
-    wq, s, b, x = case(n, k, m, seed=n * 3 + k + m)
-    want = qmv.qmv(wq, s, b, x, vpt=8)
-    ws = kernels.workspace(kernels.qgemm_workspace_bytes(m, n, k, "tma"), cuda)
-    got = run(cuda, wq, s, b, x, variant="tma", ws=ws)
-    mx, mean = rel_errors(got, want)
-    assert mx <= MAX_REL and mean <= MEAN_REL, (mx, mean)
-    assert kernels.qgemm_tma_status(ws) == 0
-
-
-def test_tma_row_invariance_and_determinism(cuda):
-    wq, s, b, x = case(15360, 3840, 32, seed=31)
-    ws = kernels.workspace(kernels.qgemm_workspace_bytes(32, 15360, 3840, "tma"), cuda)
-    full = {m: run(cuda, wq, s, b, x[:m], variant="tma", ws=ws) for m in (1, 5, 8, 13, 32)}
-    for m, y in full.items():
-        assert np.array_equal(y, full[32][:m]), m
-    assert np.array_equal(run(cuda, wq, s, b, x[:5], variant="tma", ws=ws), full[5])
-
-
-@pytest.mark.parametrize("epi", ["residual", "swiglu", "geglu"])
-def test_tma_epilogues_equal_the_mma_kernel_epilogue_math(cuda, epi):
-    wq, s, b, x = case(2048, 1024, 5, seed=44)
-    w_t, s_t, b_t, x_t = to_device(wq, s, b, x, cuda)
-    ws = kernels.workspace(kernels.qgemm_workspace_bytes(5, 2048, 1024, "tma"), cuda)
-    plain = kernels.qgemm(x_t, w_t, s_t, b_t, variant="tma", ws=ws)
-    if epi == "residual":
-        res = torch.randn(5, 2048, device=cuda).to(torch.bfloat16)
-        got = kernels.qgemm(x_t, w_t, s_t, b_t, epilogue="residual", residual=res, variant="tma", ws=ws)
-        want = (res.float() + plain.float()).to(torch.bfloat16)
-        assert torch.equal(got.view(torch.int16), want.view(torch.int16))
-    else:
-        got = torch_to_bf16_bits(kernels.qgemm(x_t, w_t, s_t, b_t, epilogue=epi, variant="tma", ws=ws))
-        g = bf16.to_f32(torch_to_bf16_bits(plain)).reshape(5, -1, 2, 16)
-        gate, up = g[:, :, 0, :].reshape(5, -1), g[:, :, 1, :].reshape(5, -1)
-        from oracle import model as om
-        want = (om.silu_mul if epi == "swiglu" else om.gelu_mul)(bf16.from_f32(gate), bf16.from_f32(up))
-        diff = np.abs(bf16.to_f32(got) - bf16.to_f32(want))
-        assert np.all(diff <= 2 * (np.abs(bf16.to_f32(want)) * 2.0 ** -7 + 1e-30))
-
-
 # ---- v4: packed weights --------------------------------------------------------------------------------------
 def packed_case(cuda, n, k, m, seed):
     wq, s, b, x = case(n, k, m, seed=seed)
