@@ -24,7 +24,6 @@ namespace im {
 constexpr int Q4_WARPS = 4;
 constexpr int Q4_THREADS = Q4_WARPS * 32;
 constexpr int Q4_DEPTH = 3;               // units in flight per warp
-constexpr int Q4_PRE = 3;                 // activation slices per thread loaded before the RMSNorm factors
 static int g_q4_split_override = 0;       // sweep hook (0 = automatic)
 static int g_q4_target_ctas = 148 * 4;    // split policy: aim for this many CTAs
 static int g_q4_max_split = Q4_MAX_SPLITS;
@@ -112,9 +111,8 @@ __global__ void q4_pack_kernel(const uint32_t* __restrict__ w, const uint16_t* _
 //   sxs  [rg][NT*8]                    group sums of the activations
 //   inv  [32]                          RMSNorm factors
 //   part [4 warps][2*NT*4][32 lanes]   this CTA's split-K partials, read by the cluster's reducing CTA
-//   nw   [rg][64]                      this CTA's slice of the RMSNorm weight (staged before the wait)
 struct Q4Smem {
-  size_t xf, sxs, inv, part, nw, total;
+  size_t xf, sxs, inv, part, total;
 };
 __host__ __device__ inline Q4Smem q4_smem(int nt, int rg, int norm_parts) {
   Q4Smem m;
@@ -124,8 +122,7 @@ __host__ __device__ inline Q4Smem q4_smem(int nt, int rg, int norm_parts) {
   m.sxs = (xf > nsum ? xf : nsum + 15) / 16 * 16;
   m.inv = m.sxs + (size_t)rg * nt * 8 * 4;
   m.part = m.inv + 32 * 4;
-  m.nw = m.part + (size_t)Q4_WARPS * 2 * nt * 4 * 32 * 4;
-  m.total = m.nw + (size_t)rg * 64 * 2;
+  m.total = m.part + (size_t)Q4_WARPS * 2 * nt * 4 * 32 * 4;
   return m;
 }
 
@@ -269,10 +266,6 @@ qgemm_packed_kernel(Q4Args a) {
       }
     }
   }
-  // ... and this CTA's slice of the RMSNorm weight, into shared memory (read after the barriers below)
-  uint16_t* nw_s = reinterpret_cast<uint16_t*>(q4_raw + lay.nw);
-  if (a.norm_w)
-    for (int i = threadIdx.x; i < ng * 64; i += Q4_THREADS) nw_s[i] = a.norm_w[(size_t)cg0 * 64 + i];
   pdl_wait();
   pdl_trigger();
 
@@ -292,20 +285,16 @@ qgemm_packed_kernel(Q4Args a) {
         }
   }
 
-  // ---- prologue: RMSNorm factors, then the activation fragments and group sums of [cg0, cg1). A job is one
-  // (group, activation row m, quarter t) slice of 16 values; this thread's first Q4_PRE jobs are loaded before
-  // the RMSNorm factors, so that every load of the prologue is in flight at once.
-  const int njobs = ng * NT * 32;
-  uint4 pre_lo[Q4_PRE], pre_hi[Q4_PRE];
-#pragma unroll
-  for (int j = 0; j < Q4_PRE; j++) {
-    const int job = threadIdx.x + j * Q4_THREADS;
+  // ---- prologue: RMSNorm factors, then the activation fragments and group sums of [cg0, cg1). This thread's
+  // first activation slice is loaded before the RMSNorm factors, so that the two loads are in flight together.
+  uint4 pre_lo = make_uint4(0, 0, 0, 0), pre_hi = pre_lo;
+  {
+    const int job = threadIdx.x;
     const int tq = job & 3, m = (job >> 2) % (NT * 8), gl = (job >> 2) / (NT * 8);
-    pre_lo[j] = pre_hi[j] = make_uint4(0, 0, 0, 0);
-    if (job < njobs && m < a.M) {
+    if (job < ng * NT * 32 && m < a.M) {
       const uint16_t* xp = a.x + (size_t)m * a.K + (size_t)(cg0 + gl) * 64 + 16 * tq;
-      pre_lo[j] = __ldg(reinterpret_cast<const uint4*>(xp));
-      pre_hi[j] = __ldg(reinterpret_cast<const uint4*>(xp + 8));
+      pre_lo = __ldg(reinterpret_cast<const uint4*>(xp));
+      pre_hi = __ldg(reinterpret_cast<const uint4*>(xp + 8));
     }
   }
   if (a.norm_w) {
@@ -338,16 +327,27 @@ qgemm_packed_kernel(Q4Args a) {
     }
     __syncthreads();
   }
-  // one job -> fragment order + partial sum (lo/hi: the slice's 16 raw values)
-  auto stage = [&](const int job, uint4 lo, uint4 hi) {
+  // one thread per (group, activation row m, quarter t): 16 values -> fragment order + partial sum
+  for (int job = threadIdx.x; job < ng * NT * 32; job += Q4_THREADS) {
+    const bool first = job == (int)threadIdx.x;
     const int tq = job & 3;
     const int m = (job >> 2) % (NT * 8);
     const int gl = (job >> 2) / (NT * 8);
+    const int grp = cg0 + gl;
+    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
     float part = 0.f;
     if (m < a.M) {
+      if (first) {
+        lo = pre_lo;
+        hi = pre_hi;
+      } else {
+        const uint16_t* xp = a.x + (size_t)m * a.K + (size_t)grp * 64 + 16 * tq;
+        lo = __ldg(reinterpret_cast<const uint4*>(xp));
+        hi = __ldg(reinterpret_cast<const uint4*>(xp + 8));
+      }
       if (a.norm_w) {
         const float inv = inv_s[m];
-        const uint16_t* wv = nw_s + gl * 64 + 16 * tq;
+        const uint16_t* wv = a.norm_w + (size_t)grp * 64 + 16 * tq;
         uint32_t* l32 = reinterpret_cast<uint32_t*>(&lo);
         uint32_t* h32 = reinterpret_cast<uint32_t*>(&hi);
 #pragma unroll
@@ -383,22 +383,6 @@ qgemm_packed_kernel(Q4Args a) {
     part += __shfl_xor_sync(0xffffffffu, part, 1);
     part += __shfl_xor_sync(0xffffffffu, part, 2);
     if (tq == 0) sxs[gl][m] = part;
-  };
-  // jobs are warp-uniform (njobs is a multiple of 32): the pair-sum shuffles see every lane
-#pragma unroll
-  for (int j = 0; j < Q4_PRE; j++) {
-    const int job = threadIdx.x + j * Q4_THREADS;
-    if (job < njobs) stage(job, pre_lo[j], pre_hi[j]);
-  }
-  for (int job = threadIdx.x + Q4_PRE * Q4_THREADS; job < njobs; job += Q4_THREADS) {
-    const int tq = job & 3, m = (job >> 2) % (NT * 8), gl = (job >> 2) / (NT * 8);
-    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-    if (m < a.M) {
-      const uint16_t* xp = a.x + (size_t)m * a.K + (size_t)(cg0 + gl) * 64 + 16 * tq;
-      lo = __ldg(reinterpret_cast<const uint4*>(xp));
-      hi = __ldg(reinterpret_cast<const uint4*>(xp + 8));
-    }
-    stage(job, lo, hi);
   }
   __syncthreads();
   constexpr bool CLUSTER = CL;
