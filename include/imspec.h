@@ -124,8 +124,9 @@ size_t im_qgemm_packed_bytes(int64_t N, int64_t K);
 int im_qgemm_pack_w4g64(const uint32_t* w, const uint16_t* scales, const uint16_t* biases, int64_t N, int64_t K,
                         void* packed, void* stream);
 size_t im_qgemm_packed_workspace_bytes(int64_t M, int64_t N, int64_t K);
-/* Tuning hook of the K-split policy: a forced split (0 = automatic), the CTA count the automatic policy aims
- * for, and its largest split. Process-wide; changes workspace sizes, so set it before sizing workspaces. */
+/* Tuning hook of the K-split policy: a forced split (0 = automatic), the most CTAs the automatic policy fills
+ * (default 592: one wave at four CTAs per SM) and its largest split. Process-wide; changes workspace sizes, so set
+ * it before sizing workspaces. */
 int im_qgemm_packed_tune(int split_override, int target_ctas, int max_split);
 /* Kernel choice: 0 (default) = automatic (tcgen05 tensor cores from 192 rows when the K split is at most 16, the
  * warp MMA otherwise), 1 = warp MMA always, 2 = tensor cores always. Process-wide; every choice gives the same

@@ -25,7 +25,7 @@ constexpr int Q4_WARPS = 4;
 constexpr int Q4_THREADS = Q4_WARPS * 32;
 constexpr int Q4_DEPTH = 3;               // units in flight per warp
 static int g_q4_split_override = 0;       // sweep hook (0 = automatic)
-static int g_q4_target_ctas = 148 * 4;    // split policy: aim for this many CTAs
+static int g_q4_target_ctas = 148 * 4;    // split policy: at most this many CTAs (one wave at 4 per SM)
 static int g_q4_max_split = Q4_MAX_SPLITS;
 static int g_q4_cluster = 1;             // reduce split-K partials inside a thread-block cluster when possible
 static int g_q4_path = 0;                 // 0: automatic, 1: warp MMA always, 2: tensor cores always
@@ -214,8 +214,10 @@ __device__ __forceinline__ void q4_epilogue(const Q4Args& a, const float (&tot)[
 // would be: the same plan, its own split-K counters and partials. CL: the K splits of a CTA column form one
 // thread-block cluster and their partials are summed through distributed shared memory (no global atomics);
 // otherwise the last split to arrive at a global counter sums them. Both sum in split order: the same bits.
+// Up to 8 rows: four CTAs per SM (128 registers a thread; at five the prologue's loads spilled and the config-2
+// round took 6.54 ms against 6.32), and the split plan keeps the grid within one wave of them.
 template <int NT, int EPI, bool CL>
-__global__ void __launch_bounds__(Q4_THREADS, NT == 1 ? 5 : 1)
+__global__ void __launch_bounds__(Q4_THREADS, NT == 1 ? 4 : 1)
 qgemm_packed_kernel(Q4Args a) {
   extern __shared__ __align__(16) unsigned char q4_raw[];
   if (gridDim.z > 1) {  // this CTA's 32-row chunk
@@ -585,7 +587,8 @@ Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
   const int G = (int)(K / 64);
   const int rmax = Q4_RMAX;
   const int need = (G + rmax - 1) / rmax;                // shared-memory budget
-  int s = (g_q4_target_ctas + p.ctas_x - 1) / p.ctas_x;
+  int s = g_q4_target_ctas / p.ctas_x;                 // the most splits that fill one wave
+  if (s < 1) s = 1;
   if (s > g_q4_max_split) s = g_q4_max_split;
   const int cap = G / 4 > 0 ? G / 4 : 1;                // at least 4 groups per CTA
   if (s > cap) s = cap;
