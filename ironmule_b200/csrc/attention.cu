@@ -124,25 +124,22 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // RMSNorm (weight w: w or 1 + w) + RoPE of one head vector by one warp; lane owns elements lane + 32 e.
 // The sum of squares is the per-32-element xor-tree sums added in element order, and the RoPE pairs
 // (i, i + D/2) sit in the same lane: the arithmetic of qk_rope_kv_kernel, value for value.
+// wd[e] = the norm weight of element lane + 32 e (w or 1 + w), fq[e] = inv_freq[lane + 32 e]: loaded by the caller
+// (before the kernel waits for the qkv projection: neither depends on it).
 template <int D>
-__device__ __forceinline__ void norm_rope_vals(const float (&v)[D / 32], const uint16_t* __restrict__ w, int gemma,
-                                               float eps, int pos, const float* __restrict__ inv_freq,
-                                               uint16_t (&outv)[D / 32]) {
+__device__ __forceinline__ void norm_rope_vals(const float (&v)[D / 32], const float (&wd)[D / 32], float eps, int pos,
+                                               const float (&fq)[D / 64], uint16_t (&outv)[D / 32]) {
   constexpr int E = D / 32, H = E / 2;
-  const int lane = threadIdx.x & 31;
   float total = 0.f;
 #pragma unroll
   for (int e = 0; e < E; e++) total += warp_sum(v[e] * v[e]);
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fdiv_rn(total, (float)D) + eps));
   float xn[E];
 #pragma unroll
-  for (int e = 0; e < E; e++) {
-    const float wd = gemma ? 1.0f + bf(w[lane + 32 * e]) : bf(w[lane + 32 * e]);
-    xn[e] = round_bf((v[e] * inv) * wd);
-  }
+  for (int e = 0; e < E; e++) xn[e] = round_bf((v[e] * inv) * wd[e]);
 #pragma unroll
   for (int e = 0; e < H; e++) {
-    const float ang = (float)pos * inv_freq[lane + 32 * e];
+    const float ang = (float)pos * fq[e];
     float sn, cs;
     sincosf(ang, &sn, &cs);
     const float x1 = xn[e], x2 = xn[e + H];
@@ -288,60 +285,104 @@ attn_kernel(AttnArgs a) {
   }
 
   if constexpr (FUSED) {
+    // Before the wait: the norm weights, RoPE frequencies, positions and cache pages (no earlier kernel of the
+    // layer writes them). After it, every element of this warp's query vectors and of its first new row is
+    // loaded at once, then normed and roped.
+    constexpr int E = D / 32, H = E / 2, VPW = NQ / (TH / 32);
+    const int stride = (a.Hq + 2 * a.Hkv) * D;
+    uint32_t qwp[H], kwp[H];  // the norm weights of elements lane + 32 e, two bf16 per word (e = 2i, 2i + 1)
+    float fq[H];
+    int qpos[VPW], kpos = 0, kpage = 0;
+    const int n0 = warp;  // this warp's first new row (later ones, if any, go one at a time below)
+    if (any) {
+#pragma unroll
+      for (int i = 0; i < H; i++) {
+        qwp[i] = (uint32_t)a.q_norm[lane + 64 * i] | ((uint32_t)a.q_norm[lane + 64 * i + 32] << 16);
+        kwp[i] = (uint32_t)a.k_norm[lane + 64 * i] | ((uint32_t)a.k_norm[lane + 64 * i + 32] << 16);
+      }
+#pragma unroll
+      for (int e = 0; e < H; e++) fq[e] = a.inv_freq[lane + 32 * e];
+#pragma unroll
+      for (int t = 0; t < VPW; t++) {
+        const int qi = warp + t * (TH / 32);
+        qpos[t] = qi < nq ? a.row_pos[r0 + (q0 + qi) / G] : 0;
+      }
+      if (n0 < sm.nnew) {
+        kpos = a.row_pos[sm.new_row[n0]];
+        kpage = a.page_table[(size_t)prow * a.max_pages + (sm.new_slot[n0] >> 4)];
+      }
+    }
     pdl_wait();
     pdl_trigger();
     if (any) {
-      const int stride = (a.Hq + 2 * a.Hkv) * D;
-      // this CTA's query vectors: RMSNorm + RoPE, rounded to bf16 as the unfused path stores them; a warp
-      // loads all of its vectors before computing any
-      {
-        constexpr int VPW = NQ / (TH / 32);
-        float v[VPW][D / 32];
-        int pos[VPW];
+      float qw[E], kw[E];
 #pragma unroll
-        for (int t = 0; t < VPW; t++) {
-          const int qi = warp + t * (TH / 32);
-          if (qi < nq) {
-            const int row = r0 + (q0 + qi) / G, head = kvh * G + (q0 + qi) % G;
-            const uint16_t* src = a.qkv + (size_t)row * stride + head * D;
+      for (int e = 0; e < E; e++) {
+        const float q1 = (e & 1) ? bf_hi(qwp[e >> 1]) : bf_lo(qwp[e >> 1]);
+        const float k1 = (e & 1) ? bf_hi(kwp[e >> 1]) : bf_lo(kwp[e >> 1]);
+        qw[e] = a.gemma ? 1.0f + q1 : q1;
+        kw[e] = a.gemma ? 1.0f + k1 : k1;
+      }
+      float v[VPW][E], kv[E];
+      uint16_t vv[E];
 #pragma unroll
-            for (int e = 0; e < D / 32; e++) v[t][e] = bf(src[lane + 32 * e]);
-            pos[t] = a.row_pos[row];
-          }
+      for (int t = 0; t < VPW; t++) {
+        const int qi = warp + t * (TH / 32);
+        if (qi < nq) {
+          const int row = r0 + (q0 + qi) / G, head = kvh * G + (q0 + qi) % G;
+          const uint16_t* src = a.qkv + (size_t)row * stride + head * D;
+#pragma unroll
+          for (int e = 0; e < E; e++) v[t][e] = bf(src[lane + 32 * e]);
         }
+      }
+      if (n0 < sm.nnew) {
+        const uint16_t* src = a.qkv + (size_t)sm.new_row[n0] * stride + (a.Hq + kvh) * D;
 #pragma unroll
-        for (int t = 0; t < VPW; t++) {
-          const int qi = warp + t * (TH / 32);
-          if (qi < nq) {
-            uint16_t o[D / 32];
-            norm_rope_vals<D>(v[t], a.q_norm, a.gemma, a.eps, pos[t], a.inv_freq, o);
+        for (int e = 0; e < E; e++) {
+          kv[e] = bf(src[lane + 32 * e]);
+          vv[e] = src[(size_t)a.Hkv * D + lane + 32 * e];
+        }
+      }
+      // this CTA's query vectors: RMSNorm + RoPE, rounded to bf16 as the unfused path stores them
 #pragma unroll
-            for (int e = 0; e < D / 32; e++) sm.qs[qi][lane + 32 * e] = o[e];
-          }
+      for (int t = 0; t < VPW; t++) {
+        const int qi = warp + t * (TH / 32);
+        if (qi < nq) {
+          uint16_t o[E];
+          norm_rope_vals<D>(v[t], qw, a.eps, qpos[t], fq, o);
+#pragma unroll
+          for (int e = 0; e < E; e++) sm.qs[qi][lane + 32 * e] = o[e];
         }
       }
       // the new rows' keys and values of this CTA's splits (the first query block's CTA also writes them out)
-      for (int n = warp; n < sm.nnew; n += TH / 32) {
-        const int row = sm.new_row[n], slot = sm.new_slot[n];
-        const uint16_t* src = a.qkv + (size_t)row * stride + (a.Hq + kvh) * D;
-        uint16_t o[D / 32];
-        float v[D / 32];
-#pragma unroll
-        for (int e = 0; e < D / 32; e++) v[e] = bf(src[lane + 32 * e]);
-        norm_rope_vals<D>(v, a.k_norm, a.gemma, a.eps, a.row_pos[row], a.inv_freq, o);
-        const int page = a.page_table[(size_t)prow * a.max_pages + (slot >> 4)];
+      auto put_new = [&](int n, const float (&kin)[E], const uint16_t (&vin)[E], int pos, int page) {
+        uint16_t o[E];
+        norm_rope_vals<D>(kin, kw, a.eps, pos, fq, o);
+        const int slot = sm.new_slot[n];
         const size_t off = (((size_t)page * a.Hkv + kvh) * 16 + (slot & 15)) * D;
 #pragma unroll
-        for (int e = 0; e < D / 32; e++) {
+        for (int e = 0; e < E; e++) {
           const int d = lane + 32 * e;
-          const uint16_t v = src[(size_t)a.Hkv * D + d];
           sm.nk[n][d] = o[e];
-          sm.nv[n][d] = v;
+          sm.nv[n][d] = vin[e];
           if (qb == 0) {
             a.kc[off + d] = o[e];
-            a.vc[off + d] = v;
+            a.vc[off + d] = vin[e];
           }
         }
+      };
+      if (n0 < sm.nnew) put_new(n0, kv, vv, kpos, kpage);
+      for (int n = n0 + TH / 32; n < sm.nnew; n += TH / 32) {
+        const int row = sm.new_row[n];
+        const uint16_t* src = a.qkv + (size_t)row * stride + (a.Hq + kvh) * D;
+        float k2[E];
+        uint16_t v2[E];
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+          k2[e] = bf(src[lane + 32 * e]);
+          v2[e] = src[(size_t)a.Hkv * D + lane + 32 * e];
+        }
+        put_new(n, k2, v2, a.row_pos[row], a.page_table[(size_t)prow * a.max_pages + (sm.new_slot[n] >> 4)]);
       }
       __syncthreads();
       fill_new(0);
