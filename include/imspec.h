@@ -143,6 +143,21 @@ int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* y, const ui
                     int64_t K, int epilogue, const float* norm_sq, int64_t norm_parts, const uint16_t* norm_weight,
                     float eps, int gemma_norm, float* out_sq, int64_t sq_ld, void* workspace, size_t workspace_bytes,
                     void* stream);
+/*
+ * The o-projection fused with the attention's split merge: im_qgemm_packed's residual epilogue
+ * (y = residual + x . W^T, out_sq as there) where x, the attention output [M][Hq * D], is merged in the
+ * prologue from the split partials that im_attention_qkv_paged left in attn_workspace when called with
+ * out = NULL (same B, max_rows_per_seq, Hq, Hkv, D, max_kv_len, keys_per_split and seq_rows; row_slot is that
+ * call's row_slot). Row r merges splits [0, row_slot[r] / keys_per_split + 1) with the attention's own merge
+ * arithmetic: the same bits as merging in the attention and calling im_qgemm_packed. Takes
+ * M <= im_qgemm_packed_attn_rows(N, K) rows (0: the shape has no fused form); K = Hq * D.
+ */
+int64_t im_qgemm_packed_attn_rows(int64_t N, int64_t K);
+int im_qgemm_packed_attn(const void* packed, const void* attn_workspace, const int32_t* seq_rows,
+                         const int32_t* row_slot, int64_t B, int64_t max_rows_per_seq, int64_t Hq, int64_t Hkv,
+                         int64_t D, int64_t max_kv_len, int64_t keys_per_split, uint16_t* y, const uint16_t* residual,
+                         int64_t M, int64_t N, int64_t K, float* out_sq, int64_t sq_ld, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /*
  * Row statistics over a logits matrix: for each row r of logits[rows, V] (bf16, row stride ld elements)
@@ -254,6 +269,8 @@ int im_attention_tune(int waves);
  * every row's K and V are written to the caches at row_slot[r] of its sequence's pages. At most 32 rows
  * per sequence. Replaces the q/k norm, RoPE and cache write of the decode step together with its
  * attention (ironmule/paired_research.py:177-215, ironmule/dense_plan.py:337-370 then :111-195, :258-274).
+ * With out = NULL the kernel only writes the split partials into the workspace and leaves their merge to
+ * im_qgemm_packed_attn.
  */
 int im_attention_qkv_paged(const uint16_t* qkv, const uint16_t* q_norm, const uint16_t* k_norm,
                            const float* inv_freq, const int32_t* row_pos, float eps, int gemma_style,

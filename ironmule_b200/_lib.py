@@ -48,6 +48,9 @@ SIGNATURES: dict[str, tuple] = {
     "im_tree_compact": (_INT, [_P, _P, _I64, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "im_qgemm_packed": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _INT, _P, _I64, _P, ctypes.c_float, _INT, _P, _I64,
                                _P, _SZ, _P]),
+    "im_qgemm_packed_attn_rows": (_I64, [_I64, _I64]),
+    "im_qgemm_packed_attn": (_INT, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _I64, _I64,
+                                    _I64, _P, _I64, _P, _SZ, _P]),
     "im_argmax_rows": (_INT, [_P, _I64, _I64, _I64, _P, _I64, _P, _P, _SZ, _P]),
     "im_argmax_workspace_bytes": (_SZ, [_I64, _I64]),
     "im_kq_mul_mat": (_INT, [ctypes.c_int, _P, _P, _P, _I64, _I64, _I64, _P]),

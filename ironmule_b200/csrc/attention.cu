@@ -29,19 +29,12 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "attention.cuh"
 
 namespace im {
 
-constexpr int AT_KB = 64;       // keys per shared-memory block
 constexpr int AT_MAXNEW = 32;   // new (written by this launch) keys per split at most: rows per sequence <= 32
 constexpr int AT_MW = 64;       // splits whose merge weights are kept in shared memory
-// A split partial per query vector: D accumulators, max, sum, 2 floats of padding (16-byte rows for float4
-// reads in the merge).
-constexpr int AT_PAD = 4;
-// Workspace layout, identical for every call so calls of different shapes may share one buffer: arrival
-// counters in a fixed region (kept at zero between launches), then the split partials.
-constexpr size_t AT_COUNTER_BYTES = 65536;
-constexpr int64_t AT_MAX_GROUPS = (int64_t)(AT_COUNTER_BYTES / 4);
 
 struct AttnArgs {
   const uint16_t* q;          // plain mode: [M][Hq][D]
@@ -62,6 +55,7 @@ struct AttnArgs {
   float* part;
   unsigned* counters;
   int max_pages, Hq, Hkv, kpc, nsplit, qblocks, window, gemma;
+  int defer;  // publish the split partials only: the o-projection merges them (out is not written)
   float scale, eps;
 };
 
@@ -612,90 +606,28 @@ attn_kernel(AttnArgs a) {
       }
     }
   }
+  if (a.defer) return;  // the partials are merged by their consumer
   __threadfence();
   __syncthreads();
   if (tid == 0) sm.last = atomicAdd(a.counters + group, 1u) == (unsigned)(stride_x - 1);
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
-  // merge the splits in split order, in one pass: every thread owns (query vector, 4 dims), loads every split's
-  // max, sum and 4 accumulators together, and forms the split weights w_s = exp(m_s - max) itself; the
-  // denominator sum_s l_s w_s and the numerator sum_s o_s w_s are both summed in split order
+  // merge the splits in split order, in one pass: every thread owns (query vector, 4 dims)
   int used = a.nsplit;
   while (used > 1 && (used - 1) * a.kpc >= kv_len) used--;
   constexpr int C4 = D / 4;
-  constexpr int SB = 8;  // splits whose loads are in flight together
   for (int job = tid; job < nq * C4; job += TH) {
     const int i = job / C4, d4 = (job % C4) * 4;
     const float* base = a.part + (group * a.nsplit * NQ + i) * (size_t)(D + AT_PAD);
-    const size_t sstride = (size_t)NQ * (D + AT_PAD);
-    float mx = -INFINITY, lsum = 0.f;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (used <= SB) {  // every split's loads in flight at once: one round trip
-      float4 v[SB];
-      float ms[SB], ls[SB];
-#pragma unroll
-      for (int j = 0; j < SB; j++) {
-        if (j < used) {
-          const float* p = base + j * sstride;
-          v[j] = __ldcg(reinterpret_cast<const float4*>(p + d4));
-          ms[j] = __ldcg(p + D);
-          ls[j] = __ldcg(p + D + 1);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < SB; j++)
-        if (j < used) mx = fmaxf(mx, ms[j]);
-#pragma unroll
-      for (int j = 0; j < SB; j++) {
-        if (j < used) {
-          const float w = (ms[j] == -INFINITY || mx == -INFINITY) ? 0.f : expf(ms[j] - mx);
-          lsum = fmaf(ls[j], w, lsum);
-          o.x = fmaf(v[j].x, w, o.x);
-          o.y = fmaf(v[j].y, w, o.y);
-          o.z = fmaf(v[j].z, w, o.z);
-          o.w = fmaf(v[j].w, w, o.w);
-        }
-      }
-    } else {
-      for (int s0 = 0; s0 < used; s0 += SB) {
-        float ms[SB];
-#pragma unroll
-        for (int j = 0; j < SB; j++) ms[j] = s0 + j < used ? __ldcg(base + (s0 + j) * sstride + D) : -INFINITY;
-#pragma unroll
-        for (int j = 0; j < SB; j++) mx = fmaxf(mx, ms[j]);
-      }
-      for (int s0 = 0; s0 < used; s0 += SB) {
-        float4 v[SB];
-        float ms[SB], ls[SB];
-#pragma unroll
-        for (int j = 0; j < SB; j++) {
-          if (s0 + j < used) {
-            const float* p = base + (s0 + j) * sstride;
-            v[j] = __ldcg(reinterpret_cast<const float4*>(p + d4));
-            ms[j] = __ldcg(p + D);
-            ls[j] = __ldcg(p + D + 1);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < SB; j++) {
-          if (s0 + j < used) {
-            const float w = (ms[j] == -INFINITY || mx == -INFINITY) ? 0.f : expf(ms[j] - mx);
-            lsum = fmaf(ls[j], w, lsum);
-            o.x = fmaf(v[j].x, w, o.x);
-            o.y = fmaf(v[j].y, w, o.y);
-            o.z = fmaf(v[j].z, w, o.z);
-            o.w = fmaf(v[j].w, w, o.w);
-          }
-        }
-      }
-    }
+    uint16_t o4[4];
+    attn_merge4(base, (size_t)NQ * (D + AT_PAD), d4, used, D, o4);
     const int row = r0 + (q0 + i) / G, head = kvh * G + (q0 + i) % G;
     uint16_t* dst = a.out + ((size_t)row * a.Hq + head) * D + d4;
-    dst[0] = to_bf(lsum > 0.f ? __fdiv_rn(o.x, lsum) : 0.f);
-    dst[1] = to_bf(lsum > 0.f ? __fdiv_rn(o.y, lsum) : 0.f);
-    dst[2] = to_bf(lsum > 0.f ? __fdiv_rn(o.z, lsum) : 0.f);
-    dst[3] = to_bf(lsum > 0.f ? __fdiv_rn(o.w, lsum) : 0.f);
+    dst[0] = o4[0];
+    dst[1] = o4[1];
+    dst[2] = o4[2];
+    dst[3] = o4[3];
   }
   if (tid == 0) a.counters[group] = 0u;
 }
@@ -748,12 +680,6 @@ static int dispatch_attn(const AttnArgs& args, int64_t D, int nq, int B, cudaStr
   return nq == 8 ? launch_attn<256, 8, FUSED, 4, 1>(args, B, st) : launch_attn<256, 32, FUSED, 8, 1>(args, B, st);
 }
 
-static void attn_geometry(int64_t rows_per_seq, int64_t G, int* nq, int* qblocks) {
-  const int64_t qv = rows_per_seq * G;
-  *nq = qv <= 8 ? 8 : 32;
-  *qblocks = (int)((qv + *nq - 1) / *nq);
-}
-
 // Shared argument checks and setup of both entry points.
 static int attn_setup(const char* who, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* page_table,
                       int64_t max_pages, const int32_t* seq_rows, const int32_t* seq_slot, const int32_t* row_slot,
@@ -796,7 +722,7 @@ static int attn_setup(const char* who, const uint16_t* k_cache, const uint16_t* 
              "%s: keys_per_split must be a positive multiple of 64", who);
   IM_REQUIRE(max_kv_len >= 1 && max_kv_len <= max_pages * 16, IM_INVALID, "%s: max_kv_len %lld exceeds the page table",
              who, (long long)max_kv_len);
-  IM_REQUIRE(k_cache && v_cache && page_table && seq_rows && row_slot && out && workspace, IM_INVALID,
+  IM_REQUIRE(k_cache && v_cache && page_table && seq_rows && row_slot && workspace, IM_INVALID,
              "%s: null pointer", who);
   IM_REQUIRE(!tree_mask || tree_base, IM_INVALID, "%s: tree_mask needs tree_base", who);
   IM_REQUIRE(aligned(k_cache, 16) && aligned(v_cache, 16) && aligned(workspace, 256), IM_INVALID,
@@ -845,7 +771,7 @@ extern "C" int im_attention_paged(const uint16_t* q, const uint16_t* k_cache, co
                       tree_mask, tree_base, B, max_rows_per_seq, Hq, Hkv, D, max_kv_len, keys_per_split, window, scale,
                       out, workspace, workspace_bytes, &args, &nq);
   if (rc) return rc;
-  IM_REQUIRE(q, IM_INVALID, "im_attention_paged: null q");
+  IM_REQUIRE(q && out, IM_INVALID, "im_attention_paged: null q or out");
   args.q = q;
   return dispatch_attn<false>(args, D, nq, (int)B, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -875,5 +801,6 @@ extern "C" int im_attention_qkv_paged(const uint16_t* qkv, const uint16_t* q_nor
   args.row_pos = row_pos;
   args.eps = eps;
   args.gemma = gemma_style;
+  args.defer = out == nullptr;
   return dispatch_attn<true>(args, D, nq, (int)B, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -16,6 +16,7 @@
 // GEMM (or the embedding) wrote, summed in tile order. A residual epilogue can write those sums for the next GEMM.
 // Partition (tiles x K splits) depends on (N, K) only; rows are independent: a row's bits do not depend on M.
 #include "common.cuh"
+#include "attention.cuh"
 #include "qgemm_packed.cuh"
 #include "../../include/imspec.h"
 
@@ -111,10 +112,11 @@ __global__ void q4_pack_kernel(const uint32_t* __restrict__ w, const uint16_t* _
 //   sxs  [rg][NT*8]                    group sums of the activations
 //   inv  [32]                          RMSNorm factors
 //   part [4 warps][2*NT*4][32 lanes]   this CTA's split-K partials, read by the cluster's reducing CTA
+//   xs   [8 rows][rg * 64]             merged attention output of the K range (attention-merge input only)
 struct Q4Smem {
-  size_t xf, sxs, inv, part, total;
+  size_t xf, sxs, inv, part, xs, total;
 };
-__host__ __device__ inline Q4Smem q4_smem(int nt, int rg, int norm_parts) {
+__host__ __device__ inline Q4Smem q4_smem(int nt, int rg, int norm_parts, bool am = false) {
   Q4Smem m;
   const size_t xf = (size_t)rg * nt * 32 * 32;
   const size_t nsum = (size_t)norm_parts * nt * 8 * 4;
@@ -122,7 +124,8 @@ __host__ __device__ inline Q4Smem q4_smem(int nt, int rg, int norm_parts) {
   m.sxs = (xf > nsum ? xf : nsum + 15) / 16 * 16;
   m.inv = m.sxs + (size_t)rg * nt * 8 * 4;
   m.part = m.inv + 32 * 4;
-  m.total = m.part + (size_t)Q4_WARPS * 2 * nt * 4 * 32 * 4;
+  m.xs = m.part + (size_t)Q4_WARPS * 2 * nt * 4 * 32 * 4;
+  m.total = m.xs + (am ? (size_t)8 * rg * 64 * 2 : 0);
   return m;
 }
 
@@ -216,7 +219,9 @@ __device__ __forceinline__ void q4_epilogue(const Q4Args& a, const float (&tot)[
 // otherwise the last split to arrive at a global counter sums them. Both sum in split order: the same bits.
 // Up to 8 rows: four CTAs per SM (128 registers a thread; at five the prologue's loads spilled and the config-2
 // round took 6.54 ms against 6.32), and the split plan keeps the grid within one wave of them.
-template <int NT, int EPI, bool CL>
+// AM: the input rows are merged from attention split partials in the prologue (up to 8 rows, one merge job of
+// 4 values per thread).
+template <int NT, int EPI, bool CL, bool AM = false>
 __global__ void __launch_bounds__(Q4_THREADS, NT == 1 ? 4 : 1)
 qgemm_packed_kernel(Q4Args a) {
   extern __shared__ __align__(16) unsigned char q4_raw[];
@@ -232,7 +237,7 @@ qgemm_packed_kernel(Q4Args a) {
     a.partial += (size_t)blockIdx.z * a.tiles * a.splits * (2 * 4 * 4 * 32);
     a.M = min(32, a.M - m0);
   }
-  const Q4Smem lay = q4_smem(NT, a.rg, a.norm_w ? a.norm_parts : 0);
+  const Q4Smem lay = q4_smem(NT, a.rg, a.norm_w ? a.norm_parts : 0, AM);
   uint4 (*xf)[NT][32][2] = reinterpret_cast<uint4 (*)[NT][32][2]>(q4_raw + lay.xf);
   float (*sxs)[NT * 8] = reinterpret_cast<float (*)[NT * 8]>(q4_raw + lay.sxs);
   float* inv_s = reinterpret_cast<float*>(q4_raw + lay.inv);
@@ -268,6 +273,24 @@ qgemm_packed_kernel(Q4Args a) {
       }
     }
   }
+  // attention-merge input: this thread's merge job (row m, 4 values at K offset 4c of the CTA's range) and where
+  // its partials sit, from row metadata no earlier kernel of the layer writes
+  const float* am_base = nullptr;
+  int am_used = 0, am_d4 = 0;
+  if constexpr (AM) {
+    const int m = (int)threadIdx.x / (ng * 16), c = (int)threadIdx.x % (ng * 16);
+    if (m < a.M) {
+      int b = 0;
+      while (b + 1 < a.am.B && a.am.seq_rows[b + 1] <= m) b++;
+      const int lr = m - a.am.seq_rows[b];
+      am_used = min(a.am.nsplit, a.am.row_slot[m] / a.am.kpc + 1);
+      const int k = cg0 * 64 + 4 * c, h = k / a.am.D, G = a.am.Hq / a.am.Hkv;
+      am_d4 = k % a.am.D;
+      const int flat = lr * G + h % G;
+      const size_t group = ((size_t)b * a.am.Hkv + h / G) * a.am.qblocks + flat / a.am.nq;
+      am_base = a.am.part + (group * a.am.nsplit * a.am.nq + flat % a.am.nq) * (size_t)(a.am.D + AT_PAD);
+    }
+  }
   pdl_wait();
   pdl_trigger();
 
@@ -289,8 +312,23 @@ qgemm_packed_kernel(Q4Args a) {
 
   // ---- prologue: RMSNorm factors, then the activation fragments and group sums of [cg0, cg1). This thread's
   // first activation slice is loaded before the RMSNorm factors, so that the two loads are in flight together.
+  uint16_t* xs = reinterpret_cast<uint16_t*>(q4_raw + lay.xs);
+  if constexpr (AM) {
+    // the attention output of this CTA's K range, merged from the split partials exactly as the attention's own
+    // merge does it, into shared memory
+    if (am_base) {
+      uint16_t o4[4];
+      attn_merge4(am_base, (size_t)a.am.nq * (a.am.D + AT_PAD), am_d4, am_used, a.am.D, o4);
+      const int m = (int)threadIdx.x / (ng * 16), c = (int)threadIdx.x % (ng * 16);
+      uint2 w;
+      w.x = (uint32_t)o4[0] | ((uint32_t)o4[1] << 16);
+      w.y = (uint32_t)o4[2] | ((uint32_t)o4[3] << 16);
+      *reinterpret_cast<uint2*>(xs + (size_t)m * a.rg * 64 + 4 * c) = w;
+    }
+    __syncthreads();
+  }
   uint4 pre_lo = make_uint4(0, 0, 0, 0), pre_hi = pre_lo;
-  {
+  if constexpr (!AM) {
     const int job = threadIdx.x;
     const int tq = job & 3, m = (job >> 2) % (NT * 8), gl = (job >> 2) / (NT * 8);
     if (job < ng * NT * 32 && m < a.M) {
@@ -339,7 +377,11 @@ qgemm_packed_kernel(Q4Args a) {
     uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
     float part = 0.f;
     if (m < a.M) {
-      if (first) {
+      if constexpr (AM) {
+        const uint4* xp = reinterpret_cast<const uint4*>(xs + (size_t)m * a.rg * 64 + gl * 64 + 16 * tq);
+        lo = xp[0];
+        hi = xp[1];
+      } else if (first) {
         lo = pre_lo;
         hi = pre_hi;
       } else {
@@ -606,7 +648,7 @@ Q4Plan q4_plan(int64_t M, int64_t N, int64_t K) {
 
 // Whether clusters of `splits` CTAs of this kernel can be scheduled at all (asked once per split count, before
 // any launch, so a refusal never happens inside a stream capture).
-template <int NT, int EPI>
+template <int NT, int EPI, bool AM>
 static bool q4_cluster_ok(int splits, size_t smem) {
   static int known[Q4_MAX_SPLITS + 1] = {};  // 0 unknown, 1 yes, 2 no
   if (splits < 2 || splits > Q4_MAX_SPLITS) return false;
@@ -623,26 +665,26 @@ static bool q4_cluster_ok(int splits, size_t smem) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, qgemm_packed_kernel<NT, EPI, true>, &cfg);
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, qgemm_packed_kernel<NT, EPI, true, AM>, &cfg);
     known[splits] = e == cudaSuccess && clusters > 0 ? 1 : 2;
     if (e != cudaSuccess) (void)cudaGetLastError();
   }
   return known[splits] == 1;
 }
 
-template <int NT, int EPI>
+template <int NT, int EPI, bool AM = false>
 static int q4_launch(const Q4Plan& p, const Q4Args& a, cudaStream_t st) {
-  const size_t smem = q4_smem(NT, a.rg, a.norm_w ? a.norm_parts : 0).total;
+  const size_t smem = q4_smem(NT, a.rg, a.norm_w ? a.norm_parts : 0, AM).total;
   static bool configured = false;
   if (!configured) {
-    const int most = (int)q4_smem(NT, Q4_RMAX, Q4_MAX_NORM_PARTS).total;
-    cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
-    cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
-    cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    const int most = (int)q4_smem(NT, Q4_RMAX, Q4_MAX_NORM_PARTS, AM).total;
+    cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI, false, AM>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI, true, AM>, cudaFuncAttributeMaxDynamicSharedMemorySize, most);
+    cudaFuncSetAttribute(qgemm_packed_kernel<NT, EPI, true, AM>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     configured = true;
   }
   dim3 grid(p.ctas_x, p.splits, p.chunks);
-  const bool cluster = g_q4_cluster && p.splits > 1 && q4_cluster_ok<NT, EPI>(p.splits, smem);
+  const bool cluster = g_q4_cluster && p.splits > 1 && q4_cluster_ok<NT, EPI, AM>(p.splits, smem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(Q4_THREADS);
@@ -664,8 +706,8 @@ static int q4_launch(const Q4Plan& p, const Q4Args& a, cudaStream_t st) {
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  const cudaError_t e = cluster ? cudaLaunchKernelEx(&cfg, qgemm_packed_kernel<NT, EPI, true>, a)
-                                : cudaLaunchKernelEx(&cfg, qgemm_packed_kernel<NT, EPI, false>, a);
+  const cudaError_t e = cluster ? cudaLaunchKernelEx(&cfg, qgemm_packed_kernel<NT, EPI, true, AM>, a)
+                                : cudaLaunchKernelEx(&cfg, qgemm_packed_kernel<NT, EPI, false, AM>, a);
   if (e != cudaSuccess) {
     set_error("qgemm_packed_kernel: %s", cudaGetErrorString(e));
     return IM_CUDA_ERROR;
@@ -777,7 +819,7 @@ extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* 
     IM_REQUIRE(workspace && aligned(workspace, 256) && workspace_bytes >= p.workspace, IM_INVALID,
                "im_qgemm_packed: workspace of %zu bytes (256-aligned) needed, %zu given", p.workspace,
                workspace_bytes);
-  Q4Args a;
+  Q4Args a = {};
   a.wp = reinterpret_cast<const unsigned char*>(packed);
   a.x = x;
   a.y = y;
@@ -805,4 +847,67 @@ extern "C" int im_qgemm_packed(const void* packed, const uint16_t* x, uint16_t* 
     case IM_EPI_SWIGLU: return q4_dispatch<IM_EPI_SWIGLU>(p, a, st);
     default: return q4_dispatch<IM_EPI_GEGLU>(p, a, st);
   }
+}
+
+extern "C" int64_t im_qgemm_packed_attn_rows(int64_t N, int64_t K) {
+  if (N < 1 || K < 64 || K % 64) return 0;
+  const Q4Plan p = q4_plan(1, N, K);
+  const int64_t rows = Q4_THREADS / ((int64_t)p.rg * 16);  // one merge job of 4 values per thread
+  return rows > 8 ? 8 : rows;
+}
+
+extern "C" int im_qgemm_packed_attn(const void* packed, const void* attn_workspace, const int32_t* seq_rows,
+                                    const int32_t* row_slot, int64_t B, int64_t max_rows_per_seq, int64_t Hq,
+                                    int64_t Hkv, int64_t D, int64_t max_kv_len, int64_t keys_per_split, uint16_t* y,
+                                    const uint16_t* residual, int64_t M, int64_t N, int64_t K, float* out_sq,
+                                    int64_t sq_ld, void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  IM_REQUIRE(M >= 0 && N >= 1 && K >= 64 && K % 64 == 0 && N <= (1 << 30) && K <= (1 << 24), IM_INVALID,
+             "im_qgemm_packed_attn: bad sizes M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (M == 0) return IM_OK;
+  IM_REQUIRE(M <= im_qgemm_packed_attn_rows(N, K), IM_UNSUPPORTED,
+             "im_qgemm_packed_attn: %lld rows exceed im_qgemm_packed_attn_rows (%lld)", (long long)M,
+             (long long)im_qgemm_packed_attn_rows(N, K));
+  IM_REQUIRE(packed && attn_workspace && seq_rows && row_slot && y && residual, IM_INVALID,
+             "im_qgemm_packed_attn: null pointer");
+  IM_REQUIRE(aligned(packed, 16) && aligned(attn_workspace, 256), IM_INVALID,
+             "im_qgemm_packed_attn: packed 16-byte and the attention workspace 256-byte aligned");
+  IM_REQUIRE(B >= 1 && B <= M && max_rows_per_seq >= 1 && Hkv >= 1 && Hq % Hkv == 0 && (D == 128 || D == 256) &&
+                 Hq * D == K && max_kv_len >= 1 && keys_per_split >= 64 && keys_per_split % 64 == 0,
+             IM_INVALID, "im_qgemm_packed_attn: attention geometry does not match K = Hq * D");
+  const int64_t ld = sq_ld > 0 ? sq_ld : (M + 31) / 32 * 32;
+  IM_REQUIRE(ld >= M, IM_INVALID, "im_qgemm_packed_attn: sq_ld %lld below M", (long long)ld);
+  const Q4Plan p = q4_plan(M, N, K);
+  if (p.splits > 1)
+    IM_REQUIRE(workspace && aligned(workspace, 256) && workspace_bytes >= p.workspace, IM_INVALID,
+               "im_qgemm_packed_attn: workspace of %zu bytes (256-aligned) needed, %zu given", p.workspace,
+               workspace_bytes);
+  int nq, qblocks;
+  attn_geometry(max_rows_per_seq, Hq / Hkv, &nq, &qblocks);
+  Q4Args a = {};
+  a.wp = reinterpret_cast<const unsigned char*>(packed);
+  a.y = y;
+  a.res = residual;
+  a.out_sq = out_sq;
+  a.counters = reinterpret_cast<unsigned*>(workspace);
+  a.partial = workspace ? reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + Q4_COUNTER_BYTES) : nullptr;
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.tiles = p.tiles;
+  a.splits = p.splits;
+  a.sq_ld = (int)ld;
+  a.rg = p.rg;
+  a.am.part = reinterpret_cast<const float*>(reinterpret_cast<const char*>(attn_workspace) + AT_COUNTER_BYTES);
+  a.am.seq_rows = seq_rows;
+  a.am.row_slot = row_slot;
+  a.am.B = (int)B;
+  a.am.Hq = (int)Hq;
+  a.am.Hkv = (int)Hkv;
+  a.am.D = (int)D;
+  a.am.kpc = (int)keys_per_split;
+  a.am.nsplit = (int)((max_kv_len + keys_per_split - 1) / keys_per_split);
+  a.am.qblocks = qblocks;
+  a.am.nq = nq;
+  return q4_launch<1, IM_EPI_RESIDUAL, true>(p, a, reinterpret_cast<cudaStream_t>(stream));
 }

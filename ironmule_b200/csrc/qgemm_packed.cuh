@@ -17,6 +17,16 @@ constexpr int Q4_MAX_NORM_PARTS = 256;       // partial sums of squares per acti
 constexpr size_t Q4_COUNTER_BYTES = 524288;  // split-K arrival counters; the last word is the error word
 constexpr int Q4_MAX_ROWS = 320;             // activation rows per call
 
+// The o-projection's input taken from the attention's unmerged split partials (part == NULL: from x). Row r of
+// sequence b (seq_rows[b] <= r < seq_rows[b + 1]) merges, per head, splits [0, row_slot[r] / kpc + 1): the
+// splits past its own slot hold no key it sees.
+struct Q4Attn {
+  const float* part;      // the attention workspace's split partials
+  const int* seq_rows;    // [B + 1]
+  const int* row_slot;    // [M]
+  int B, Hq, Hkv, D, kpc, nsplit, qblocks, nq;
+};
+
 struct Q4Args {
   const unsigned char* wp;  // packed units
   const uint16_t* x;        // [M, K] activations (raw residual when norm_w != NULL)
@@ -30,6 +40,7 @@ struct Q4Args {
   float eps;
   int M, N, K, tiles, splits, norm_parts, gemma_norm, sq_ld;
   int rg;                   // the most groups any split holds (sizes the activation staging)
+  Q4Attn am;                // attention-merge input (am.part != NULL)
 };
 
 struct Q4Plan {

@@ -307,6 +307,10 @@ class QuantModel:
                                                        self.max_ctx, self.keys_per_split)
                      for rows in (1, 8, min(r, MAX_SEQ_ROWS)))
         self.ws_attn = kernels.workspace(a_need, dev)
+        # forwards of at most this many rows merge the attention's splits in the o-projection's prologue (not with
+        # tensor parallelism or Gemma-3's post-attention norm, whose o-projections have no residual epilogue)
+        self.o_merge_rows = (kernels.qgemm_packed_attn_rows(c.hidden, c.heads * c.head_dim)
+                             if self.tp == 1 and c.family != "gemma3" else 0)
         self.ws_argmax = kernels.workspace(kernels.argmax_workspace_bytes(self.max_logit_rows, c.vocab), dev)
 
     def _gemm_shapes(self):
@@ -345,13 +349,22 @@ class QuantModel:
                                  norm_weight=layer.in_norm, eps=c.eps, gemma_norm=gemma, sq_ld=self.sq_ld, ws=ws)
             tr("qkv", self.qkv)
             glob = c.is_global(li)
+            row_slot = meta.pos if meta.slot is None else meta.slot
+            # few rows: the attention leaves its split partials for the o-projection's prologue to merge (same
+            # bits; the per-op trace keeps the attention output, so it takes the unmerged route)
+            merge_in_o = m <= self.o_merge_rows and trace is None
             kernels.attention_qkv(self.qkv, layer.q_norm, layer.k_norm, self.inv_freq if glob else self.inv_freq_local,
                                   meta.pos, self.k_cache[li], self.v_cache[li], self.page_table, meta.seq_rows,
-                                  meta.pos if meta.slot is None else meta.slot, tree_mask=meta.tree_mask,
+                                  row_slot, tree_mask=meta.tree_mask,
                                   tree_base=meta.tree_base, hq=c.heads, hkv=c.kv_heads, d=c.head_dim, eps=c.eps, gemma=gemma,
                                   max_rows_per_seq=meta.max_rows_per_seq, max_kv_len=max_kv_len, scale=c.scale,
                                   keys_per_split=self.keys_per_split, window=0 if glob else c.sliding_window,
-                                  out=self.attn, rows=m, ws=self.ws_attn, seq_slot=meta.seq_slot)
+                                  out=self.attn, rows=m, ws=self.ws_attn, seq_slot=meta.seq_slot, defer=merge_in_o)
+            if merge_in_o:
+                kernels.qgemm_packed_attn(self.ws_attn, layer.o.p, meta.seq_rows, row_slot, residual=h, out=h, rows=m,
+                                          max_rows_per_seq=meta.max_rows_per_seq, hq=c.heads, hkv=c.kv_heads,
+                                          d=c.head_dim, max_kv_len=max_kv_len, keys_per_split=self.keys_per_split,
+                                          out_sq=self.sq_attn, sq_ld=self.sq_ld, ws=ws)
             tr("attn", self.attn)
             if self.tp > 1:  # partial sums of the row-sharded o and down, all-reduced before the residual add
                 kernels.qgemm_packed(self.attn, layer.o.p, out=self.y, rows=m, sq_ld=self.sq_ld, ws=ws)
@@ -379,8 +392,9 @@ class QuantModel:
                                          out_sq=self.sq_mlp)
                 sq, parts = self.sq_mlp, 1
                 continue
-            kernels.qgemm_packed(self.attn, layer.o.p, epilogue="residual", residual=h, out=h, rows=m,
-                                 out_sq=self.sq_attn, sq_ld=self.sq_ld, ws=ws)
+            if not merge_in_o:
+                kernels.qgemm_packed(self.attn, layer.o.p, epilogue="residual", residual=h, out=h, rows=m,
+                                     out_sq=self.sq_attn, sq_ld=self.sq_ld, ws=ws)
             tr("h_mid", h)
             kernels.qgemm_packed(h, layer.gate_up.p, epilogue="swiglu", out=self.act, rows=m,
                                  norm_sq=self.sq_attn, norm_parts=self.h_tiles, norm_weight=layer.post_norm,

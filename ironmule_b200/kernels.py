@@ -277,14 +277,19 @@ def attention_qkv(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor,
                   max_rows_per_seq: int, max_kv_len: int, scale: float, gemma: bool = False,
                   keys_per_split: int = 64, window: int = 0, tree_mask: torch.Tensor | None = None,
                   tree_base: torch.Tensor | None = None, out: torch.Tensor | None = None, rows: int | None = None,
-                  ws: torch.Tensor | None = None, seq_slot: torch.Tensor | None = None) -> torch.Tensor:
+                  ws: torch.Tensor | None = None, seq_slot: torch.Tensor | None = None,
+                  defer: bool = False) -> torch.Tensor | None:
     """Attention from the packed qkv projection rows [M, (Hq + 2 Hkv) D]: q/k RMSNorm + RoPE and the K/V cache
-    write happen inside the kernel; returns out [M, Hq, D] (bf16)."""
+    write happen inside the kernel; returns out [M, Hq, D] (bf16). defer: only the split partials are written
+    (into ws), for qgemm_packed_attn to merge; returns None."""
     if qkv.dtype != torch.bfloat16 or not qkv.is_contiguous():
         raise TypeError("qkv must be a contiguous bf16 tensor")
     m = qkv.shape[0] if rows is None else rows
     b = seq_rows.numel() - 1
-    out = torch.empty((m, hq, d), dtype=torch.bfloat16, device=qkv.device) if out is None else out
+    if defer and ws is None:
+        raise ValueError("a deferred merge needs the workspace its consumer reads")
+    if not defer:
+        out = torch.empty((m, hq, d), dtype=torch.bfloat16, device=qkv.device) if out is None else out
     need = attention_workspace_bytes(b, max_rows_per_seq, hq, hkv, d, max_kv_len, keys_per_split)
     if need == 0:
         raise ValueError("attention shape not supported")
@@ -293,9 +298,9 @@ def attention_qkv(qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor,
               row_pos.data_ptr(), float(eps), int(gemma), k_cache.data_ptr(), v_cache.data_ptr(),
               page_table.data_ptr(), page_table.shape[-1], seq_rows.data_ptr(), _ptr_or_none(seq_slot),
               row_slot.data_ptr(), _ptr_or_none(tree_mask), _ptr_or_none(tree_base), b, max_rows_per_seq, hq, hkv,
-              d, max_kv_len, keys_per_split, window, float(scale), out.data_ptr(), ws_ptr, ws_bytes,
-              _stream(qkv.device))
-    return out
+              d, max_kv_len, keys_per_split, window, float(scale), None if defer else out.data_ptr(), ws_ptr,
+              ws_bytes, _stream(qkv.device))
+    return None if defer else out
 
 
 def spec_prepare(hist, n, target, b: int, k: int, slot_cap: int, d0_tok, d0_pos, d_pos, v_tok, v_pos) -> None:
@@ -471,6 +476,27 @@ def qgemm_packed(x: torch.Tensor, p: Packed, *, epilogue: str = "store", residua
     _lib.call("im_qgemm_packed", p.data.data_ptr(), x.data_ptr(), out.data_ptr(), _ptr_or_none(residual), m, p.n, p.k,
               epi, _ptr_or_none(norm_sq), norm_parts, _ptr_or_none(norm_weight), float(eps), int(gemma_norm),
               _ptr_or_none(out_sq), sq_ld, ws_ptr, ws_bytes, _stream(device))
+    return out
+
+
+def qgemm_packed_attn_rows(n: int, k: int) -> int:
+    """The most rows qgemm_packed_attn takes for an [n, k] projection (0: none)."""
+    return int(_lib.load().im_qgemm_packed_attn_rows(n, k))
+
+
+def qgemm_packed_attn(attn_ws: torch.Tensor, p: Packed, seq_rows: torch.Tensor, row_slot: torch.Tensor, *,
+                      residual: torch.Tensor, out: torch.Tensor, rows: int, max_rows_per_seq: int, hq: int, hkv: int,
+                      d: int, max_kv_len: int, keys_per_split: int, out_sq: torch.Tensor | None = None,
+                      sq_ld: int = 0, ws: torch.Tensor | None = None) -> torch.Tensor:
+    """The o-projection with a residual epilogue whose input is the attention output merged, in its prologue,
+    from the split partials that attention_qkv(..., defer=True) left in attn_ws (the same bits as merging them
+    in the attention and projecting its output). Takes at most qgemm_packed_attn_rows(p.n, p.k) rows."""
+    device = residual.device
+    b = seq_rows.numel() - 1
+    ws_ptr, ws_bytes = _scratch(ws, device, qgemm_packed_workspace_bytes(rows, p.n, p.k), "qgemm_packed")
+    _lib.call("im_qgemm_packed_attn", p.data.data_ptr(), attn_ws.data_ptr(), seq_rows.data_ptr(), row_slot.data_ptr(),
+              b, max_rows_per_seq, hq, hkv, d, max_kv_len, keys_per_split, out.data_ptr(), residual.data_ptr(), rows,
+              p.n, p.k, _ptr_or_none(out_sq), sq_ld, ws_ptr, ws_bytes, _stream(device))
     return out
 
 

@@ -237,6 +237,58 @@ def test_attention_ctas_per_group_change_no_bits(cuda, d, hq, hkv, rows, tree):
         assert torch.equal(x, y)
 
 
+@pytest.mark.parametrize("d,hq,hkv,rows,lens,kpc,hidden", [
+    (128, 16, 8, 1, [600], 128, 1024),        # a config-2 draft pass
+    (128, 16, 8, 2, [601], 128, 1024),        # its two-row catch-up pass
+    (128, 16, 8, 1, [700, 130], 128, 1024),   # two sequences
+    (128, 16, 8, 1, [1500], 64, 1024),        # 24 splits: the two-pass merge
+    (256, 8, 4, 1, [333], 64, 1536)])
+def test_o_projection_merges_the_attention_splits(cuda, d, hq, hkv, rows, lens, kpc, hidden):
+    """attention_qkv(defer) + qgemm_packed_attn == attention_qkv + qgemm_packed(residual), bit for bit: the
+    o-projection's prologue merges the split partials exactly as the attention's own merge does."""
+    rng = np.random.default_rng(d + rows + len(lens) + kpc)
+    b, max_pages = len(lens), 96
+    table = rng.permutation(b * max_pages).reshape(b, max_pages).astype(np.int32)
+    shape = (b * max_pages, hkv, 16, d)
+    kc0, vc0 = rand_bits(rng, shape), rand_bits(rng, shape)
+    m = b * rows
+    qkv = rand_bits(rng, (m, (hq + 2 * hkv) * d))
+    qn, kn = rand_bits(rng, (d,), 0.5), rand_bits(rng, (d,), 0.5)
+    inv_freq = torch.from_numpy((1e6 ** (-2.0 * np.arange(d // 2) / d)).astype(np.float32)).to(cuda)
+    slots = np.concatenate([np.arange(n - rows, n) for n in lens]).astype(np.int32)
+    seq_rows = torch.arange(0, m + 1, rows, dtype=torch.int32, device=cuda)
+    tbl, sl = torch.from_numpy(table).to(cuda), torch.from_numpy(slots).to(cuda)
+    qkv_t, qn_t, kn_t = bf16_bits_to_torch(qkv, cuda), bf16_bits_to_torch(qn, cuda), bf16_bits_to_torch(kn, cuda)
+    k = hq * d
+    assert kernels.qgemm_packed_attn_rows(hidden, k) >= m
+    w = torch.randint(-2 ** 31, 2 ** 31 - 1, (hidden, k // 8), dtype=torch.int32, device=cuda)
+    sc = bf16_bits_to_torch(rand_bits(rng, (hidden, k // 64), 0.02), cuda)
+    bi = bf16_bits_to_torch(rand_bits(rng, (hidden, k // 64), 0.02), cuda)
+    p = kernels.Packed(w, sc, bi)
+    h0 = bf16_bits_to_torch(rand_bits(rng, (m, hidden)), cuda)
+    kw = dict(max_rows_per_seq=rows, max_kv_len=max_pages * 16, scale=d ** -0.5, keys_per_split=kpc)
+    need = kernels.attention_workspace_bytes(b, rows, hq, hkv, d, max_pages * 16, kpc)
+    outs = []
+    for fused in (False, True):
+        kc, vc = bf16_bits_to_torch(kc0, cuda), bf16_bits_to_torch(vc0, cuda)
+        ws = torch.zeros(need, dtype=torch.uint8, device=cuda)
+        h, sq = h0.clone(), torch.zeros((hidden // 32, 32), dtype=torch.float32, device=cuda)
+        attn = kernels.attention_qkv(qkv_t, qn_t, kn_t, inv_freq, sl, kc, vc, tbl, seq_rows, sl, hq=hq, hkv=hkv, d=d,
+                                     eps=1e-6, ws=ws, defer=fused, **kw)
+        if fused:
+            assert attn is None
+            kernels.qgemm_packed_attn(ws, p, seq_rows, sl, residual=h, out=h, rows=m, max_rows_per_seq=rows, hq=hq,
+                                      hkv=hkv, d=d, max_kv_len=max_pages * 16, keys_per_split=kpc, out_sq=sq, sq_ld=32)
+        else:
+            kernels.qgemm_packed(attn.view(m, k), p, epilogue="residual", residual=h, out=h, rows=m, out_sq=sq,
+                                 sq_ld=32)
+        torch.cuda.synchronize()
+        outs.append((h.view(torch.int16).clone(), sq.clone(), kc.view(torch.int16).clone()))
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1].view(torch.int32), outs[1][1].view(torch.int32))
+    assert torch.equal(outs[0][2], outs[1][2])
+
+
 def tiny(name="tiny-target", seed=0, **kw):
     return engine.QuantModel(engine.PRESETS[name], "cuda", seed=seed, max_ctx=256, **kw)
 
