@@ -214,6 +214,10 @@ attn_kernel(AttnArgs a) {
   __syncthreads();
   const int kv_len = sm.kv_len;
   const bool any = nq > 0 && (int)blockIdx.x * a.kpc < kv_len;  // this CTA has at least one non-empty split
+  // A CTA without a split leaves now, before the wait, and frees its slot for one that has work; the merge
+  // counts only the CTAs of the group that have a split.
+  if (!any) return;
+  const int live_ctas = min(stride_x, (kv_len + a.kpc - 1) / a.kpc);
   // keys below min_vis are visible to every query vector of this CTA (no window; below the tree slots)
   int min_vis = 0;
   if (a.window <= 0 && nq > 0) {
@@ -609,7 +613,7 @@ attn_kernel(AttnArgs a) {
   if (a.defer) return;  // the partials are merged by their consumer
   __threadfence();
   __syncthreads();
-  if (tid == 0) sm.last = atomicAdd(a.counters + group, 1u) == (unsigned)(stride_x - 1);
+  if (tid == 0) sm.last = atomicAdd(a.counters + group, 1u) == (unsigned)(live_ctas - 1);
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
