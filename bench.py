@@ -307,8 +307,8 @@ def run_spec_decode(args, world: int, rank: int, local: int) -> None:
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     pk = peaks()
-    target = QuantModel(PRESETS["qwen3-4b"], device, seed=0, max_ctx=MAX_CTX, max_rows=32, max_logit_rows=8)
-    draft = QuantModel(PRESETS["qwen3-0.6b"], device, seed=1, max_ctx=MAX_CTX, max_rows=8, max_logit_rows=8)
+    target = QuantModel(PRESETS["qwen3-4b"], device, seed=0, max_ctx=MAX_CTX, max_rows=256, max_logit_rows=8)
+    draft = QuantModel(PRESETS["qwen3-0.6b"], device, seed=1, max_ctx=MAX_CTX, max_rows=256, max_logit_rows=8)
     dec = SpecDecoder(target, draft, k=K_DRAFTS, batch=1)
     gen = torch.Generator().manual_seed(rank)
     prompt = torch.randint(0, PRESETS["qwen3-4b"].vocab, (PROMPT,), generator=gen, dtype=torch.int32)

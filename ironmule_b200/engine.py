@@ -35,7 +35,9 @@ from . import kernels
 from .kvpool import PAGE, PagePool  # PAGE: KV slots per cache page
 
 MAX_QGEMM_ROWS = 320   # rows of one forward (the packed qGEMM takes them in chunks of 32)
-MAX_SEQ_ROWS = 32      # rows of one sequence in one forward (the fused attention's limit): prefill chunks
+MAX_SEQ_ROWS = 32      # rows of one sequence in one forward through the fused attention
+PREFILL_SEQ_ROWS = 256  # rows of one sequence in one prefill forward (above 32: q/k norm + RoPE + KV write, then
+                        # the paged attention, as two kernels)
 PARK_PAGES = 3         # pages an idle decoder slot writes (positions 0 .. 2 + MAX_SEQ_ROWS)
 
 
@@ -160,7 +162,7 @@ class RowMeta:
     tokens: torch.Tensor
     token_stride: int
     pos: torch.Tensor
-    seq: torch.Tensor
+    seq: torch.Tensor  # sequence group per row (an index into seq_rows, and into seq_slot when given)
     seq_rows: torch.Tensor
     rows: int
     max_rows_per_seq: int
@@ -305,8 +307,10 @@ class QuantModel:
         self.ws_gemm = kernels.workspace(max(q_need, head_need), dev)
         a_need = max(kernels.attention_workspace_bytes(self.max_seqs, rows, c.heads, c.kv_heads, c.head_dim,
                                                        self.max_ctx, self.keys_per_split)
-                     for rows in (1, 8, min(r, MAX_SEQ_ROWS)))
+                     for rows in (1, 8, min(r, MAX_SEQ_ROWS), min(r, PREFILL_SEQ_ROWS)))
         self.ws_attn = kernels.workspace(a_need, dev)
+        # the roped queries of forwards with more rows per sequence than the fused attention takes (prefill)
+        self.q_wide = torch.zeros((r, c.heads * c.head_dim), dtype=bf, device=dev) if r > MAX_SEQ_ROWS else None
         # forwards of at most this many rows merge the attention's splits in the o-projection's prologue (not with
         # tensor parallelism or Gemma-3's post-attention norm, whose o-projections have no residual epilogue)
         self.o_merge_rows = (kernels.qgemm_packed_attn_rows(c.hidden, c.heads * c.head_dim)
@@ -338,6 +342,11 @@ class QuantModel:
         kernels.embed(meta.tokens, self.embed.w, self.embed.s, self.embed.b, mult=mult, out=h, rows=m,
                       stride=meta.token_stride, out_sq=self.sq_embed)
         sq, parts = self.sq_embed, 1
+        row_page = None  # page-table row of every row, for the two-kernel attention of wide prefill chunks
+        if meta.max_rows_per_seq > MAX_SEQ_ROWS:
+            if self.q_wide is None or m > self.q_wide.shape[0]:
+                raise ValueError(f"{meta.max_rows_per_seq} rows of one sequence exceed this model's rows")
+            row_page = meta.seq if meta.seq_slot is None else meta.seq_slot[meta.seq.long()]
         def tr(key: str, t: torch.Tensor) -> None:
             if trace is not None:
                 trace[-1][key] = t[:m].clone()
@@ -353,13 +362,25 @@ class QuantModel:
             # few rows: the attention leaves its split partials for the o-projection's prologue to merge (same
             # bits; the per-op trace keeps the attention output, so it takes the unmerged route)
             merge_in_o = m <= self.o_merge_rows and trace is None
-            kernels.attention_qkv(self.qkv, layer.q_norm, layer.k_norm, self.inv_freq if glob else self.inv_freq_local,
-                                  meta.pos, self.k_cache[li], self.v_cache[li], self.page_table, meta.seq_rows,
-                                  row_slot, tree_mask=meta.tree_mask,
-                                  tree_base=meta.tree_base, hq=c.heads, hkv=c.kv_heads, d=c.head_dim, eps=c.eps, gemma=gemma,
-                                  max_rows_per_seq=meta.max_rows_per_seq, max_kv_len=max_kv_len, scale=c.scale,
-                                  keys_per_split=self.keys_per_split, window=0 if glob else c.sliding_window,
-                                  out=self.attn, rows=m, ws=self.ws_attn, seq_slot=meta.seq_slot, defer=merge_in_o)
+            inv_freq = self.inv_freq if glob else self.inv_freq_local
+            window = 0 if glob else c.sliding_window
+            if meta.max_rows_per_seq > MAX_SEQ_ROWS:  # prefill chunks beyond the fused attention's rows
+                q = kernels.qk_norm_rope_kv(self.qkv, layer.q_norm, layer.k_norm, inv_freq, meta.pos, row_slot, row_page,
+                                            self.page_table, c.heads, c.kv_heads, c.head_dim, c.eps, self.k_cache[li],
+                                            self.v_cache[li], gemma=gemma, q_out=self.q_wide, rows=m)
+                kernels.attention(q.view(-1, c.heads, c.head_dim), self.k_cache[li], self.v_cache[li], self.page_table,
+                                  meta.seq_rows, row_slot, max_rows_per_seq=meta.max_rows_per_seq,
+                                  max_kv_len=max_kv_len, scale=c.scale, keys_per_split=self.keys_per_split,
+                                  window=window, tree_mask=meta.tree_mask, tree_base=meta.tree_base, out=self.attn,
+                                  rows=m, ws=self.ws_attn, seq_slot=meta.seq_slot)
+            else:
+                kernels.attention_qkv(self.qkv, layer.q_norm, layer.k_norm, inv_freq, meta.pos, self.k_cache[li],
+                                      self.v_cache[li], self.page_table, meta.seq_rows, row_slot,
+                                      tree_mask=meta.tree_mask, tree_base=meta.tree_base, hq=c.heads, hkv=c.kv_heads,
+                                      d=c.head_dim, eps=c.eps, gemma=gemma, max_rows_per_seq=meta.max_rows_per_seq,
+                                      max_kv_len=max_kv_len, scale=c.scale, keys_per_split=self.keys_per_split,
+                                      window=window, out=self.attn, rows=m, ws=self.ws_attn, seq_slot=meta.seq_slot,
+                                      defer=merge_in_o)
             if merge_in_o:
                 kernels.qgemm_packed_attn(self.ws_attn, layer.o.p, meta.seq_rows, row_slot, residual=h, out=h, rows=m,
                                           max_rows_per_seq=meta.max_rows_per_seq, hq=c.heads, hkv=c.kv_heads,
@@ -451,7 +472,7 @@ class QuantModel:
         m = len(positions)
         return RowMeta(tokens=tokens, token_stride=1,
                        pos=torch.tensor(positions, dtype=torch.int32, device=dev),
-                       seq=torch.full((m,), seq, dtype=torch.int32, device=dev),
+                       seq=torch.zeros((m,), dtype=torch.int32, device=dev),
                        seq_rows=torch.tensor([0, m], dtype=torch.int32, device=dev),
                        rows=m, max_rows_per_seq=m,
                        seq_slot=torch.tensor([seq], dtype=torch.int32, device=dev))
@@ -459,21 +480,21 @@ class QuantModel:
     def prefill(self, tokens: torch.Tensor, seq: int = 0, start: int = 0) -> None:
         """Write the KV of `tokens` (int32 on the device) at slots start.. of sequence slot `seq`."""
         total = tokens.numel()
-        step = min(self.max_rows, MAX_SEQ_ROWS)
+        step = min(self.max_rows, PREFILL_SEQ_ROWS)
         for off in range(0, total, step):
             part = tokens[off:off + step].contiguous()
             meta = self._meta(part, list(range(start + off, start + off + part.numel())), seq)
             self.forward(meta, max_kv_len=self.max_ctx)
 
     def prefill_many(self, prompts: list[tuple[int, torch.Tensor]]) -> None:
-        """Prefill several sequence slots together: each forward packs the next (up to 32-token) chunk of as many
+        """Prefill several sequence slots together: each forward packs the next (up to 256-token) chunk of as many
         sequences as fit in max_rows (up to 320 rows), so the projections run at many rows at once. A sequence's
         chunks are the ones `prefill` would cut, and every kernel is row-invariant, so the KV written is the same
         bits as prefilling the sequences one by one. `prompts`: (slot, int32 tokens on the device[, start]), the
         tokens going to slots start.. of the slot (0 by default: the K/V of slots below start are already there)."""
         dev = self.device
         starts = [p[2] if len(p) > 2 else 0 for p in prompts]
-        plan = prefill_plan([p[1].numel() for p in prompts], min(self.max_rows, MAX_SEQ_ROWS),
+        plan = prefill_plan([p[1].numel() for p in prompts], min(self.max_rows, PREFILL_SEQ_ROWS),
                             min(self.max_rows, MAX_QGEMM_ROWS))
         for forward in plan:
             parts = [prompts[i][1][off:off + n] for i, off, n in forward]

@@ -470,6 +470,29 @@ def test_batched_prefill_writes_the_same_kv(cuda):
             assert torch.equal(slots(one).view(torch.int16), slots(many).view(torch.int16)), (b, cache)
 
 
+def test_wide_prefill_chunks_write_the_same_kv(cuda):
+    """Prefill in chunks wider than the fused attention's 32 rows per sequence (the q/k norm + RoPE + KV write
+    kernel, then the paged attention): the caches and the next token's logits are the same bits as with 32-row
+    chunks through the fused attention."""
+    gen = torch.Generator().manual_seed(21)
+    prompt = torch.randint(0, 1000, (200,), generator=gen).to(torch.int32).to(cuda)
+    narrow = tiny("tiny-target", seed=5, sigma=0.08, max_rows=32, max_logit_rows=8)
+    wide = tiny("tiny-target", seed=5, sigma=0.08, max_rows=256, max_logit_rows=8)
+    for model in (narrow, wide):
+        model.prefill(prompt[:-1])
+    torch.cuda.synchronize()
+    pages = narrow.page_table[0]
+    for cache in ("k_cache", "v_cache"):
+        def slots(model):  # [layers, pages, Hkv, 16, D] -> [layers, slot, Hkv, D]
+            t = getattr(model, cache)[:, pages].permute(0, 1, 3, 2, 4)
+            return t.reshape(model.cfg.layers, -1, model.cfg.kv_heads, model.cfg.head_dim)[:, :prompt.numel() - 1]
+        assert torch.equal(slots(narrow).view(torch.int16), slots(wide).view(torch.int16)), cache
+    last = prompt[-1:].contiguous()
+    a = narrow.logits_for(last, prompt.numel() - 1).clone()
+    b = wide.logits_for(last, prompt.numel() - 1).clone()
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
 @pytest.mark.parametrize("rows,hq", [(1, 16), (2, 16), (5, 32)])
 def test_attention_row_alone_equals_row_in_a_batch(cuda, rows, hq):
     """20 sequences in one launch (160 kv-head groups: the large-batch warp layout and several splits per CTA)
