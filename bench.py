@@ -11,7 +11,8 @@ the data path), timed with CUDA events over K rounds replayed from one captured 
 streams the full 3.6 GB of weights, far more than the 126 MB L2, so no flush is needed.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload spec_decode|verify_step|stochastic|tree|tp|attention|kquant]
+                    [--workload spec_decode|verify_step|qgemm_pass|stochastic|tree|tp|attention|kquant|
+                                small_kernels|prefill]
 
 --workload stochastic: BASELINE config 3's round -- Qwen3-4B + 0.6B, temperature 0.7, top-p 0.95, k = 4, rejection
 sampling with residual resampling on Philox -- over 32 concurrent sequences with prompt lengths drawn uniformly
@@ -54,7 +55,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["spec_decode", "verify_step", "qgemm_pass", "stochastic", "tree", "tp",
-                                           "attention", "kquant", "small_kernels"],
+                                           "attention", "kquant", "small_kernels", "prefill"],
                     default="spec_decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -426,6 +427,44 @@ def run_qgemm_pass(args, world: int, rank: int, local: int) -> None:
                 "config": {"workload": "verify pass qGEMMs, Qwen3-4B, M=5, graph-replayed",
                            "l2": "2.26 GB of weights per pass >> 126 MB L2"},
                 "roofline": roof, "peak_source": pk["source"]}
+        print(json.dumps(line), flush=True)
+
+
+def run_prefill(args, world: int, rank: int, local: int) -> None:
+    """The e2e path's prompt prefill: the default workload's 511 prompt tokens (all but the last) into both
+    models, in the chunks QuantModel.prefill cuts (256 rows per forward). Each step prefills both models from
+    scratch; the timed steps run inside an NVTX range "timed" (the ncu launch list selects it)."""
+    import torch
+
+    from ironmule_b200.engine import PRESETS, QuantModel
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    target = QuantModel(PRESETS["qwen3-4b"], device, seed=0, max_ctx=MAX_CTX, max_rows=256, max_logit_rows=8)
+    draft = QuantModel(PRESETS["qwen3-0.6b"], device, seed=1, max_ctx=MAX_CTX, max_rows=256, max_logit_rows=8)
+    gen = torch.Generator().manual_seed(rank)
+    prompt = torch.randint(0, PRESETS["qwen3-4b"].vocab, (PROMPT - 1,), generator=gen, dtype=torch.int32).to(device)
+    steps = max(args.steps, 1)
+    for _ in range(max(args.warmup, 1)):
+        target.prefill(prompt)
+        draft.prefill(prompt)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("timed")
+    e0.record()
+    for _ in range(steps):
+        target.prefill(prompt)
+        draft.prefill(prompt)
+    e1.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    if rank == 0:
+        line = {"metric": "prefill tokens/s (Qwen3-4B + Qwen3-0.6B, 511-token prompt)",
+                "value": round((PROMPT - 1) / (ms / 1000), 1), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+                "warmup": max(args.warmup, 1), "ms_per_step": round(ms, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, 4-bit weights",
+                "data": "synthetic", "config": {"workload": "prompt prefill of both models, 256-row chunks"}}
         print(json.dumps(line), flush=True)
 
 
@@ -983,6 +1022,8 @@ def main() -> int:
             run_qgemm_pass(args, world, rank, local)
         elif args.workload == "small_kernels":
             run_small_kernels(args, world, rank, local)
+        elif args.workload == "prefill":
+            run_prefill(args, world, rank, local)
         elif args.workload == "attention":
             run_attention(args, world, rank, local)
         elif args.workload == "kquant":
