@@ -23,8 +23,8 @@
 //    K-major, swizzled);
 //  * warp 1, the MMA warp: 4 MMAs (M = 128, N = the chunk's rows rounded up to 16, K = 16) per group into one of
 //    four tensor-memory accumulators, committed to the A, load-stage and accumulator barriers;
-//  * warps 4-11, the epilogue warps (lane quadrant = tile w%4, columns [64 ((w-4)/4), +64)): per group the accumulator and
-//    group sums into 64 fp32 totals per thread; at an item's last group the split-K partials (the last split to
+//  * warps 4-19, the epilogue warps (lane quadrant = tile w%4, columns [32 ((w-4)/4), +32)): per group the accumulator and
+//    group sums into 32 fp32 totals per thread; at an item's last group the split-K partials (the last split to
 //    arrive sums them in split order) and the epilogue (store / residual (+ sums of squares) / SwiGLU / GeGLU) in
 //    the warp-MMA kernel's order.
 // Every mbarrier wait is bounded (1 s). A wait that runs out sets the error word (the last word of the counter
@@ -44,8 +44,9 @@ constexpr int QT_LS = 4;                // load stages (weights + activation til
 constexpr int QT_AS = 3;                // A stages
 constexpr int QT_TB = 4;                // tensor-memory accumulators
 constexpr int QT_SR = 16;               // group-sum ring entries
-constexpr int QT_CW = 64;               // accumulator columns per epilogue warp
-constexpr int QT_TRANSFORM = 2, QT_EPI = 8;
+constexpr int QT_CW = 32;               // accumulator columns per epilogue warp
+constexpr int QT_PARTS = QT_N / QT_CW;  // epilogue warps per tile (column parts of an accumulator)
+constexpr int QT_TRANSFORM = 2, QT_EPI = 4 * QT_PARTS;
 constexpr int QT_W_TRANSFORM = 2, QT_W_EPI = 2 + QT_TRANSFORM;
 constexpr int QT_THREADS = (2 + QT_TRANSFORM + QT_EPI) * 32;
 constexpr uint32_t QT_TMEM_COLS = QT_TB * QT_N;
@@ -492,26 +493,32 @@ qtc_kernel(QtArgs a) {
     if (!qt_wait(&sx_full[r], (uint32_t)((k / QT_SR) & 1), abort_flag, a.error)) break;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const float s0 = bf_lo(sb_cur), b0 = fmaf(-128.f, s0, bf_hi(sb_cur));
+    // the warp's accumulator columns, every load in flight before one wait
+    uint32_t acc[QT_CW];
+#pragma unroll
+    for (int h = 0; h < QT_CW / 16; h++) {
+      const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(tb * QT_N + col0 + 16 * h);
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+          : "=r"(acc[16 * h + 0]), "=r"(acc[16 * h + 1]), "=r"(acc[16 * h + 2]), "=r"(acc[16 * h + 3]),
+            "=r"(acc[16 * h + 4]), "=r"(acc[16 * h + 5]), "=r"(acc[16 * h + 6]), "=r"(acc[16 * h + 7]),
+            "=r"(acc[16 * h + 8]), "=r"(acc[16 * h + 9]), "=r"(acc[16 * h + 10]), "=r"(acc[16 * h + 11]),
+            "=r"(acc[16 * h + 12]), "=r"(acc[16 * h + 13]), "=r"(acc[16 * h + 14]), "=r"(acc[16 * h + 15])
+          : "r"(ta));
+    }
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int h = 0; h < QT_CW / 16; h++) {
       if (16 * h < ncols) {
-        uint32_t acc[16];
-        const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(tb * QT_N + col0 + 16 * h);
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-            : "=r"(acc[0]), "=r"(acc[1]), "=r"(acc[2]), "=r"(acc[3]), "=r"(acc[4]), "=r"(acc[5]), "=r"(acc[6]),
-              "=r"(acc[7]), "=r"(acc[8]), "=r"(acc[9]), "=r"(acc[10]), "=r"(acc[11]), "=r"(acc[12]), "=r"(acc[13]),
-              "=r"(acc[14]), "=r"(acc[15])
-            : "r"(ta));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         const float4* sx4 = reinterpret_cast<const float4*>(sx_ring + (size_t)r * QT_N + col0 + 16 * h);
 #pragma unroll
         for (int j4 = 0; j4 < 4; j4++) {
           const float4 sx = sx4[j4];
           float* tt = tot + 16 * h + 4 * j4;
+          const uint32_t* ac = acc + 16 * h + 4 * j4;
           // tot = fmaf(b', sx, fmaf(s, acc, tot)), two columns per instruction
-          qt_fma2(tt[0], tt[1], s0, s0, __uint_as_float(acc[4 * j4 + 0]), __uint_as_float(acc[4 * j4 + 1]));
-          qt_fma2(tt[2], tt[3], s0, s0, __uint_as_float(acc[4 * j4 + 2]), __uint_as_float(acc[4 * j4 + 3]));
+          qt_fma2(tt[0], tt[1], s0, s0, __uint_as_float(ac[0]), __uint_as_float(ac[1]));
+          qt_fma2(tt[2], tt[3], s0, s0, __uint_as_float(ac[2]), __uint_as_float(ac[3]));
           qt_fma2(tt[0], tt[1], b0, b0, sx.x, sx.y);
           qt_fma2(tt[2], tt[3], b0, b0, sx.z, sx.w);
         }
@@ -531,7 +538,7 @@ qtc_kernel(QtArgs a) {
       if (tile < a.tiles && ncols > 0) {
         bool last = true;
         if (a.splits > 1) {
-          const size_t slot = ((size_t)ce.chunk * a.tiles + tile) * 2 + part;
+          const size_t slot = ((size_t)ce.chunk * a.tiles + tile) * QT_PARTS + part;
           float* mine = a.partial + (slot * a.splits + ce.split) * (QT_CW * 32);
 #pragma unroll
           for (int j = 0; j < QT_CW; j++) __stcg(mine + j * 32 + lane, tot[j]);
@@ -643,7 +650,7 @@ static void qtc_shape(int64_t M, int* chunks, int* nmma) {
 }
 
 static size_t qtc_partials(const Q4Plan& p, int chunks) {
-  return p.splits > 1 ? (size_t)chunks * p.tiles * 2 * p.splits * QT_CW * 32 * sizeof(float) : 0;
+  return p.splits > 1 ? (size_t)chunks * p.tiles * QT_PARTS * p.splits * QT_CW * 32 * sizeof(float) : 0;
 }
 
 size_t qtc_workspace_bytes(const Q4Plan& p, int64_t M, int64_t K) {
@@ -658,7 +665,7 @@ int qtc_launch(const Q4Plan& p, const Q4Args& a4, int epilogue, void* workspace,
   int chunks, nmma;
   qtc_shape(a4.M, &chunks, &nmma);
   const int G = a4.K / 64;
-  IM_REQUIRE((size_t)chunks * p.tiles * 2 < Q4_COUNTER_BYTES / 4 - 1, IM_UNSUPPORTED,
+  IM_REQUIRE((size_t)chunks * p.tiles * QT_PARTS < Q4_COUNTER_BYTES / 4 - 1, IM_UNSUPPORTED,
              "im_qgemm_packed: N too large at %d rows", a4.M);
   IM_REQUIRE(workspace, IM_INVALID, "im_qgemm_packed: the tensor-core path needs the workspace");
   char* ws = reinterpret_cast<char*>(workspace);
