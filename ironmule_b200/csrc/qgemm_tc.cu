@@ -54,7 +54,9 @@ constexpr int QT_BARS = 2 * QT_LS + 2 * QT_AS + 2 * QT_TB + 2 * QT_SR;
 constexpr size_t QT_OFF_A = (size_t)QT_LS * QT_B;
 constexpr size_t QT_OFF_W = QT_OFF_A + (size_t)QT_AS * QT_A;
 constexpr size_t QT_OFF_SX = QT_OFF_W + (size_t)QT_LS * QT_WBYTES;
-constexpr size_t QT_OFF_BAR = QT_OFF_SX + (size_t)QT_SR * QT_N * 4;
+constexpr int QT_SBB = 4 * 128;           // a group's scales and biases of the item's 4 tiles
+constexpr size_t QT_OFF_SB = QT_OFF_SX + (size_t)QT_SR * QT_N * 4;
+constexpr size_t QT_OFF_BAR = QT_OFF_SB + (size_t)QT_SR * QT_SBB;
 constexpr size_t QT_SMEM = 1024 + QT_OFF_BAR + (size_t)QT_BARS * 8 + 16;
 constexpr unsigned long long QT_WAIT_NS = 1000000000ull;
 constexpr uint32_t QT_128 = 0x43004300u;
@@ -353,8 +355,14 @@ qtc_kernel(QtArgs a) {
           k++;
           break;
         }
-        expect(&sx_full[r], sbytes);
+        expect(&sx_full[r], sbytes + (uint32_t)QT_SBB);
         copy(base + (uint32_t)(QT_OFF_SX + (size_t)r * QT_N * 4), a.sxt + t * QT_N, sbytes, &sx_full[r]);
+#pragma unroll
+        for (int tt = 0; tt < 4; tt++) {  // the group's scales and biases (bytes 1024.. of each tile's unit)
+          const int tile = min(4 * c.x + tt, a.tiles - 1);
+          copy(base + (uint32_t)(QT_OFF_SB + (size_t)r * QT_SBB + tt * 128),
+               a.wp + ((size_t)tile * G + c.cg0 + c.gl) * Q4_UNIT + 1024, 128u, &sx_full[r]);
+        }
         if (!qt_next(a, c)) {
           k++;
           break;
@@ -469,15 +477,9 @@ qtc_kernel(QtArgs a) {
   const int ncols = max(0, min(QT_CW, a.nmma - col0));  // accumulator columns of this warp holding chunk rows
   pdl_wait();
   pdl_trigger();
-  // scale and bias of this thread's row (tile row `lane`) in a group
-  auto load_sb = [&](const QtCursor& cs, bool valid) -> uint32_t {
-    const int tile = 4 * cs.x + q;
-    if (!valid || tile >= a.tiles) return 0u;
-    const unsigned char* sb =
-        a.wp + ((size_t)tile * G + cs.cg0 + cs.gl) * Q4_UNIT + 1024 + (lane & 7) * 16 + (lane >> 3) * 2;
-    return (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(sb)) |
-           ((uint32_t)__ldg(reinterpret_cast<const uint16_t*>(sb + 8)) << 16);
-  };
+  // this thread's row (tile row `lane`) in a group's scale/bias block: scales of rows g, g+8, 16+g, 24+g, then
+  // their biases, 16 bytes per g
+  const uint32_t sb_off = (uint32_t)(q * 128 + (lane & 7) * 16 + (lane >> 3) * 2);
   float tot[QT_CW];
 #pragma unroll
   for (int j = 0; j < QT_CW; j++) tot[j] = 0.f;
@@ -485,14 +487,14 @@ qtc_kernel(QtArgs a) {
   qt_item(a, blockIdx.x, ce);
   cn = ce;
   bool has_next = qt_next(a, cn);
-  uint32_t sb_cur = load_sb(ce, true);
   for (int k = 0;; k++) {
     const int tb = k % QT_TB, r = k % QT_SR;
-    const uint32_t sb_next = load_sb(cn, has_next);
     if (!qt_wait(&t_full[tb], (uint32_t)((k / QT_TB) & 1), abort_flag, a.error)) break;
     if (!qt_wait(&sx_full[r], (uint32_t)((k / QT_SR) & 1), abort_flag, a.error)) break;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const float s0 = bf_lo(sb_cur), b0 = fmaf(-128.f, s0, bf_hi(sb_cur));
+    const unsigned char* sbp = sbase + QT_OFF_SB + (size_t)r * QT_SBB + sb_off;
+    const float s0 = bf(*reinterpret_cast<const uint16_t*>(sbp));
+    const float b0 = fmaf(-128.f, s0, bf(*reinterpret_cast<const uint16_t*>(sbp + 8)));
     // the warp's accumulator columns, every load in flight before one wait
     uint32_t acc[QT_CW];
 #pragma unroll
@@ -530,7 +532,6 @@ qtc_kernel(QtArgs a) {
       qt_arrive(&t_empty[tb]);
       qt_arrive(&sx_empty[r]);
     }
-    sb_cur = sb_next;
 
     if (ce.gl == ce.ng - 1) {
       // ---- the item's last group: split-K, then the epilogue
