@@ -128,7 +128,7 @@ size_t im_qgemm_packed_workspace_bytes(int64_t M, int64_t N, int64_t K);
  * (default 592: one wave at four CTAs per SM) and its largest split. Process-wide; changes workspace sizes, so set
  * it before sizing workspaces. */
 int im_qgemm_packed_tune(int split_override, int target_ctas, int max_split);
-/* Kernel choice: 0 (default) = automatic (tcgen05 tensor cores from 192 rows when the K split is at most 16, the
+/* Kernel choice: 0 (default) = automatic (tcgen05 tensor cores from 128 rows when the K split is at most 16, the
  * warp MMA otherwise), 1 = warp MMA always, 2 = tensor cores always. Process-wide; every choice gives the same
  * bits; changes workspace sizes, so set it before sizing workspaces. */
 int im_qgemm_packed_path(int path);

@@ -31,13 +31,13 @@ static int g_q4_max_split = Q4_MAX_SPLITS;
 static int g_q4_cluster = 1;             // reduce split-K partials inside a thread-block cluster when possible
 static int g_q4_path = 0;                 // 0: automatic, 1: warp MMA always, 2: tensor cores always
 
-// The tensor-core kernel wins where an item streams many groups for many rows. Measured on B200 whole rounds:
-// Gemma-3-12B tree verification at 232 rows 71.2 ms (automatic) vs 75.1 ms (warp MMA only); Qwen3-4B at 160 rows
-// 49.3 ms vs 42.0 ms; Gemma-3-27B at 320 rows even. So: from 192 rows with at most 16 K splits.
+// The tensor-core kernel wins where an item streams many groups for many rows. Measured on B200 whole rounds,
+// with the kernel's 16 epilogue warps: config 3 (Qwen3-4B verification at 160 rows) 37.5 ms from 128 rows against
+// 38.6 ms from 192; config 5a (Gemma-3-27B) even. So: from 128 rows with at most 16 K splits.
 static bool q4_tensor_cores(int64_t M, int splits) {
   if (g_q4_path == 2) return true;
   if (g_q4_path == 1) return false;
-  return M >= 192 && splits <= 16;
+  return M >= 128 && splits <= 16;
 }
 constexpr uint32_t Q4_128 = 0x43004300u;
 
